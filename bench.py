@@ -1,0 +1,367 @@
+"""Benchmark: bit-exact sf16 elementwise ops on B200 (Gelem/s), with the wide
+8192^3 and chain 512^3 matmuls measured beside it.
+
+One step = the five status-reporting sf16 ops (add, sub, mul, fma, div) over
+2^26-element inputs resident in HBM, each op's exact event counts reduced on
+the device (and all-reduced over ranks when N > 1: the status exchange).
+``value`` = elements processed by all ranks / max-over-ranks device time.
+``e2e`` = the same ops through the reference-facing plug-in call
+``B200Device.run(op, fmt, x, y)`` on HOST int64 code arrays (the reference's
+Device.run contract): host narrowing, host->device copies, kernels, and the
+device->host copies of codes and per-output event bytes are all inside the
+timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 is launched with torchrun; each rank runs its own 2^26 elements (weak
+scaling, no data-path collective; only the status counts are all-reduced).
+``--impl reference`` times the reference's host implementation of the same
+ops (the oracle's NumPy restatement of src/sf/_vectorized.py, the reference's
+own code path being NumPy) on this host's cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+OPS = ("add", "sub", "mul", "fma", "div")
+N_ELEM = 1 << 26
+BYTES_PER_ELEM = {"add": 6, "sub": 6, "mul": 6, "div": 6, "fma": 8}   # int16 reads + write
+METRIC = "bit-exact sf16 matmul TOPS + elementwise Gelem/s at 1/2/4/8 B200 vs host CPU"
+
+
+def _env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def peaks():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles(kernel_key):
+    """DRAM bytes per launch recorded by ncu (profiles/ncu_traffic.txt:
+    '<key> <bytes per launch>' lines), or None."""
+    p = os.path.join(HERE, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_key:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(n_sample):
+    """The oracle's NumPy ops (the reference's own NumPy formulation) on
+    n_sample elements of the same workload, single-threaded."""
+    from oracle import sfref
+    from superfloat.python_b200 import workloads
+    x, y, z, d = workloads.elementwise(n_sample, 0)
+    args = {"add": (x, y), "sub": (x, y), "mul": (x, y), "fma": (x, y, z), "div": (x, d)}
+    t0 = time.perf_counter()
+    for op in OPS:
+        sfref.ew(op, 16, *args[op])
+    return time.perf_counter() - t0
+
+
+def _cpu_pool_worker(n):
+    return cpu_sample(n)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    n_sample = 1 << 22                             # per process per step
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        for _ in range(args.warmup):
+            pool.map(_cpu_pool_worker, [n_sample] * cores)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            pool.map(_cpu_pool_worker, [n_sample] * cores)
+            times.append(time.perf_counter() - t0)
+    elems = len(OPS) * n_sample * cores
+    ms = 1e3 * statistics.median(times)
+    v = elems / (ms / 1e3) / 1e9
+    line = {"metric": METRIC, "value": v, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": {"workload": "sf16 elementwise add/sub/mul/fma/div with status, seeded (2^26 generator)",
+                       "sample_elements_per_op": n_sample * cores, "processes": cores},
+            "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": "Gelem/s", "cores": cores, "kind": "port",
+                             "sample": f"{n_sample} elements x 5 ops per process, {cores} spawn processes"},
+            "e2e": {"value": v, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--elements", type=int, default=N_ELEM)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-matmul", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank, world, local = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from superfloat.python_b200 import FORMATS, B200Device, _lib, workloads
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = B200Device(local)
+    fmt = FORMATS[16]
+    n = args.elements
+    x, y, z, d = workloads.elementwise(n, seed=rank)
+    tx, ty, tz, td = (dev.upload(v) for v in (x, y, z, d))
+    outs = {op: torch.empty(n, dtype=torch.int16, device=dev.torch_device) for op in OPS}
+    counts = torch.zeros(len(OPS), _lib.N_COUNTS, dtype=torch.int64, device=dev.torch_device)
+    targs = {"add": (tx, ty), "sub": (tx, ty), "mul": (tx, ty), "fma": (tx, ty, tz), "div": (tx, td)}
+    stream = torch.cuda.current_stream()
+
+    def step(evs=None):
+        counts.zero_()
+        for i, op in enumerate(OPS):
+            if evs is not None:
+                evs[op][0].record(stream)
+            dev.run_device(op, fmt, *targs[op], out=outs[op], counts=counts[i])
+            if evs is not None:
+                evs[op][1].record(stream)
+        if world > 1:
+            dist.all_reduce(counts)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    per_op = {op: [] for op in OPS}
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start.record(stream)
+    evs_all = []
+    for _ in range(args.steps):
+        evs = {op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
+        step(evs)
+        evs_all.append(evs)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_total = t_start.elapsed_time(t_end)
+    for evs in evs_all:
+        for op in OPS:
+            per_op[op].append(evs[op][0].elapsed_time(evs[op][1]))
+    t = torch.tensor([ms_total], dtype=torch.float64, device=dev.torch_device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    elems = len(OPS) * n * world * args.steps
+    value = elems / (ms_total / 1e3) / 1e9
+
+    # status check: the step's counts are the oracle's on a sample (sanity, rank 0)
+    cnt = counts.cpu().numpy()
+
+    hbm, peak_kind = peaks()
+    mean_ms = {op: statistics.mean(v) for op, v in per_op.items()}
+    dom = max(mean_ms, key=mean_ms.get)
+    achieved = BYTES_PER_ELEM[dom] * n / (mean_ms[dom] / 1e3) / 1e9
+    traffic = traffic_from_profiles(f"ew_{dom}_{n}")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                "traffic": traffic, "kernel": f"ew_kernel<{dom}>", "peak_kind": peak_kind,
+                "per_op_GBps": {op: BYTES_PER_ELEM[op] * n / (mean_ms[op] / 1e3) / 1e9 for op in OPS},
+                "algorithmic_bytes_per_launch": BYTES_PER_ELEM[dom] * n}
+
+    line = {"metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16", "data": "synthetic",
+            "config": {"workload": "sf16 elementwise add/sub/mul/fma/div with exact status counts, "
+                                   f"{n} elements per op per rank (seeded 2^26 generator)",
+                       "elements_per_op_per_rank": n, "l2": "inputs larger than L2 (3 x 128 MiB per op)",
+                       "parallelism": f"element-range shards x{world}, status all-reduce"},
+            "gpu_launches": len(OPS) * args.steps, "roofline": roofline,
+            "status_counts_last_step": {op: {"overflow": int(cnt[i][0]), "underflow": int(cnt[i][1]),
+                                             "divide": int(cnt[i][2])} for i, op in enumerate(OPS)}}
+    if clocks:
+        line["clocks"] = clocks
+
+    # end to end through the plug-in call on host int64 arrays
+    if not args.no_e2e:
+        e2e_steps = max(1, min(3, args.steps))
+        xs = {"add": (x, y), "sub": (x, y), "mul": (x, y), "fma": (x, y, z), "div": (x, d)}
+        for op in OPS:                              # warm-up of the host path
+            dev.run(op, fmt, *(a[:4096] for a in xs[op]))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for op in OPS:
+                dev.run(op, fmt, *xs[op])
+        torch.cuda.synchronize()
+        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev.torch_device)
+        if world > 1:
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        dt = float(dt.item())
+        h2d = sum(2 * n * len(xs[op]) for op in OPS)
+        d2h = sum(3 * n for op in OPS)
+        line["e2e"] = {"value": len(OPS) * n * world * e2e_steps / dt / 1e9, "unit": "Gelem/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "path": "B200Device.run(op, sf16, x, y) on host int64 codes, masks returned"}
+
+    # CPU baseline on rank 0, N = 1
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n_sample = 1 << 22
+        cpu_sample(1 << 16)
+        reps = 3
+        ts = [cpu_sample(n_sample) for _ in range(reps)]
+        v = len(OPS) * n_sample / statistics.median(ts) / 1e9
+        line["cpu_baseline"] = {"value": v, "unit": "Gelem/s", "cores": 1, "kind": "port",
+                                "sample": f"{n_sample} elements x 5 ops, NumPy, median of {reps}"}
+
+    # the matmuls beside it (rank 0 only, N = 1): not part of `value`
+    if rank == 0 and world == 1 and not args.no_matmul:
+        line["matmul"] = bench_matmuls(dev, fmt, torch)
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_matmuls(dev, fmt, torch):
+    from superfloat.python_b200 import workloads
+    res = {}
+    stream = torch.cuda.current_stream()
+    # wide 8192^3 (the MX engine, v4.9.2, shift 0)
+    A, B = workloads.wide_square(8192, 8192, 8192, 0)
+    tA, tB = dev.upload(A), dev.upload(B)
+    del A, B
+    out = torch.empty(8192, 8192, dtype=torch.int16, device=dev.torch_device)
+    cnt = torch.zeros(8, dtype=torch.int64, device=dev.torch_device)
+    for _ in range(2):
+        dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    res["wide_8192"] = {"ms": ms, "TOPS": 2 * 8192 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
+    del tA, tB, out
+    # chain 512^3
+    A, B = workloads.chain_square(512, 0)
+    tA, tB = dev.upload(A), dev.upload(B)
+    out = torch.empty(512, 512, dtype=torch.int16, device=dev.torch_device)
+    for _ in range(3):
+        dev.run_device("matmul", fmt, tA, tB, out=out, counts=cnt)
+    torch.cuda.synchronize()
+    reps = 20
+    e0.record(stream)
+    for _ in range(reps):
+        dev.run_device("matmul", fmt, tA, tB, out=out, counts=cnt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    res["chain_512"] = {"ms": ms, "TOPS": 2 * 512 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
+    return res
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,138 @@
+/* sfb200.h - C ABI of the B200 (sm_100a) sf hot-path library, libsfb200.so.
+ *
+ * Codes: every sfN value (N = 4..16) is held in device memory as a signed
+ * 16-bit integer code k in [-M, M], M = 2^(N-1) - 1, value k / 2^(N-1)
+ * (the reference keeps the same signed codes as int64 NumPy arrays,
+ * src/sf/_format.py:1-11).  All buffers are caller-owned DEVICE pointers
+ * on the current CUDA device; every call is asynchronous on `stream`
+ * (a cudaStream_t, NULL = the legacy default stream).  No call allocates
+ * device memory.
+ *
+ * Status: each call adds its event counts into `counts` (device memory,
+ * one sfb_counts; the caller zeroes it) and, when `flags` is not NULL,
+ * writes one event byte per output (SFB_F_* bits).  An event count is the
+ * number of OUTPUTS whose computation raised that event, which is what the
+ * reference's runtime counts from its per-output masks
+ * (src/sf/_array.py:555-569).
+ *
+ * Errors: every entry point returns 0 on success or a negative SFB_E* code;
+ * sfb_last_error() then gives a message (per thread).  No exception and no
+ * process exit crosses this boundary.
+ */
+#ifndef SFB200_H
+#define SFB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SFB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SFB_API __attribute__((visibility("default")))
+#else
+#define SFB_API
+#endif
+
+/* return codes */
+#define SFB_OK 0
+#define SFB_EINVAL (-1)   /* bad argument: width, op, shape, null pointer */
+#define SFB_ECUDA (-2)    /* a CUDA runtime error (launch, device) */
+#define SFB_ERANGE (-3)   /* a size beyond what the kernels index */
+#define SFB_ENODEV (-4)   /* no sm_100 device */
+
+/* per-output event bits written to `flags` */
+#define SFB_F_OVERFLOW 1u
+#define SFB_F_UNDERFLOW 2u
+#define SFB_F_DIVIDE 4u
+#define SFB_F_INVALID 8u
+#define SFB_F_ACC_CLIPPED 16u /* wide only: the MX accumulator reached its limit */
+
+/* elementwise ops (the reference's device op table, src/sf/_device.py:181-185) */
+#define SFB_OP_ADD 0
+#define SFB_OP_SUB 1
+#define SFB_OP_MUL 2
+#define SFB_OP_DIV 3
+#define SFB_OP_FMA 4
+#define SFB_OP_NEG 5
+#define SFB_OP_ABS 6
+#define SFB_OP_SQRT 7
+#define SFB_OP_POW 8
+
+/* MX engine versions (src/sf/_linalg.py:144-147) */
+#define SFB_MX_V492 0
+#define SFB_MX_V481 1
+
+typedef struct sfb_counts {
+    unsigned long long overflow;    /* outputs that saturated (any step) */
+    unsigned long long underflow;   /* outputs where a nonzero result became 0 */
+    unsigned long long divide;      /* div outputs with a zero divisor */
+    unsigned long long invalid;     /* sqrt outputs of a negative input */
+    unsigned long long acc_clipped; /* wide outputs whose accumulator clipped */
+    unsigned long long reserved[3];
+} sfb_counts;
+
+typedef void *sfb_stream; /* a cudaStream_t */
+
+/* Library and device. */
+SFB_API int sfb_abi_version(void);
+SFB_API const char *sfb_last_error(void);
+/* Makes `device` current for the calling thread and checks it is an sm_100
+ * part.  Replaces the device attributes a reference target declares
+ * (src/sf/_device.py:38-50). */
+SFB_API int sfb_device_init(int device);
+
+/* Elementwise op over n codes: out[i] = op(a[i], b[i], c[i]).
+ * Replaces Device.run(op, fmt, a[, b[, c]]) for op in add, sub, mul, div, fma,
+ * neg, abs, sqrt, pow (src/sf/_device.py:96-106, :138-148; semantics of
+ * src/sf/_vectorized.py:94-156).  b is read by binary ops and fma, c by fma
+ * only; pow_n is pow's exponent (>= 1).  Operands have n elements each (the
+ * caller broadcasts).  Events: overflow (add, sub, div, fma), underflow (mul,
+ * fma, pow), divide (div), invalid (sqrt). */
+SFB_API int sfb_elementwise(int op, int bits, const int16_t *a, const int16_t *b, const int16_t *c,
+                    int16_t *out, uint8_t *flags, int64_t n, int pow_n, sfb_counts *counts,
+                    sfb_stream stream);
+
+/* Chain matmul: per output a chain of fma in increasing k,
+ * acc = clip(acc + trunc(a_k b_k / 2^(N-1))), then (bias != NULL) one
+ * saturating add of bias[n].  Replaces Device.run("matmul", fmt, A, B)
+ * (src/sf/_device.py:166-168 -> src/sf/_linalg.py:61-81) and, fused, the
+ * add that follows it in the linear layer (src/sf/torch/_core.py:376-378).
+ * A: batch x M x K, B: batch x K x N, out: batch x M x N, all row-major;
+ * stride_a / stride_b / stride_out are the element strides between batch
+ * entries (0 broadcasts one matrix over the batch); lda, ldb are the row
+ * strides of A and B.  Overflow counts outputs where a chain step or the
+ * bias add saturated; underflow outputs where a nonzero product truncated
+ * to 0 on a step that did not saturate. */
+SFB_API int sfb_matmul_chain(int bits, const int16_t *A, const int16_t *B, const int16_t *bias, int16_t *out,
+                     uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                     int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_out,
+                     sfb_counts *counts, sfb_stream stream);
+
+/* Bytes of device workspace sfb_matmul_wide needs for this problem (0 when
+ * it needs none); negative on a bad argument. */
+SFB_API int64_t sfb_matmul_wide_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K);
+
+/* Wide (MX engine) matmul: accumulators of the MX version `mx`
+ * (src/sf/_linalg.py:261-308), then POP at the per-output shift
+ * (src/sf/_linalg.py:201-220): shift_arr (int8, batch x M x N with strides
+ * shift_sb / shift_sm / shift_sn, 0 to broadcast) or, when shift_arr is
+ * NULL, the scalar `shift` (-32..31).  Replaces Device.run("matmul_wide",
+ * fmt, A, B, shift=, mx=) (src/sf/_device.py:171-173).  Overflow counts
+ * outputs whose accumulator clipped or whose POP saturated; underflow
+ * nonzero totals that rounded to 0; acc_clipped the clipped accumulators.
+ * `workspace` is caller-owned device memory of at least
+ * sfb_matmul_wide_workspace() bytes (NULL when that is 0). */
+SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr,
+                    int shift, int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N,
+                    int64_t K, int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b,
+                    int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
+                    void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SFB200_H */

@@ -1,0 +1,323 @@
+"""NumPy restatement of the reference's sfN arithmetic (oracle; test infrastructure).
+
+Codes are signed integers k in [-M, M], M = 2^(N-1) - 1, value k / 2^(N-1)
+(reference src/sf/_format.py:1-11, :21-60).  Every op returns
+``(codes int64, events)`` where ``events`` maps an event name to a boolean
+mask over the output, the shape the reference's vectorised ops return
+(src/sf/_vectorized.py:1-11).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+EVENTS = ("overflow", "underflow", "divide", "invalid")
+
+
+def consts(bits: int):
+    """(M, S) for sfN: M = 2^(N-1) - 1 the largest code, S = 2^(N-1) one unit
+    (src/sf/_format.py:40-48)."""
+    if not 4 <= bits <= 16:
+        raise ValueError(f"sf width must be 4..16, got {bits}")
+    S = 1 << (bits - 1)
+    return S - 1, S
+
+
+def _i64(x):
+    return np.asarray(x, dtype=np.int64)
+
+
+def _tdiv(num, den):
+    """Integer quotient rounded toward zero (src/sf/_vectorized.py:19-22)."""
+    num, den = _i64(num), _i64(den)
+    mag = np.abs(num) // np.abs(den)
+    return np.where((num < 0) ^ (den < 0), -mag, mag)
+
+
+# --- elementwise ops (src/sf/_vectorized.py:94-156) -------------------------------------
+
+def add(bits, a, b):
+    """clip(a + b) with overflow where |a + b| > M (_vectorized.py:94-95, :25-27)."""
+    M, _ = consts(bits)
+    s = _i64(a) + _i64(b)
+    return np.clip(s, -M, M), {"overflow": np.abs(s) > M}
+
+
+def sub(bits, a, b):
+    """clip(a - b), as add (_vectorized.py:98-99)."""
+    M, _ = consts(bits)
+    s = _i64(a) - _i64(b)
+    return np.clip(s, -M, M), {"overflow": np.abs(s) > M}
+
+
+def neg(bits, a):
+    """Exact negation, no event (_vectorized.py:102-103)."""
+    return -_i64(a), {}
+
+
+def abs_(bits, a):
+    """Exact magnitude, no event (_vectorized.py:106-107)."""
+    return np.abs(_i64(a)), {}
+
+
+def mul(bits, a, b):
+    """trunc(a b / S); underflow where a nonzero product truncates to 0
+    (_vectorized.py:110-113)."""
+    _, S = consts(bits)
+    p = _i64(a) * _i64(b)
+    k = _tdiv(p, S)
+    return k, {"underflow": (p != 0) & (k == 0)}
+
+
+def div(bits, a, b):
+    """Saturating division (_vectorized.py:116-125):
+    b == 0        -> sign(a) M (0 for 0/0), divide event;
+    a != 0 and |a| >= |b| -> +-M with the quotient's sign, overflow event;
+    otherwise     -> trunc(a S / b)."""
+    M, S = consts(bits)
+    a, b = np.broadcast_arrays(_i64(a), _i64(b))
+    zero = b == 0
+    q = _tdiv(a * S, np.where(zero, 1, b))
+    over = ~zero & (a != 0) & (np.abs(a) >= np.abs(b))
+    sat = np.where(np.sign(a) == np.sign(b), M, -M)
+    out = np.where(zero, np.sign(a) * M, np.where(over, sat, q))
+    return out, {"overflow": over, "divide": zero}
+
+
+def fma(bits, a, b, c):
+    """add(mul(a, b), c): two roundings, not fused; the product's underflow is
+    reported only where the add did not overflow (_vectorized.py:128-131)."""
+    p, ep = mul(bits, a, b)
+    s, es = add(bits, p, c)
+    return s, {"overflow": es["overflow"], "underflow": ep["underflow"] & ~es["overflow"]}
+
+
+def sqrt(bits, a):
+    """floor(sqrt(a S)) for a >= 0; 0 and an invalid event for a < 0
+    (_vectorized.py:134-142).  Integer square root, exact."""
+    _, S = consts(bits)
+    a = _i64(a)
+    bad = a < 0
+    x = np.where(bad, 0, a) * S
+    r = np.floor(np.sqrt(x.astype(np.float64))).astype(np.int64)
+    r = np.where(r * r > x, r - 1, r)
+    r = np.where((r + 1) * (r + 1) <= x, r + 1, r)
+    return np.where(bad, 0, r), {"invalid": bad}
+
+
+def pow_int(bits, a, n: int):
+    """a ** n as a left-to-right chain of ``mul`` (_vectorized.py:145-156).
+    The reference stops early once every element is 0; later steps would
+    only multiply zeros, which raises no event, so running all n - 1 steps
+    gives the same codes and masks."""
+    if n < 1:
+        raise ValueError("pow needs n >= 1")
+    a = _i64(a)
+    k = a.copy()
+    under = np.zeros(k.shape, bool)
+    for _ in range(n - 1):
+        k, ev = mul(bits, k, a)
+        under |= ev["underflow"]
+    return k, {"underflow": under}
+
+
+OPS = {"add": add, "sub": sub, "mul": mul, "div": div, "fma": fma,
+       "neg": neg, "abs": abs_, "sqrt": sqrt}
+
+
+def ew(op: str, bits: int, *operands, **kw):
+    if op == "pow":
+        return pow_int(bits, *operands, **kw)
+    return OPS[op](bits, *operands)
+
+
+# --- chain accumulation (src/sf/_linalg.py:30-111) -----------------------------------------
+
+def sum_chain(bits, a, axis=0):
+    """Sequential saturating sum from index 0 (_linalg.py:30-40)."""
+    a = np.moveaxis(_i64(a), axis, 0)
+    acc = np.zeros(a.shape[1:], np.int64)
+    over = np.zeros(a.shape[1:], bool)
+    for k in range(a.shape[0]):
+        acc, ev = add(bits, acc, a[k])
+        over |= ev["overflow"]
+    return acc, {"overflow": over}
+
+
+def matmul_chain(bits, A, B):
+    """(..., M, K) @ (..., K, N), one fma chain per output in increasing k:
+    acc = clip(acc + trunc(a_k b_k / S)) (_linalg.py:61-81).  Overflow marks
+    outputs where any step saturated; underflow outputs where a product
+    truncated to 0 on a step that did not saturate (the fma rule)."""
+    A, B = _i64(A), _i64(B)
+    K = A.shape[-1]
+    shape = np.broadcast_shapes(A.shape[:-2], B.shape[:-2]) + (A.shape[-2], B.shape[-1])
+    acc = np.zeros(shape, np.int64)
+    over = np.zeros(shape, bool)
+    under = np.zeros(shape, bool)
+    for k in range(K):
+        acc, ev = fma(bits, A[..., :, k:k + 1], B[..., k:k + 1, :], acc)
+        over |= ev["overflow"]
+        under |= ev["underflow"]
+    return acc, {"overflow": over, "underflow": under}
+
+
+def chain_bound(bits, A, B) -> int:
+    """The reference's L1 bound on every partial sum, in codes (_linalg.py:84-106):
+    min(max_i ||a_i||_1 max|b|, max|a| max_j ||b_j||_1) // S."""
+    _, S = consts(bits)
+    A, B = np.abs(_i64(A)), np.abs(_i64(B))
+    if A.size == 0 or B.size == 0 or A.shape[-1] == 0:
+        return 0
+    r = int(A.sum(axis=-1).max()) * int(B.max())
+    c = int(A.max()) * int(B.sum(axis=-2).max())
+    return min(r, c) // S
+
+
+# --- wide accumulation: the MX engine (src/sf/_linalg.py:114-369) --------------------------
+
+# The accumulator units per chip (_linalg.py:144-147): W accumulator bits,
+# F fraction bits, tk the first kept partial-product column, comp the
+# constant added to each SF16-block product.
+MX_UNITS = {
+    "v4.9.2": {16: dict(W=32, F=22, tk=6, comp=80), 8: dict(W=32, F=14, tk=None, comp=None)},
+    "v4.8.1": {16: dict(W=25, F=19, tk=9, comp=1024), 8: dict(W=20, F=14, tk=None, comp=None)},
+}
+MX_DEFAULT = "v4.9.2"
+SHIFT_MIN, SHIFT_MAX = -32, 31
+
+
+def mx_block(bits: int) -> int:
+    """sf9..sf16 run on the SF16 block, sf4..sf8 on the SF8 block (_linalg.py:178-180)."""
+    return 16 if bits >= 9 else 8
+
+
+def mx_mags(bits, codes):
+    """|code| left-aligned in the 16-bit word's 15-bit magnitude field, or the
+    top byte's 7-bit field on the SF8 block (_linalg.py:183-187)."""
+    m = np.abs(_i64(codes)) << (16 - bits)
+    return m >> 8 if mx_block(bits) == 8 else m
+
+
+def mx_product16(am, wm, unit):
+    """SF16-block product magnitude (_linalg.py:190-198): the 15 partial-product
+    rows bit_i(a) (w << i) with columns below tk dropped, plus comp, masked to
+    30 bits and cut to F fraction bits.  Walked bit by bit, as defined."""
+    am, wm = _i64(am), _i64(wm)
+    keep = ~np.int64((1 << unit["tk"]) - 1)
+    acc = np.full(np.broadcast_shapes(am.shape, wm.shape), unit["comp"], np.int64)
+    for i in range(15):
+        acc = acc + ((am >> i) & 1) * ((wm << i) & keep)
+    return (acc & ((1 << 30) - 1)) >> (30 - unit["F"])
+
+
+def wide_acc(bits, A, B, mx=MX_DEFAULT, chunk_cols=256):
+    """MX accumulators before POP (_linalg.py:261-308): per output, K in
+    chunks of 8; a chunk's signed products are summed exactly, added to the
+    W-bit accumulator, which saturates at +-(2^(W-1)) once per chunk.
+    Returns (acc int64, clipped bool, F)."""
+    A, B = _i64(A), _i64(B)
+    blk = mx_block(bits)
+    u = MX_UNITS[mx][blk]
+    lo, hi = -(1 << (u["W"] - 1)), (1 << (u["W"] - 1)) - 1
+    am, bm = mx_mags(bits, A), mx_mags(bits, B)
+    an, bn = A < 0, B < 0
+    K = A.shape[-1]
+    shape = np.broadcast_shapes(A.shape[:-2], B.shape[:-2]) + (A.shape[-2], B.shape[-1])
+    acc = np.zeros(shape, np.int64)
+    clip = np.zeros(shape, bool)
+    N = shape[-1]
+    for n0 in range(0, N, chunk_cols):
+        cs = slice(n0, min(N, n0 + chunk_cols))
+        s = np.zeros(shape[:-1] + (cs.stop - cs.start,), np.int64)
+        c = np.zeros(s.shape, bool)
+        for k0 in range(0, K, 8):
+            ks = slice(k0, min(K, k0 + 8))
+            a_ = am[..., :, ks][..., :, :, None]
+            b_ = bm[..., ks, cs][..., None, :, :]
+            t = mx_product16(a_, b_, u) if blk == 16 else a_ * b_
+            ng = an[..., :, ks][..., :, :, None] ^ bn[..., ks, cs][..., None, :, :]
+            s = s + np.where(ng, -t, t).sum(axis=-2)
+            c |= (s < lo) | (s > hi)
+            s = np.clip(s, lo, hi)
+        acc[..., cs] = s
+        clip[..., cs] = c
+    return acc, clip, u["F"]
+
+
+def wide_pop(bits, acc, shift, frac):
+    """POP (_linalg.py:201-220): acc 2^(shift - frac) in sfN codes, rounded
+    half to even on the magnitude, saturated at M, sign restored (never -0).
+    Returns (codes, overflow (q > M before the clamp), underflow (acc != 0,
+    q == 0))."""
+    M, _ = consts(bits)
+    acc = _i64(acc)
+    e = np.broadcast_to(_i64(shift) - frac + bits - 1, acc.shape)
+    mag = np.abs(acc)
+    d = np.maximum(-e, 1)
+    fl = mag >> d
+    rem = mag - (fl << d)
+    half = np.int64(1) << (d - 1)
+    rnd = fl + ((rem > half) | ((rem == half) & (fl & 1 == 1)))
+    q = np.where(e >= 0, mag << np.maximum(e, 0), rnd)
+    over = q > M
+    q = np.minimum(q, M)
+    return np.where(acc < 0, -q, q), over, (acc != 0) & (q == 0)
+
+
+def check_shift(shift):
+    """An int in [-32, 31] or an integer array of them (_linalg.py:223-247)."""
+    if shift is None:
+        return 0
+    if isinstance(shift, (bool, np.bool_)):
+        raise TypeError("shift must be an int or an array of ints, got bool")
+    if isinstance(shift, (int, np.integer)):
+        if not SHIFT_MIN <= int(shift) <= SHIFT_MAX:
+            raise ValueError(f"shift must be between {SHIFT_MIN} and {SHIFT_MAX}, got {shift}")
+        return int(shift)
+    arr = np.asarray(shift)
+    if arr.dtype == bool or not np.issubdtype(arr.dtype, np.integer):
+        raise TypeError(f"shift must be an int or an array of ints, got an array of {arr.dtype}")
+    if arr.size and (arr.min() < SHIFT_MIN or arr.max() > SHIFT_MAX):
+        raise ValueError("every shift must be between -32 and 31")
+    arr = arr.astype(np.int64)
+    return int(arr) if arr.ndim == 0 else arr
+
+
+def matmul_wide(bits, A, B, shift=0, mx=MX_DEFAULT, acc_fn=None):
+    """(..., M, K) @ (..., K, N) on the MX engine (_linalg.py:330-348):
+    overflow = accumulator clipped or POP saturated; underflow = a nonzero
+    total rounded to 0.  ``acc_fn`` replaces ``wide_acc`` (the C oracle)."""
+    shift = check_shift(shift)
+    acc, clip, F = (acc_fn or wide_acc)(bits, A, B, mx)
+    if not isinstance(shift, int):
+        shift = np.broadcast_to(shift, acc.shape)
+    q, over, under = wide_pop(bits, acc, shift, F)
+    return q, {"overflow": clip | over, "underflow": under}
+
+
+def wide_acc_safe(bits, A, B, mx=MX_DEFAULT) -> bool:
+    """Host proof that no accumulator can clip (_linalg.py:351-369): the L1
+    relaxation of sum |t|, each SF16 term at most |a||w| / 2^(30-F) + 1."""
+    A, B = _i64(A), _i64(B)
+    if A.size == 0 or B.size == 0 or A.shape[-1] == 0:
+        return True
+    blk = mx_block(bits)
+    am, bm = mx_mags(bits, A), mx_mags(bits, B)
+    l1 = min(int(am.sum(axis=-1).max()) * int(bm.max()), int(am.max()) * int(bm.sum(axis=-2).max()))
+    u = MX_UNITS[mx][blk]
+    bound = l1 // (1 << (30 - u["F"])) + A.shape[-1] if blk == 16 else l1
+    return bound <= (1 << (u["W"] - 1)) - 1
+
+
+# --- the exact decomposition the B200 wide kernel uses, stated on the CPU ----------------
+
+def t16_closed(am, wm):
+    """v4.9.2 SF16-block product in closed form: with x = a mod 64, y = w mod 64,
+    C[x][y] = sum_{i+j<6} 2^(i+j) x_i y_j (the dropped columns), the product is
+    (a w + 80 - C) >> 8.  Equal to ``mx_product16`` for every 15-bit pair."""
+    am, wm = _i64(am), _i64(wm)
+    x, y = am & 63, wm & 63
+    C = np.zeros(np.broadcast_shapes(x.shape, y.shape), np.int64)
+    for i in range(6):
+        C = C + ((x >> i) & 1) * ((y << i) & 63)
+    return (am * wm + 80 - C) >> 8

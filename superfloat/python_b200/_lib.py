@@ -1,0 +1,123 @@
+"""ctypes binding of libsfb200.so (the C ABI declared in include/sfb200.h).
+
+The library is loaded from this package's directory; there is no fallback:
+when it is missing or no sm_100 device is present every call raises
+``SFDeviceError``.  Device buffers are torch tensors on the current CUDA
+device (torch is the allocator and the stream owner here); the library only
+sees raw pointers and a ``cudaStream_t``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from ._errors import SFDeviceError, SFLaunchError, SFShapeError
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsfb200.so")
+
+SFB_OK, SFB_EINVAL, SFB_ECUDA, SFB_ERANGE, SFB_ENODEV = 0, -1, -2, -3, -4
+F_OVERFLOW, F_UNDERFLOW, F_DIVIDE, F_INVALID, F_ACC_CLIPPED = 1, 2, 4, 8, 16
+OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "fma": 4, "neg": 5, "abs": 6, "sqrt": 7, "pow": 8}
+MX = {"v4.9.2": 0, "v4.8.1": 1}
+COUNT_FIELDS = ("overflow", "underflow", "divide", "invalid", "acc_clipped")
+N_COUNTS = 8                       # sfb_counts: 8 x uint64
+
+# every symbol include/sfb200.h declares: name -> (restype, argtypes)
+_p, _i32, _i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+SIGNATURES = {
+    "sfb_abi_version": (_i32, []),
+    "sfb_last_error": (ctypes.c_char_p, []),
+    "sfb_device_init": (_i32, [_i32]),
+    "sfb_elementwise": (_i32, [_i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _p, _p]),
+    "sfb_matmul_chain": (_i32, [_i32, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                _i64, _p, _p]),
+    "sfb_matmul_wide_workspace": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64]),
+    "sfb_matmul_wide": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                               _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+_ready_devices: set[int] = set()
+
+
+def load(path: str = LIB_PATH):
+    """Load the library and bind every declared symbol (no GPU needed)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(path):
+                raise SFDeviceError(f"libsfb200.so is missing at {path}; build it with "
+                                    "`python -m superfloat.python_b200.build`")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype, fn.argtypes = res, args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return load().sfb_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc == SFB_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc == SFB_EINVAL:
+        raise SFShapeError(msg)
+    if rc == SFB_ERANGE:
+        raise SFLaunchError(msg)
+    raise SFDeviceError(msg)
+
+
+def ensure_device(index: int) -> None:
+    """sfb_device_init once per device (checks it is an sm_100 part)."""
+    if index in _ready_devices:
+        return
+    check(load().sfb_device_init(index), "sfb_device_init")
+    _ready_devices.add(index)
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def elementwise(op: str, bits: int, a, b, c, out, flags, counts, pow_n: int = 0, stream=None) -> None:
+    """out = op(a, b, c) over a.numel() int16 codes (all contiguous, same length)."""
+    rc = load().sfb_elementwise(OPS[op], bits, _ptr(a), _ptr(b), _ptr(c), _ptr(out), _ptr(flags),
+                                a.numel(), pow_n, _ptr(counts), _stream(stream))
+    check(rc, f"sf {op}")
+
+
+def matmul_chain(bits, A, B, bias, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so, stream=None):
+    rc = load().sfb_matmul_chain(bits, _ptr(A), _ptr(B), _ptr(bias), _ptr(out), _ptr(flags), batch, M, N, K,
+                                 lda, ldb, sa, sb, so, _ptr(counts), _stream(stream))
+    check(rc, "sf matmul (chain)")
+
+
+def wide_workspace(bits, mx, batch, M, N, K) -> int:
+    n = load().sfb_matmul_wide_workspace(bits, MX[mx], batch, M, N, K)
+    if n < 0:
+        check(int(n), "sf matmul (wide) workspace")
+    return int(n)
+
+
+def matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so,
+                ssb, ssm, ssn, workspace, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_matmul_wide(bits, MX[mx], _ptr(A), _ptr(B), _ptr(shift_arr), int(shift), _ptr(out),
+                                _ptr(flags), batch, M, N, K, lda, ldb, sa, sb, so, ssb, ssm, ssn,
+                                _ptr(workspace), ws_bytes, _ptr(counts), _stream(stream))
+    check(rc, "sf matmul (wide)")

@@ -1,0 +1,190 @@
+// Elementwise sfN ops with per-output events, HBM-streaming on sm_100a.
+//
+// Semantics follow the reference's vectorised ops (src/sf/_vectorized.py:94-156):
+//   add/sub  clip(a +- b, +-M), overflow where |a +- b| > M          (:94-99, :25-27)
+//   mul      trunc(a b / S), underflow where a b != 0 truncates to 0  (:110-113)
+//   div      b == 0: sign(a) M, divide; a != 0, |a| >= |b|: +-M, overflow;
+//            else trunc(a S / b)                                      (:116-125)
+//   fma      add(mul(a, b), c); underflow only where the add did not overflow (:128-131)
+//   neg/abs  exact                                                    (:102-107)
+//   sqrt     floor(sqrt(a S)), a < 0 -> 0 and invalid                 (:134-142)
+//   pow      chain of mul, underflow if any step underflowed          (:145-156)
+//
+// Layout: int16 codes, 8 per 128-bit vector.  Each thread streams whole
+// vectors (grid-stride, grid = SMs x resident blocks), counts events in
+// registers and flushes them once per block (warp reduce + one atomic per
+// counter).  Optional per-output event bytes are written 8 at a time.
+#include <math.h>
+
+#include "sfb_common.cuh"
+
+namespace sfb {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int OP>
+__device__ __forceinline__ int ew_one(int a, int b, int c, const Width w, int pow_n, unsigned &fl) {
+    const int M = w.M, sh = w.sh;
+    if constexpr (OP == SFB_OP_ADD || OP == SFB_OP_SUB) {
+        const int s = (OP == SFB_OP_ADD) ? a + b : a - b;
+        fl = (s > M || s < -M) ? SFB_F_OVERFLOW : 0u;
+        return clampi(s, -M, M);
+    } else if constexpr (OP == SFB_OP_MUL) {
+        const int p = a * b;
+        const int k = tdiv_pow2(p, sh);
+        fl = (p != 0 && k == 0) ? SFB_F_UNDERFLOW : 0u;
+        return k;
+    } else if constexpr (OP == SFB_OP_FMA) {
+        const int p = a * b;
+        const int k = tdiv_pow2(p, sh);
+        const int s = k + c;
+        const bool ov = s > M || s < -M;
+        fl = (ov ? SFB_F_OVERFLOW : 0u) | ((!ov && p != 0 && k == 0) ? SFB_F_UNDERFLOW : 0u);
+        return clampi(s, -M, M);
+    } else if constexpr (OP == SFB_OP_DIV) {
+        if (b == 0) {
+            fl = SFB_F_DIVIDE;
+            return a > 0 ? M : (a < 0 ? -M : 0);
+        }
+        const unsigned ua = (unsigned)abs(a), ub = (unsigned)abs(b);
+        if (a != 0 && ua >= ub) {
+            fl = SFB_F_OVERFLOW;
+            return ((a ^ b) >= 0) ? M : -M;
+        }
+        fl = 0u;
+        const int q = (int)((ua << sh) / ub);
+        return ((a ^ b) < 0) ? -q : q;
+    } else if constexpr (OP == SFB_OP_NEG) {
+        fl = 0u;
+        return -a;
+    } else if constexpr (OP == SFB_OP_ABS) {
+        fl = 0u;
+        return abs(a);
+    } else if constexpr (OP == SFB_OP_SQRT) {
+        if (a < 0) {
+            fl = SFB_F_INVALID;
+            return 0;
+        }
+        fl = 0u;
+        const int x = a << sh;  // < 2^30
+        int r = (int)sqrtf((float)x);  // within 1 of floor(sqrt(x)) for x < 2^30
+        if (r * r > x) r -= 1;
+        if ((r + 1) * (r + 1) <= x) r += 1;
+        return r;
+    } else {  // SFB_OP_POW
+        int k = a;
+        bool un = false;
+        for (int i = 1; i < pow_n; i++) {
+            const int p = k * a;
+            k = tdiv_pow2(p, sh);
+            un |= (p != 0 && k == 0);
+        }
+        fl = un ? SFB_F_UNDERFLOW : 0u;
+        return k;
+    }
+}
+
+__device__ __forceinline__ void tally(Counts &c, unsigned fl) {
+    c.over += fl & 1u;
+    c.under += (fl >> 1) & 1u;
+    c.div0 += (fl >> 2) & 1u;
+    c.inval += (fl >> 3) & 1u;
+}
+
+union Vec8 {
+    uint4 u;
+    int16_t h[8];
+};
+
+template <int OP, bool FLAGS>
+__global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict__ a, const int16_t *__restrict__ b,
+                                                     const int16_t *__restrict__ c, int16_t *__restrict__ out,
+                                                     uint8_t *__restrict__ flags, int64_t n, Width w, int pow_n,
+                                                     int vec_ok, sfb_counts *counts) {
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    Counts cnt;
+    constexpr bool kB = OP == SFB_OP_ADD || OP == SFB_OP_SUB || OP == SFB_OP_MUL || OP == SFB_OP_DIV ||
+                        OP == SFB_OP_FMA;
+    constexpr bool kC = OP == SFB_OP_FMA;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec_ok) {
+        const int64_t nv = n >> 3;
+        for (int64_t v = tid; v < nv; v += stride) {
+            Vec8 va, vb, vc, vo;
+            va.u = __ldcs(reinterpret_cast<const uint4 *>(a) + v);
+            if constexpr (kB) vb.u = __ldcs(reinterpret_cast<const uint4 *>(b) + v);
+            if constexpr (kC) vc.u = __ldcs(reinterpret_cast<const uint4 *>(c) + v);
+            uint64_t fb = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                unsigned fl;
+                vo.h[j] = (int16_t)ew_one<OP>(va.h[j], kB ? vb.h[j] : 0, kC ? vc.h[j] : 0, w, pow_n, fl);
+                tally(cnt, fl);
+                fb |= (uint64_t)fl << (8 * j);
+            }
+            __stcs(reinterpret_cast<uint4 *>(out) + v, vo.u);
+            if constexpr (FLAGS) __stcs(reinterpret_cast<unsigned long long *>(flags) + v, (unsigned long long)fb);
+        }
+        done = nv << 3;
+    }
+    for (int64_t i = done + tid; i < n; i += stride) {
+        unsigned fl;
+        out[i] = (int16_t)ew_one<OP>(a[i], kB ? b[i] : 0, kC ? c[i] : 0, w, pow_n, fl);
+        tally(cnt, fl);
+        if constexpr (FLAGS) flags[i] = (uint8_t)fl;
+    }
+    flush_counts(cnt, counts, sc);
+}
+
+template <int OP>
+int launch(const int16_t *a, const int16_t *b, const int16_t *c, int16_t *out, uint8_t *flags, int64_t n,
+           Width w, int pow_n, sfb_counts *counts, cudaStream_t st) {
+    const bool vec_ok = ((uintptr_t)a % 16 == 0) && (b == nullptr || (uintptr_t)b % 16 == 0) &&
+                        (c == nullptr || (uintptr_t)c % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
+                        (flags == nullptr || (uintptr_t)flags % 8 == 0);
+    const int64_t work = vec_ok ? (n >> 3) + 1 : n;
+    const int64_t max_blocks = (int64_t)sm_count() * (2048 / kThreads);
+    int blocks = (int)std::min<int64_t>(max_blocks, (work + kThreads - 1) / kThreads);
+    if (blocks < 1) blocks = 1;
+    if (flags)
+        ew_kernel<OP, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    else
+        ew_kernel<OP, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    return check_launch("sfb_elementwise");
+}
+
+}  // namespace
+}  // namespace sfb
+
+extern "C" int sfb_elementwise(int op, int bits, const int16_t *a, const int16_t *b, const int16_t *c,
+                               int16_t *out, uint8_t *flags, int64_t n, int pow_n, sfb_counts *counts,
+                               sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_elementwise: width %d is not 4..16", bits);
+    if (n < 0) return set_error(SFB_EINVAL, "sfb_elementwise: negative length %lld", (long long)n);
+    if (n == 0) return SFB_OK;
+    if (a == nullptr || out == nullptr) return set_error(SFB_EINVAL, "sfb_elementwise: null operand or output");
+    const bool binary = op == SFB_OP_ADD || op == SFB_OP_SUB || op == SFB_OP_MUL || op == SFB_OP_DIV ||
+                        op == SFB_OP_FMA;
+    if (binary && b == nullptr) return set_error(SFB_EINVAL, "sfb_elementwise: op %d needs b", op);
+    if (op == SFB_OP_FMA && c == nullptr) return set_error(SFB_EINVAL, "sfb_elementwise: fma needs c");
+    if (op == SFB_OP_POW && pow_n < 1) return set_error(SFB_EINVAL, "sfb_elementwise: pow needs n >= 1");
+    const Width w = width(bits);
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (op) {
+        case SFB_OP_ADD: return launch<SFB_OP_ADD>(a, b, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_SUB: return launch<SFB_OP_SUB>(a, b, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_MUL: return launch<SFB_OP_MUL>(a, b, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_DIV: return launch<SFB_OP_DIV>(a, b, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_FMA: return launch<SFB_OP_FMA>(a, b, c, out, flags, n, w, 0, counts, st);
+        case SFB_OP_NEG: return launch<SFB_OP_NEG>(a, nullptr, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_ABS: return launch<SFB_OP_ABS>(a, nullptr, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_SQRT: return launch<SFB_OP_SQRT>(a, nullptr, nullptr, out, flags, n, w, 0, counts, st);
+        case SFB_OP_POW: return launch<SFB_OP_POW>(a, nullptr, nullptr, out, flags, n, w, pow_n, counts, st);
+        default: return set_error(SFB_EINVAL, "sfb_elementwise: unknown op %d", op);
+    }
+}
