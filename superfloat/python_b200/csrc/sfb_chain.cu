@@ -130,7 +130,7 @@ extern "C" int sfb_matmul_chain(int bits, const int16_t *A, const int16_t *B, co
     if (batch == 0 || M == 0 || N == 0) return SFB_OK;
     if (out == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
         return set_error(SFB_EINVAL, "sfb_matmul_chain: null operand or output");
-    if (lda < K || ldb < N) return set_error(SFB_EINVAL, "sfb_matmul_chain: lda < K or ldb < N");
+    if (K > 0 && (lda < K || ldb < N)) return set_error(SFB_EINVAL, "sfb_matmul_chain: lda < K or ldb < N");
     if (stride_out < M * N && batch > 1)
         return set_error(SFB_EINVAL, "sfb_matmul_chain: output batch entries overlap");
     const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;

@@ -23,6 +23,24 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// floor(ua 2^sh / ub) for 0 <= ua < ub < 2^15, sh <= 15 (the quotient is < 2^15).
+// Reciprocal estimate, then one exact integer correction:
+//   x = ua 2^sh / ub;  both operands convert to float exactly (< 2^23, by the
+//   2^23 bias trick); rcp.approx has relative error < 2^-22 and the product
+//   rounds once more, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.
+//   Rounding it to the nearest integer gives floor(x) or floor(x) + 1, and the
+//   remainder's sign tells which.
+__device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
+    const float fa = __int_as_float(0x4B000000 | ua) - 8388608.0f;
+    const float fb = __int_as_float(0x4B000000 | ub) - 8388608.0f;
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fb));
+    const float est = fa * r * __int_as_float((127 + sh) << 23);      // times 2^sh, exact
+    const int q0 = __float_as_int(est + 12582912.0f) - 0x4B400000;    // nearest integer (est < 2^22)
+    const int rem = (int)(ua << sh) - q0 * (int)ub;
+    return (unsigned)(q0 + (rem >> 31));                               // q0 - 1 when rem < 0
+}
+
 template <int OP>
 __device__ __forceinline__ int ew_one(int a, int b, int c, const Width w, int pow_n, unsigned &fl) {
     const int M = w.M, sh = w.sh;
@@ -53,7 +71,7 @@ __device__ __forceinline__ int ew_one(int a, int b, int c, const Width w, int po
             return ((a ^ b) >= 0) ? M : -M;
         }
         fl = 0u;
-        const int q = (int)((ua << sh) / ub);
+        const int q = (int)udiv_small(ua, ub, sh);
         return ((a ^ b) < 0) ? -q : q;
     } else if constexpr (OP == SFB_OP_NEG) {
         fl = 0u;

@@ -181,7 +181,7 @@ extern "C" int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t
     if (batch == 0 || M == 0 || N == 0) return SFB_OK;
     if (out == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
         return set_error(SFB_EINVAL, "sfb_matmul_wide: null operand or output");
-    if (lda < K || ldb < N) return set_error(SFB_EINVAL, "sfb_matmul_wide: lda < K or ldb < N");
+    if (K > 0 && (lda < K || ldb < N)) return set_error(SFB_EINVAL, "sfb_matmul_wide: lda < K or ldb < N");
     if (stride_out < M * N && batch > 1) return set_error(SFB_EINVAL, "sfb_matmul_wide: output batch entries overlap");
     cudaStream_t st = (cudaStream_t)stream;
     bool handled = false;
