@@ -185,7 +185,7 @@ class B200Device(Device):
                                                     device=A.device)
         fl = torch.empty(tuple(batch_shape) + (M, N), dtype=torch.uint8, device=A.device) if flags else None
         if op == "matmul":
-            _lib.matmul_chain(fmt.bits, A3, B3, bias, o, fl, cnt, nb, M, N, K, A3.stride(-2), B3.stride(-2),
+            _lib.matmul_chain(fmt.bits, A3, B3, bias, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
                               sa, sb, M * N, stream=stream)
         else:
             mxv = mx or self.mx
@@ -201,8 +201,8 @@ class B200Device(Device):
                 sh_t = st
                 ss = (st.stride(0), st.stride(1), st.stride(2))
             ws = self.workspace(_lib.wide_workspace(fmt.bits, mxv, nb, M, N, K))
-            _lib.matmul_wide(fmt.bits, mxv, A3, B3, sh_t, sh_int, o, fl, cnt, nb, M, N, K, A3.stride(-2),
-                             B3.stride(-2), sa, sb, M * N, ss[0], ss[1], ss[2], ws, stream=stream)
+            _lib.matmul_wide(fmt.bits, mxv, A3, B3, sh_t, sh_int, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
+                             sa, sb, M * N, ss[0], ss[1], ss[2], ws, stream=stream)
         return o, cnt, fl
 
     # --- the reference's plug-in contract --------------------------------------------------
@@ -231,6 +231,12 @@ class B200Device(Device):
         fl = fl.cpu().numpy()
         masks = {e: (fl & _EVENT_BIT[e]) != 0 for e in OP_EVENTS[op]}
         return codes, masks
+
+
+def _ld(T):
+    """Row stride of a row-major matrix; a single row may carry any stride
+    (NumPy and torch leave size-1 dimensions' strides arbitrary)."""
+    return T.stride(-2) if T.shape[-2] > 1 else T.shape[-1]
 
 
 def _batched(T, batch_shape, nb):

@@ -13,7 +13,9 @@
 // Layout: int16 codes, 8 per 128-bit vector.  Each thread streams whole
 // vectors (grid-stride, grid = SMs x resident blocks), counts events in
 // registers and flushes them once per block (warp reduce + one atomic per
-// counter).  Optional per-output event bytes are written 8 at a time.
+// counter).  Optional per-output event bytes are written 8 at a time.  The
+// sf16 kernels are compiled with the width's shifts and bounds as constants;
+// other widths take them at run time.
 #include <math.h>
 
 #include "sfb_common.cuh"
@@ -25,89 +27,111 @@ constexpr int kThreads = 256;
 
 // floor(ua 2^sh / ub) for 0 <= ua < ub < 2^15, sh <= 15 (the quotient is < 2^15).
 // Reciprocal estimate, then one exact integer correction:
-//   x = ua 2^sh / ub;  both operands convert to float exactly (< 2^23, by the
-//   2^23 bias trick); rcp.approx has relative error < 2^-22 and the product
-//   rounds once more, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.
-//   Rounding it to the nearest integer gives floor(x) or floor(x) + 1, and the
-//   remainder's sign tells which.
+//   x = ua 2^sh / ub.  ua 2^sh and ub convert to float exactly with the
+//   exponent-bias trick (ua < 2^23 placed in the mantissa under exponent
+//   23 + sh); rcp.approx has relative error < 2^-22 and the product rounds
+//   once, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding
+//   it to the nearest integer (the 1.5 * 2^23 bias) gives floor(x) or
+//   floor(x) + 1, and the sign of the remainder tells which.
+// Outside the precondition (ua >= ub) the result is meaningless but every
+// step stays defined (unsigned arithmetic); callers discard it there.
 __device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
-    const float fa = __int_as_float(0x4B000000 | ua) - 8388608.0f;
+    const float fa = __int_as_float(((150 + sh) << 23) | ua) - __int_as_float((150 + sh) << 23);
     const float fb = __int_as_float(0x4B000000 | ub) - 8388608.0f;
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fb));
-    const float est = fa * r * __int_as_float((127 + sh) << 23);      // times 2^sh, exact
-    const int q0 = __float_as_int(est + 12582912.0f) - 0x4B400000;    // nearest integer (est < 2^22)
-    const int rem = (int)(ua << sh) - q0 * (int)ub;
-    return (unsigned)(q0 + (rem >> 31));                               // q0 - 1 when rem < 0
+    const unsigned q0 = (unsigned)__float_as_int(fa * r + 12582912.0f) - 0x4B400000u;
+    const unsigned rem = (ua << sh) - q0 * ub;
+    return q0 + (unsigned)((int)rem >> 31);                            // q0 - 1 when rem < 0
 }
 
-template <int OP>
-__device__ __forceinline__ int ew_one(int a, int b, int c, const Width w, int pow_n, unsigned &fl) {
+// Events one output raised; each op sets only the ones it can raise, so the
+// compiler drops the others from the tally.
+struct Ev {
+    bool over = false, under = false, div0 = false, inval = false;
+};
+
+// Width constants, folded at compile time for BITS != 0 (the sf16 kernels).
+template <int BITS>
+__device__ __forceinline__ Width wfix(Width w) {
+    if constexpr (BITS != 0) return Width{BITS, BITS - 1, (1 << (BITS - 1)) - 1};
+    return w;
+}
+
+// 0 < |p| < 2^sh: a nonzero product that truncates to 0.
+__device__ __forceinline__ bool small_nonzero(int p, int sh) {
+    return (unsigned)(p + ((1 << sh) - 1)) <= (unsigned)((2 << sh) - 2) && p != 0;
+}
+
+template <int OP, int BITS>
+__device__ __forceinline__ int ew_one(int a, int b, int c, Width w0, int pow_n, Ev &ev) {
+    const Width w = wfix<BITS>(w0);
     const int M = w.M, sh = w.sh;
     if constexpr (OP == SFB_OP_ADD || OP == SFB_OP_SUB) {
         const int s = (OP == SFB_OP_ADD) ? a + b : a - b;
-        fl = (s > M || s < -M) ? SFB_F_OVERFLOW : 0u;
-        return clampi(s, -M, M);
+        const int r = clampi(s, -M, M);
+        ev.over = r != s;
+        return r;
     } else if constexpr (OP == SFB_OP_MUL) {
         const int p = a * b;
-        const int k = tdiv_pow2(p, sh);
-        fl = (p != 0 && k == 0) ? SFB_F_UNDERFLOW : 0u;
-        return k;
+        ev.under = small_nonzero(p, sh);
+        return tdiv_pow2(p, sh);
     } else if constexpr (OP == SFB_OP_FMA) {
+        // a product that truncates to 0 leaves c unchanged and in range, so
+        // the fma's underflow needs no "and not overflow" term
         const int p = a * b;
-        const int k = tdiv_pow2(p, sh);
-        const int s = k + c;
-        const bool ov = s > M || s < -M;
-        fl = (ov ? SFB_F_OVERFLOW : 0u) | ((!ov && p != 0 && k == 0) ? SFB_F_UNDERFLOW : 0u);
-        return clampi(s, -M, M);
+        const int s = tdiv_pow2(p, sh) + c;
+        const int r = clampi(s, -M, M);
+        ev.over = r != s;
+        ev.under = small_nonzero(p, sh);
+        return r;
     } else if constexpr (OP == SFB_OP_DIV) {
-        if (b == 0) {
-            fl = SFB_F_DIVIDE;
-            return a > 0 ? M : (a < 0 ? -M : 0);
-        }
+        // branch-free: every lane computes the quotient (meaningless where
+        // |a| >= |b| or b == 0, and discarded there), then selects
+        const bool z = b == 0;
         const unsigned ua = (unsigned)abs(a), ub = (unsigned)abs(b);
-        if (a != 0 && ua >= ub) {
-            fl = SFB_F_OVERFLOW;
-            return ((a ^ b) >= 0) ? M : -M;
-        }
-        fl = 0u;
-        const int q = (int)udiv_small(ua, ub, sh);
-        return ((a ^ b) < 0) ? -q : q;
+        const bool ov = !z && a != 0 && ua >= ub;
+        const unsigned q = udiv_small(ua, ub + z, sh);
+        const int s = (a ^ b) >> 31;                 // -1 where the quotient is negative
+        const int sq = ((int)q ^ s) - s;
+        const int sat = a == 0 ? 0 : ((M ^ s) - s);  // +-M with the quotient's sign; 0/0 -> 0
+        ev.over = ov;
+        ev.div0 = z;
+        return (z || ov) ? sat : sq;
     } else if constexpr (OP == SFB_OP_NEG) {
-        fl = 0u;
         return -a;
     } else if constexpr (OP == SFB_OP_ABS) {
-        fl = 0u;
         return abs(a);
     } else if constexpr (OP == SFB_OP_SQRT) {
-        if (a < 0) {
-            fl = SFB_F_INVALID;
-            return 0;
-        }
-        fl = 0u;
-        const int x = a << sh;  // < 2^30
-        int r = (int)sqrtf((float)x);  // within 1 of floor(sqrt(x)) for x < 2^30
-        if (r * r > x) r -= 1;
-        if ((r + 1) * (r + 1) <= x) r += 1;
+        ev.inval = a < 0;
+        const int x = max(a, 0) << sh;      // < 2^30
+        int r = (int)sqrtf((float)x);       // within 1 of floor(sqrt(x)) for x < 2^30
+        r -= (r * r > x);
+        r += ((r + 1) * (r + 1) <= x);
         return r;
     } else {  // SFB_OP_POW
         int k = a;
         bool un = false;
         for (int i = 1; i < pow_n; i++) {
             const int p = k * a;
+            un |= small_nonzero(p, sh);
             k = tdiv_pow2(p, sh);
-            un |= (p != 0 && k == 0);
         }
-        fl = un ? SFB_F_UNDERFLOW : 0u;
+        ev.under = un;
         return k;
     }
 }
 
-__device__ __forceinline__ void tally(Counts &c, unsigned fl) {
-    c.over += fl & 1u;
-    c.under += (fl >> 1) & 1u;
-    c.div0 += (fl >> 2) & 1u;
-    c.inval += (fl >> 3) & 1u;
+__device__ __forceinline__ void tally(Counts &c, const Ev &e) {
+    c.over += e.over;
+    c.under += e.under;
+    c.div0 += e.div0;
+    c.inval += e.inval;
+}
+
+__device__ __forceinline__ unsigned flag_byte(const Ev &e) {
+    return (e.over ? SFB_F_OVERFLOW : 0u) | (e.under ? SFB_F_UNDERFLOW : 0u) | (e.div0 ? SFB_F_DIVIDE : 0u) |
+           (e.inval ? SFB_F_INVALID : 0u);
 }
 
 union Vec8 {
@@ -115,7 +139,7 @@ union Vec8 {
     int16_t h[8];
 };
 
-template <int OP, bool FLAGS>
+template <int OP, int BITS, bool FLAGS>
 __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict__ a, const int16_t *__restrict__ b,
                                                      const int16_t *__restrict__ c, int16_t *__restrict__ out,
                                                      uint8_t *__restrict__ flags, int64_t n, Width w, int pow_n,
@@ -139,10 +163,10 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
             uint64_t fb = 0;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                unsigned fl;
-                vo.h[j] = (int16_t)ew_one<OP>(va.h[j], kB ? vb.h[j] : 0, kC ? vc.h[j] : 0, w, pow_n, fl);
-                tally(cnt, fl);
-                fb |= (uint64_t)fl << (8 * j);
+                Ev ev;
+                vo.h[j] = (int16_t)ew_one<OP, BITS>(va.h[j], kB ? vb.h[j] : 0, kC ? vc.h[j] : 0, w, pow_n, ev);
+                tally(cnt, ev);
+                if constexpr (FLAGS) fb |= (uint64_t)flag_byte(ev) << (8 * j);
             }
             __stcs(reinterpret_cast<uint4 *>(out) + v, vo.u);
             if constexpr (FLAGS) __stcs(reinterpret_cast<unsigned long long *>(flags) + v, (unsigned long long)fb);
@@ -150,10 +174,10 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
         done = nv << 3;
     }
     for (int64_t i = done + tid; i < n; i += stride) {
-        unsigned fl;
-        out[i] = (int16_t)ew_one<OP>(a[i], kB ? b[i] : 0, kC ? c[i] : 0, w, pow_n, fl);
-        tally(cnt, fl);
-        if constexpr (FLAGS) flags[i] = (uint8_t)fl;
+        Ev ev;
+        out[i] = (int16_t)ew_one<OP, BITS>(a[i], kB ? b[i] : 0, kC ? c[i] : 0, w, pow_n, ev);
+        tally(cnt, ev);
+        if constexpr (FLAGS) flags[i] = (uint8_t)flag_byte(ev);
     }
     flush_counts(cnt, counts, sc);
 }
@@ -168,10 +192,14 @@ int launch(const int16_t *a, const int16_t *b, const int16_t *c, int16_t *out, u
     const int64_t max_blocks = (int64_t)sm_count() * (2048 / kThreads);
     int blocks = (int)std::min<int64_t>(max_blocks, (work + kThreads - 1) / kThreads);
     if (blocks < 1) blocks = 1;
-    if (flags)
-        ew_kernel<OP, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
-    else
-        ew_kernel<OP, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    const bool f = flags != nullptr;
+    if (w.bits == 16) {
+        if (f) ew_kernel<OP, 16, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+        else ew_kernel<OP, 16, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    } else {
+        if (f) ew_kernel<OP, 0, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+        else ew_kernel<OP, 0, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    }
     return check_launch("sfb_elementwise");
 }
 
