@@ -13,6 +13,8 @@ hand-written CUDA kernels in ``libsfb200.so`` behind the reference's
 """
 from __future__ import annotations
 
+from ._array import (DTYPES, SFArray, SFDType, addmm, array, asarray, div, dot, fma, from_codes, full, matmul,
+                     resolve_dtype, sqrt, zeros)
 from ._config import accumulate, config, getaccumulate, getconfig, setaccumulate
 from ._device import HOST, B200Device, Device, devices, get_device, register_device
 from ._errors import *  # noqa: F401,F403
@@ -23,6 +25,21 @@ from ._status import SFStatus
 
 __version__ = "0.1.0"
 
-__all__ = ["SFFormat", "FORMATS", "MIN_BITS", "MAX_BITS", "SFStatus", "Device", "B200Device", "HOST",
-           "devices", "get_device", "register_device", "errstate", "geterr", "seterr", "config", "getconfig",
-           "accumulate", "getaccumulate", "setaccumulate", "__version__"] + list(_errors_all)
+globals().update({f"sf{b}": DTYPES[b] for b in DTYPES})
+dtypes = tuple(DTYPES[b] for b in sorted(DTYPES))
+
+
+def dtype(spec):
+    """'sf16', 16 or sf.sf16 -> the sf16 dtype."""
+    return resolve_dtype(spec)
+
+
+def device(name="b200"):
+    return get_device(name)
+
+
+__all__ = ["SFFormat", "FORMATS", "MIN_BITS", "MAX_BITS", "SFStatus", "SFArray", "SFDType", "Device",
+           "B200Device", "HOST", "devices", "get_device", "register_device", "device", "errstate", "geterr",
+           "seterr", "config", "getconfig", "accumulate", "getaccumulate", "setaccumulate", "array", "asarray",
+           "from_codes", "zeros", "full", "matmul", "dot", "addmm", "fma", "div", "sqrt", "dtype", "dtypes",
+           "__version__"] + [f"sf{b}" for b in DTYPES] + list(_errors_all)

@@ -209,11 +209,17 @@ class B200Device(Device):
     def run(self, op, fmt, *operands, **kw):
         """Execute ``op`` on int64 code arrays (src/sf/_device.py:96-106).
         Returns ``(codes, flags)``: int64 codes of the broadcast output shape
-        and a dict of boolean masks for the events ``op`` can raise."""
-        if op not in ARITY:
-            raise SFUnsupportedError(f"{op} is not an op of the {self.name} target")
+        and a dict of boolean masks for the events ``op`` can raise.  Counts
+        one launch in ``launches``."""
         with self._lock:
             self.launches += 1
+        return self.evaluate(op, fmt, *operands, **kw)
+
+    def evaluate(self, op, fmt, *operands, **kw):
+        """``run`` without counting a launch: the pre-flight probe and replay
+        use it, so ``launches`` counts only the ops the runtime committed to."""
+        if op not in ARITY:
+            raise SFUnsupportedError(f"{op} is not an op of the {self.name} target")
         ops = [np.asarray(o, dtype=np.int64) for o in operands[:ARITY[op]]]
         if op in ("matmul", "matmul_wide"):
             out_shape = np.broadcast_shapes(ops[0].shape[:-2], ops[1].shape[:-2]) + (ops[0].shape[-2],

@@ -10,7 +10,7 @@
 //   sqrt     floor(sqrt(a S)), a < 0 -> 0 and invalid                 (:134-142)
 //   pow      chain of mul, underflow if any step underflowed          (:145-156)
 //
-// Layout: int16 codes, 8 per 128-bit vector.  Each thread streams whole
+// Layout: int16 codes, 8 per 128-bit vector.  Each thread streams pairs of
 // vectors (grid-stride, grid = SMs x resident blocks), counts events in
 // registers and flushes them once per block (warp reduce + one atomic per
 // counter).  Optional per-output event bytes are written 8 at a time.  The
@@ -154,22 +154,41 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t done = 0;
     if (vec_ok) {
+        // two vectors per thread per iteration, loads issued before any math,
+        // so each thread keeps up to 6 x 16 B in flight
         const int64_t nv = n >> 3;
-        for (int64_t v = tid; v < nv; v += stride) {
-            Vec8 va, vb, vc, vo;
-            va.u = __ldcs(reinterpret_cast<const uint4 *>(a) + v);
-            if constexpr (kB) vb.u = __ldcs(reinterpret_cast<const uint4 *>(b) + v);
-            if constexpr (kC) vc.u = __ldcs(reinterpret_cast<const uint4 *>(c) + v);
-            uint64_t fb = 0;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                Ev ev;
-                vo.h[j] = (int16_t)ew_one<OP, BITS>(va.h[j], kB ? vb.h[j] : 0, kC ? vc.h[j] : 0, w, pow_n, ev);
-                tally(cnt, ev);
-                if constexpr (FLAGS) fb |= (uint64_t)flag_byte(ev) << (8 * j);
+        for (int64_t v = tid; v < nv; v += 2 * stride) {
+            const int64_t v2 = v + stride;
+            const bool has2 = v2 < nv;
+            Vec8 va[2], vb[2], vc[2], vo[2];
+            va[0].u = __ldcs(reinterpret_cast<const uint4 *>(a) + v);
+            if constexpr (kB) vb[0].u = __ldcs(reinterpret_cast<const uint4 *>(b) + v);
+            if constexpr (kC) vc[0].u = __ldcs(reinterpret_cast<const uint4 *>(c) + v);
+            if (has2) {
+                va[1].u = __ldcs(reinterpret_cast<const uint4 *>(a) + v2);
+                if constexpr (kB) vb[1].u = __ldcs(reinterpret_cast<const uint4 *>(b) + v2);
+                if constexpr (kC) vc[1].u = __ldcs(reinterpret_cast<const uint4 *>(c) + v2);
+            } else {
+                va[1].u = make_uint4(0, 0, 0, 0);
+                vb[1].u = va[1].u;
+                vc[1].u = va[1].u;
             }
-            __stcs(reinterpret_cast<uint4 *>(out) + v, vo.u);
-            if constexpr (FLAGS) __stcs(reinterpret_cast<unsigned long long *>(flags) + v, (unsigned long long)fb);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if (h == 1 && !has2) break;
+                uint64_t fb = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    Ev ev;
+                    vo[h].h[j] = (int16_t)ew_one<OP, BITS>(va[h].h[j], kB ? vb[h].h[j] : 0, kC ? vc[h].h[j] : 0, w,
+                                                           pow_n, ev);
+                    tally(cnt, ev);
+                    if constexpr (FLAGS) fb |= (uint64_t)flag_byte(ev) << (8 * j);
+                }
+                const int64_t vv = h ? v2 : v;
+                __stcs(reinterpret_cast<uint4 *>(out) + vv, vo[h].u);
+                if constexpr (FLAGS) __stcs(reinterpret_cast<unsigned long long *>(flags) + vv, (unsigned long long)fb);
+            }
         }
         done = nv << 3;
     }
@@ -182,25 +201,38 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
     flush_counts(cnt, counts, sc);
 }
 
+template <typename K>
+int resident_blocks(K kernel) {
+    int nb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, kThreads, 0) != cudaSuccess || nb < 1) nb = 1;
+    return nb;
+}
+
+template <int OP, int BITS, bool FLAGS>
+int launch_one(const int16_t *a, const int16_t *b, const int16_t *c, int16_t *out, uint8_t *flags, int64_t n,
+               Width w, int pow_n, bool vec_ok, sfb_counts *counts, cudaStream_t st) {
+    auto kern = ew_kernel<OP, BITS, FLAGS>;
+    static const int per_sm = resident_blocks(kern);   // grid = SMs x resident blocks
+    const int64_t work = vec_ok ? (n >> 4) + 1 : n;
+    const int64_t max_blocks = (int64_t)sm_count() * per_sm;
+    int blocks = (int)std::min<int64_t>(max_blocks, (work + kThreads - 1) / kThreads);
+    if (blocks < 1) blocks = 1;
+    kern<<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
+    return check_launch("sfb_elementwise");
+}
+
 template <int OP>
 int launch(const int16_t *a, const int16_t *b, const int16_t *c, int16_t *out, uint8_t *flags, int64_t n,
            Width w, int pow_n, sfb_counts *counts, cudaStream_t st) {
     const bool vec_ok = ((uintptr_t)a % 16 == 0) && (b == nullptr || (uintptr_t)b % 16 == 0) &&
                         (c == nullptr || (uintptr_t)c % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
                         (flags == nullptr || (uintptr_t)flags % 8 == 0);
-    const int64_t work = vec_ok ? (n >> 3) + 1 : n;
-    const int64_t max_blocks = (int64_t)sm_count() * (2048 / kThreads);
-    int blocks = (int)std::min<int64_t>(max_blocks, (work + kThreads - 1) / kThreads);
-    if (blocks < 1) blocks = 1;
     const bool f = flags != nullptr;
-    if (w.bits == 16) {
-        if (f) ew_kernel<OP, 16, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
-        else ew_kernel<OP, 16, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
-    } else {
-        if (f) ew_kernel<OP, 0, true><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
-        else ew_kernel<OP, 0, false><<<blocks, kThreads, 0, st>>>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts);
-    }
-    return check_launch("sfb_elementwise");
+    if (w.bits == 16)
+        return f ? launch_one<OP, 16, true>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts, st)
+                 : launch_one<OP, 16, false>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts, st);
+    return f ? launch_one<OP, 0, true>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts, st)
+             : launch_one<OP, 0, false>(a, b, c, out, flags, n, w, pow_n, vec_ok, counts, st);
 }
 
 }  // namespace

@@ -104,6 +104,18 @@ def main(ref: str = "/root/reference") -> None:
                                            "overflow": ev["overflow"].astype(int).tolist(),
                                            "underflow": ev["underflow"].astype(int).tolist()})
 
+    # casts of host floats (asarray's input conversion), every width
+    runs["cast"] = []
+    crng = np.random.default_rng(99)
+    for bits in (16, 12, 8, 4):
+        S = 1 << (bits - 1)
+        vals = np.concatenate([crng.uniform(-1.2, 1.2, 200), (np.arange(-40, 41) + 0.5) / S,
+                               [0.0, -0.0, 1.0, -1.0, 1 - 2.0 ** -bits, -(1 - 2.0 ** -bits), 2.0 ** -bits,
+                                -2.0 ** -bits, 2.0 ** -(bits + 1), np.inf, -np.inf, np.nan, 1e-300]])
+        k, ev = vec.cast_array(FORMATS[bits], vals)
+        runs["cast"].append({"bits": bits, "values": [repr(float(v)) for v in vals], "codes": k.tolist(),
+                             **{e: m.astype(int).tolist() for e, m in ev.items()}})
+
     # the 512 x 512 chain workload, whole
     A, B = workloads.chain_square(512, 0)
     q, ev = _linalg.matmul_codes(FORMATS[16], A, B)
