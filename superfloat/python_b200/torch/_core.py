@@ -1,0 +1,341 @@
+"""The SF linear / matmul of converted layers, with the scale policy, on the B200.
+
+Same steps and the same float64 arithmetic as the reference's torch core
+(src/sf/torch/_core.py:336-433), run on the GPU:
+
+1. ``sanitize``: NaN / inf in x, W, b go through the error policy
+   (src/sf/torch/_core.py:200-232);
+2. weight scale ``s_w`` per tensor or per channel and ``W_code = cast(W / s_w)``
+   (:256-296); cached per weight tensor version, since inference weights do
+   not change between calls;
+3. activation scale ``a``: ``a0 = max|x| / max``, then with
+   ``headroom="bound"`` raised until the L1 bound proves that no chain step and
+   no bias add can saturate (:306-331);
+4. the chain matmul ``x_code @ W_code^T`` and the one saturating bias add,
+   fused in libsfb200's chain kernel (exact per-output events);
+5. ``y = acc / 2^(N-1) * a * s_w`` in float64.
+
+Every float64 operation here (division, multiplication, round half to even)
+is IEEE correctly rounded on the GPU as in NumPy, so the codes, scales and
+outputs are the reference's, bit for bit.
+"""
+from __future__ import annotations
+
+import math
+import weakref
+from collections import OrderedDict
+from dataclasses import dataclass
+
+import torch
+
+from .. import _config, _errstate
+from .._device import get_device
+from .._format import FORMATS, SFFormat
+
+WSCALES = ("per_tensor", "per_channel")
+HEADROOMS = ("bound", "none")
+ACCUMULATES = ("chain", "wide")
+_MAX_ITER = 32
+
+
+@dataclass
+class CoreResult:
+    y: torch.Tensor
+    saturated: int | None
+    exact: bool
+    underflow: int | None
+    input_underflow: int
+    weight_underflow: int
+    bias_saturated: int
+    headroom_bits: float
+    outputs: int
+    act_scale: float = 1.0
+    accumulate: str = "chain"
+    shift_min: int | None = None
+    shift_max: int | None = None
+    h: int | None = None
+    redone: int = 0
+    flushed: int | None = None
+    acc_clipped: int | None = None
+    guard_raised: int = 0
+
+
+def check_args(bits, wscale=None, headroom=None, accumulate=None) -> SFFormat:
+    if accumulate is not None and accumulate not in ACCUMULATES:
+        raise ValueError(f"accumulate must be one of {ACCUMULATES}, got {accumulate!r}")
+    if bits not in FORMATS:
+        raise ValueError(f"unsupported SF width {bits}")
+    if wscale is not None and wscale not in WSCALES:
+        raise ValueError(f"scale must be one of {WSCALES}, got {wscale!r}")
+    if headroom is not None and headroom not in HEADROOMS:
+        raise ValueError(f"headroom must be one of {HEADROOMS}, got {headroom!r}")
+    return FORMATS[bits]
+
+
+def target():
+    """The target the torch path runs on (``default_device``)."""
+    dev = get_device(_config.get("default_device"))
+    if not hasattr(dev, "run_device"):
+        from .._errors import SFUnsupportedError
+        raise SFUnsupportedError(f"{dev.name} cannot run the torch path (no device-resident entry)")
+    return dev
+
+
+# --- elementwise helpers on float64 device tensors --------------------------------------------
+
+def finite_absmax(x: torch.Tensor) -> float:
+    if x.numel() == 0:
+        return 0.0
+    fin = torch.isfinite(x)
+    if not bool(fin.any()):
+        return 0.0
+    return float(torch.where(fin, x.abs(), torch.zeros((), dtype=x.dtype, device=x.device)).max())
+
+
+def sanitize(x: torch.Tensor, fmt: SFFormat, what: str) -> torch.Tensor:
+    """NaN -> invalid event, +-inf -> overflow event; under a non-raising policy
+    NaN becomes 0 and +-inf the tensor's largest finite magnitude (or +-max)."""
+    nan = torch.isnan(x)
+    inf = torch.isinf(x)
+    n_nan, n_inf = int(nan.sum()), int(inf.sum())
+    if n_nan:
+        _errstate.handle("invalid", f"{fmt.name} {what}: invalid (NaN) in {n_nan} of {x.numel()} element(s)")
+    if n_inf:
+        _errstate.handle("overflow", f"{fmt.name} {what}: ±inf in {n_inf} of {x.numel()} element(s) (saturates)")
+    if n_nan:
+        x = torch.where(nan, torch.zeros((), dtype=x.dtype, device=x.device), x)
+    if n_inf:
+        big = finite_absmax(x)
+        if big == 0.0:
+            big = fmt.max_code / fmt.scale
+        x = torch.where(inf, torch.sign(x) * big, x)
+    return x
+
+
+def cast(fmt: SFFormat, v: torch.Tensor):
+    """float64 values -> int16 codes: round half to even, saturate at
+    |v| >= 1 - 2^-N, NaN -> 0.  Returns (codes, {event: count tensor})."""
+    nan = torch.isnan(v)
+    over = (v.abs() >= 1.0 - 2.0 ** -fmt.bits) & ~nan
+    fits = ~over & ~nan
+    k = torch.round(torch.where(fits, v, torch.zeros((), dtype=v.dtype, device=v.device)) * fmt.scale)
+    k = torch.where(over, torch.sign(v) * fmt.max_code, k)
+    under = fits & (k == 0) & (v != 0)
+    return k.to(torch.int16), {"overflow": over.sum(), "underflow": under.sum(), "invalid": nan.sum()}
+
+
+# --- weights -----------------------------------------------------------------------------------
+
+def weight_scales(fmt: SFFormat, w: torch.Tensor, wscale: str) -> torch.Tensor:
+    """One positive scale per output row from the finite magnitudes
+    (src/sf/torch/_core.py:277-289)."""
+    m = fmt.max_code / fmt.scale
+    fin = torch.where(torch.isfinite(w), w.abs(), torch.zeros((), dtype=w.dtype, device=w.device))
+    N = w.shape[0]
+    if wscale == "per_tensor":
+        amax = float(fin.max()) if w.numel() else 0.0
+        return torch.full((N,), amax / m if amax > 0 else 1.0, dtype=torch.float64, device=w.device)
+    amax = fin.max(dim=1).values if w.numel() else torch.zeros(N, dtype=torch.float64, device=w.device)
+    return torch.where(amax > 0, amax / m, torch.ones((), dtype=torch.float64, device=w.device))
+
+
+@dataclass
+class PreparedWeight:
+    """A weight as the chain kernel reads it: W_code^T (K, N) int16, the
+    scales, and the L1 statistics the headroom bound needs."""
+
+    kwT: torch.Tensor
+    s_w: torch.Tensor
+    w_under: int
+    max_abs: int          # max |W_code|
+    max_col_l1: int       # max_n sum_k |W_code[n, k]|
+
+
+def prepare_weight(fmt: SFFormat, w: torch.Tensor, wscale: str) -> PreparedWeight:
+    s = weight_scales(fmt, w, wscale)
+    codes, ev = cast(fmt, w / s[:, None])
+    kwT = codes.t().contiguous()
+    if codes.numel():
+        stats = torch.stack([codes.abs().max().to(torch.int64), codes.abs().to(torch.int64).sum(1).max()]).cpu()
+        mx, l1 = int(stats[0]), int(stats[1])
+    else:
+        mx = l1 = 0
+    return PreparedWeight(kwT, s, int(ev["underflow"]), mx, l1)
+
+
+class WeightCache:
+    """Prepared weights keyed by the tensor's storage, shape, strides and
+    version counter (an in-place update prepares it again), with a weak
+    reference to the owning tensor so a new tensor at a freed address is never
+    mistaken for the old one.  Least recently used entries go first."""
+
+    def __init__(self, max_entries: int = 512):
+        self.items = OrderedDict()
+        self.max_entries = max_entries
+        self.hits = self.misses = 0
+
+    @staticmethod
+    def _owner(w):
+        while w._base is not None:
+            w = w._base
+        return w
+
+    def get(self, fmt, w: torch.Tensor, wscale: str, dev) -> PreparedWeight:
+        key = (w.untyped_storage().data_ptr(), w.storage_offset(), tuple(w.shape), tuple(w.stride()),
+               w._version, w.dtype, str(w.device), fmt.bits, wscale, str(dev))
+        hit = self.items.get(key)
+        if hit is not None and hit[0]() is not None:
+            self.items.move_to_end(key)
+            self.hits += 1
+            return hit[1]
+        self.misses += 1
+        wd = w.detach().to(device=dev, dtype=torch.float64)
+        finite = bool(torch.isfinite(wd).all())
+        wd = sanitize(wd, fmt, "linear weight")
+        pw = prepare_weight(fmt, wd, wscale)
+        if finite:                                  # a NaN / inf weight raises its events on every call
+            self.items[key] = (weakref.ref(self._owner(w)), pw)
+        while len(self.items) > self.max_entries:
+            self.items.popitem(last=False)
+        return pw
+
+    def clear(self):
+        self.items.clear()
+
+
+weight_cache = WeightCache()
+
+
+# --- the activation scale ------------------------------------------------------------------
+
+def _bound(fmt, kx: torch.Tensor, b_max_abs: int, b_max_col_l1: int) -> int:
+    """The reference's L1 bound (src/sf/_linalg.py:84-106), with the right
+    operand's statistics precomputed."""
+    if kx.numel() == 0 or kx.shape[-1] == 0:
+        return 0
+    ax = kx.abs().to(torch.int64)
+    st = torch.stack([ax.sum(-1).max(), ax.max()]).cpu()
+    row_l1, mx = int(st[0]), int(st[1])
+    return min(row_l1 * b_max_abs, mx * b_max_col_l1) // fmt.scale
+
+
+def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_over_scale, headroom: str):
+    """The activation scale search (src/sf/torch/_core.py:306-331).
+    Returns (codes, events, a, a0)."""
+    m = fmt.max_code / fmt.scale
+    amax = finite_absmax(x)
+    a0 = amax / m if amax > 0 else 1.0
+    a = a0
+    kx, ev = cast(fmt, x / a)
+    if headroom == "none":
+        return kx, ev, a, a0
+    a_bias = bias_over_scale(None)
+    if a_bias is not None and math.isfinite(a_bias) and a_bias > a:
+        a = a_bias
+        kx, ev = cast(fmt, x / a)
+    for _ in range(_MAX_ITER):
+        ratio = bias_over_scale(a)
+        bias_codes = int(math.ceil(ratio)) if ratio is not None and math.isfinite(ratio) else 0
+        bound = _bound(fmt, kx, b_max_abs, b_max_col_l1) + bias_codes
+        if bound <= fmt.max_code:
+            return kx, ev, a, a0
+        a *= max(bound / fmt.max_code, 1.0 + 2.0 ** -20)
+        kx, ev = cast(fmt, x / a)
+    raise RuntimeError("sf: headroom search did not converge")
+
+
+# --- linear ----------------------------------------------------------------------------------
+
+def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_tensor",
+           headroom: str = "bound", dev=None) -> CoreResult:
+    """x: (R, K), w: (N, K), b: (N,) or None, any float dtype, any device;
+    the result ``y`` is float64 on the target's CUDA device."""
+    fmt = check_args(bits, wscale, headroom)
+    dev = dev or target()
+    cuda = dev.torch_device
+    S, M = fmt.scale, fmt.max_code
+    x = sanitize(x.detach().to(device=cuda, dtype=torch.float64), fmt, "linear input")
+    pw = weight_cache.get(fmt, w, wscale, cuda)
+    if b is not None:
+        b = sanitize(b.detach().to(device=cuda, dtype=torch.float64), fmt, "linear bias")
+    if b is not None and b.numel():
+        need = b.abs() / pw.s_w                                     # may hold inf
+        fin = torch.isfinite(need)
+        a_bias = float(torch.where(fin, need, torch.zeros((), dtype=need.dtype, device=cuda)).max()) / (M / S) \
+            if bool(fin.any()) else 0.0
+
+        def bias_over_scale(a):
+            if a is None:
+                return a_bias
+            return float((need / a).max() * S)
+    else:
+        def bias_over_scale(a):
+            return None if a is None else 0.0
+
+    kx, ev_x, a, a0 = activation(fmt, x, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom)
+    bias_sat = 0
+    kb = None
+    if b is not None:
+        kb, ev_b = cast(fmt, b / (a * pw.s_w))
+        bias_sat = int(ev_b["overflow"])
+    acc, cnt, _ = dev.run_device("matmul", fmt, kx, pw.kwT, bias=kb)
+    c = cnt.cpu()
+    y = acc.to(torch.float64) / S * a * pw.s_w[None, :]
+    return CoreResult(y=y, saturated=int(c[0]), exact=True, underflow=int(c[1]),
+                      input_underflow=int(ev_x["underflow"]), weight_underflow=pw.w_under,
+                      bias_saturated=bias_sat, headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
+                      outputs=int(acc.numel()), act_scale=a)
+
+
+def matmul(a_val: torch.Tensor, b_val: torch.Tensor, bits: int, headroom: str = "bound", dev=None) -> CoreResult:
+    """(..., M, K) @ (..., K, N) of two activations, both with a dynamic
+    per-tensor scale, headroom on ``a`` (src/sf/torch/_core.py:412-433)."""
+    fmt = check_args(bits, None, headroom)
+    dev = dev or target()
+    cuda = dev.torch_device
+    S, M = fmt.scale, fmt.max_code
+    m = M / S
+    a_val = sanitize(a_val.detach().to(device=cuda, dtype=torch.float64), fmt, "matmul left operand")
+    b_val = sanitize(b_val.detach().to(device=cuda, dtype=torch.float64), fmt, "matmul right operand")
+    bmax = finite_absmax(b_val)
+    s_b = bmax / m if bmax > 0 else 1.0
+    kb, ev_b = cast(fmt, b_val / s_b)
+    if kb.numel() and kb.shape[-2]:
+        ab = kb.abs().to(torch.int64)
+        st = torch.stack([ab.max(), ab.sum(-2).max()]).cpu()
+        b_max, b_l1 = int(st[0]), int(st[1])
+    else:
+        b_max = b_l1 = 0
+    ka, ev_a, a, a0 = activation(fmt, a_val, b_max, b_l1, lambda _a: None if _a is None else 0.0, headroom)
+    acc, cnt, _ = dev.run_device("matmul", fmt, ka, kb)
+    c = cnt.cpu()
+    y = acc.to(torch.float64) / S * a * s_b
+    return CoreResult(y=y, saturated=int(c[0]), exact=True, underflow=int(c[1]),
+                      input_underflow=int(ev_a["underflow"]) + int(ev_b["underflow"]), weight_underflow=0,
+                      bias_saturated=0, headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
+                      outputs=int(acc.numel()), act_scale=a)
+
+
+def fake_quantize(x: torch.Tensor, bits: int, mode: str, scale: float):
+    """Values snapped to the SF grid (src/sf/torch/_core.py:438-460).
+    Returns (values float64, codes, scale, event counts)."""
+    fmt = check_args(bits)
+    if mode == "none":
+        s = 1.0
+    elif mode == "dynamic":
+        amax = finite_absmax(x)
+        s = amax / (fmt.max_code / fmt.scale) if amax > 0 else 1.0
+    elif mode == "fixed":
+        if not (scale > 0 and math.isfinite(scale)):
+            raise ValueError("scale must be a positive finite float")
+        s = float(scale)
+    else:
+        raise ValueError(f"unknown quantize mode {mode!r}")
+    codes, ev = cast(fmt, x / s)
+    return codes.to(torch.float64) / fmt.scale * s, codes, s, ev
+
+
+def dequantize_weight(fmt, w: torch.Tensor, wscale: str) -> torch.Tensor:
+    s = weight_scales(fmt, w, wscale)
+    codes, _ = cast(fmt, w / s[:, None])
+    return codes.to(torch.float64) / fmt.scale * s[:, None]
