@@ -179,6 +179,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-matmul", action="store_true")
+    ap.add_argument("--matmul-only", type=int, default=0, metavar="SIZE",
+                    help="time only the wide and chain matmuls, wide at SIZE^3 (a small case for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
@@ -189,6 +191,9 @@ def main():
     import torch.distributed as dist
     from superfloat.python_b200 import FORMATS, B200Device, _lib, workloads
     torch.cuda.set_device(local)
+    if args.matmul_only:
+        print(json.dumps(bench_matmuls(B200Device(local), FORMATS[16], torch, args.matmul_only)), flush=True)
+        return 0
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -322,15 +327,15 @@ def main():
     return 0
 
 
-def bench_matmuls(dev, fmt, torch):
+def bench_matmuls(dev, fmt, torch, n=8192):
     from superfloat.python_b200 import workloads
     res = {}
     stream = torch.cuda.current_stream()
-    # wide 8192^3 (the MX engine, v4.9.2, shift 0)
-    A, B = workloads.wide_square(8192, 8192, 8192, 0)
+    # wide n^3 (the MX engine, v4.9.2, shift 0)
+    A, B = workloads.wide_square(n, n, n, 0)
     tA, tB = dev.upload(A), dev.upload(B)
     del A, B
-    out = torch.empty(8192, 8192, dtype=torch.int16, device=dev.torch_device)
+    out = torch.empty(n, n, dtype=torch.int16, device=dev.torch_device)
     cnt = torch.zeros(8, dtype=torch.int64, device=dev.torch_device)
     for _ in range(2):
         dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
@@ -343,7 +348,7 @@ def bench_matmuls(dev, fmt, torch):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    res["wide_8192"] = {"ms": ms, "TOPS": 2 * 8192 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
+    res[f"wide_{n}"] = {"ms": ms, "TOPS": 2 * n ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
     del tA, tB, out
     # chain 512^3
     A, B = workloads.chain_square(512, 0)
