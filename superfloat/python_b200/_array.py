@@ -334,6 +334,8 @@ def _launch(dev, op, fmt, codes, out_shape, kw):
     out, cnt, _ = dev.run_device(op, fmt, *ts, **kw)
     res = out.cpu().numpy().astype(np.int64)
     c = cnt.cpu().numpy()
+    from . import _lib
+    _lib.check_counts(c)
     res = np.broadcast_to(res, out_shape).copy() if res.shape != tuple(out_shape) else res
     return res, {k: int(c[i]) for k, i in _COUNT_INDEX.items()}
 

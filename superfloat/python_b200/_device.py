@@ -232,7 +232,8 @@ class B200Device(Device):
         if op == "matmul_wide" and "shift" in kw and not isinstance(kw["shift"], (int, np.integer)):
             kw = dict(kw)
             kw["shift"] = np.asarray(kw["shift"], dtype=np.int64)
-        codes, _, fl = self.run_device(op, fmt, *xs, flags=True, **kw)
+        codes, cnt, fl = self.run_device(op, fmt, *xs, flags=True, **kw)
+        _lib.check_counts(cnt.cpu().numpy())
         codes = codes.cpu().numpy().astype(np.int64)
         fl = fl.cpu().numpy()
         masks = {e: (fl & _EVENT_BIT[e]) != 0 for e in OP_EVENTS[op]}

@@ -76,6 +76,14 @@ def check(rc: int, what: str) -> None:
     raise SFDeviceError(msg)
 
 
+def check_counts(counts) -> None:
+    """Raise if a kernel recorded a device-side failure (a bounded wait that
+    ran out) in the counters' first reserved slot; ``counts`` is host data."""
+    if int(counts[5]) != 0:
+        raise SFDeviceError(f"a libsfb200 kernel gave up waiting on the device ({int(counts[5])} CTA(s)); "
+                            "the outputs of that call are not valid")
+
+
 def ensure_device(index: int) -> None:
     """sfb_device_init once per device (checks it is an sm_100 part)."""
     if index in _ready_devices:

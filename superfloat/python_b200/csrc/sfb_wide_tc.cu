@@ -1,15 +1,623 @@
-// Tensor-core (tcgen05) path of the wide matmul: not yet enabled; every
-// problem goes to the exact CUDA-core kernel.
+// Wide (MX v4.9.2) matmul on sm_100a tensor cores: the SF16 block (sf9..sf16).
+//
+// The SF16-block product of 15-bit magnitudes a, w (src/sf/_linalg.py:190-198)
+// is t = (a w + 80 - C) >> 8 with C = C(a mod 64, w mod 64) the dropped
+// partial-product columns, C(x, y) = sum_{i<6} x_i ((y << i) mod 64).  Writing
+// X = (a w - C) / 64 (an integer), t = (X + 1) >> 2, so with s = +-1 the
+// product's sign and r = (X + 1) mod 4:
+//
+//     4 sum_k s t = sum_k s (a w - C) / 64  +  sum_k s (1 - r).
+//
+// * sum s (a w - C) is exact integer linear algebra on int8 operands:
+//   the left-aligned signed codes k = s a split into limbs k = 256 h + l
+//   (h signed, l unsigned) give 4 GEMMs, and sum s C = sum_i (s_a bit_i(a))
+//   (s_w ((w << i) mod 64)) 6 more.  They run as tcgen05 kind::i8 MMAs into
+//   three s32 TMEM accumulators by scale: D0 = h.h (x 2^16), D1 = h.l + l.h
+//   (x 2^8), D2 = l.l - sum_i bit_i . C_i (x 1; the C planes are stored
+//   negated).  |D| < 2^31 for K <= 16384.
+// * sum s (1 - r) needs r per product: X mod 4 = (P + 2Q) mod 4 with
+//   P = sum_{i<=6} a_i w_{6-i}, Q = sum_{i<=7} a_i w_{7-i} over the low bits,
+//   computed bit-sliced on the INT pipe, 32 products per 32-bit word
+//   (kernel wide_rem_kernel), about one logic op per product.
+//
+// The sum is the MX accumulator when no chunk of 8 can clip; each output is
+// checked against the bound sum_k |t_k| <= min(rowL1 colmax, rowmax colL1)/256
+// + K, and an output that fails it is recomputed exactly, chunk by chunk, on
+// the CUDA cores.  POP as in the CUDA-core kernel.
+//
+// Pipeline of the GEMM kernel (one CTA per 128 x 128 output tile, 128
+// threads): thread 0 issues TMA loads of 128 x 128-byte operand tiles (128-byte
+// swizzle) into a ring of stages; thread 32 issues the MMAs (one thread, as
+// tcgen05 requires) and commits each stage back to the producer; all four
+// warps then read the TMEM accumulators (tcgen05.ld, one 32-lane quarter per
+// warp) and write sum s (a w - C) / 64 as int64.  Every wait is bounded: on
+// timeout the kernel records an error in the caller's counters and returns
+// after freeing its TMEM.
+#include <cuda.h>
+
 #include "sfb_wide_simt.cuh"
 
 namespace sfb {
 
-int64_t wide_tc_workspace(int, int, int64_t, int64_t, int64_t, int64_t) { return 0; }
+int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
+              int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+              int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn,
+              sfb_counts *counts, cudaStream_t st);
 
-int wide_tc_try(int, int, const int16_t *, const int16_t *, const int8_t *, int, int16_t *, uint8_t *, int64_t,
-                int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                void *, int64_t, sfb_counts *, cudaStream_t, bool *handled) {
+namespace {
+
+constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
+constexpr int STAGES = 6;
+constexpr int NPASS = 10;
+constexpr int NPLANES = 8;         // int8 operand planes per matrix
+constexpr int STAGE_BYTES = 2 * TILE * TILE;
+constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int KMAX = 16384;        // |D| < 2^31 up to this K
+constexpr unsigned kSpinLimit = 1u << 26;
+
+// pass -> (A plane, B plane, accumulator, A signed, B signed)
+__constant__ int c_pass[NPASS][5] = {
+    {0, 0, 0, 1, 1}, {0, 1, 1, 1, 0}, {1, 0, 1, 0, 1}, {1, 1, 2, 0, 0}, {2, 2, 2, 1, 1},
+    {3, 3, 2, 1, 1}, {4, 4, 2, 1, 1}, {5, 5, 2, 1, 1}, {6, 6, 2, 1, 1}, {7, 7, 2, 1, 1}};
+
+// --- PTX wrappers --------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait: false after kSpinLimit polls
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (unsigned i = 0; i < kSpinLimit; i++)
+        if (mbar_try(bar, parity)) return true;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand tile in shared memory, 128-byte swizzle: rows of 128 bytes,
+// 8-row groups 1024 bytes apart (SBO), the leading offset unused (1).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+    d |= (uint64_t)1 << 46;                 // descriptor version for sm_100
+    d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+    return d;
+}
+
+// kind::i8 instruction descriptor: s32 accumulate, K-major A and B, M = N = 128
+__device__ __forceinline__ uint32_t idesc_i8(int a_signed, int b_signed) {
+    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((uint32_t)(TILE >> 3) << 17) |
+           ((uint32_t)(TILE >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = (int32_t)r[i];
+}
+
+// --- operand preparation ------------------------------------------------------------------
+//
+// One thread per (row, 32-k word).  Writes the eight int8 planes (h, l,
+// bit_0..bit_5 of A; h, l, -C_0..-C_5 of B), the nine bit planes of the
+// remainder (bits 0..7 of the magnitude and the sign, 32 k per word), and the
+// row / column L1 norm and maximum of the magnitudes.
+
+template <bool IS_A>
+__global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X, int64_t ld, int rows, int K,
+                                                   int rows_pad, int Kp, int bits, uint8_t *__restrict__ planes,
+                                                   uint32_t *__restrict__ bitp, long long *__restrict__ l1,
+                                                   int *__restrict__ mx) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    const int kw = blockIdx.y;
+    if (r >= rows_pad) return;
+    uint32_t bw[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    long long sum = 0;
+    int mval = 0;
+    const int sh = 16 - bits;
+    for (int half = 0; half < 2; half++) {
+        uint32_t pw[NPLANES][4];
+#pragma unroll
+        for (int p = 0; p < NPLANES; p++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) pw[p][q] = 0;
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) {
+            const int j = half * 16 + jj;
+            const int k = kw * 32 + j;
+            int code = 0;
+            if (r < rows && k < K) code = IS_A ? (int)X[(int64_t)r * ld + k] : (int)X[(int64_t)k * ld + r];
+            const int a = abs(code) << sh;               // 15-bit magnitude as the SF16 block reads it
+            const int s = code < 0;
+            const int kt = s ? -a : a;
+            const uint32_t sh8 = 8 * (jj & 3);
+            pw[0][jj >> 2] |= ((uint32_t)(kt >> 8) & 0xFFu) << sh8;      // h (signed)
+            pw[1][jj >> 2] |= ((uint32_t)kt & 0xFFu) << sh8;             // l (unsigned)
+#pragma unroll
+            for (int i = 0; i < 6; i++) {
+                int v = IS_A ? ((a >> i) & 1) : -(((a << i) & 63));     // A: bit_i(a); B: -((w << i) mod 64)
+                if (s) v = -v;
+                pw[2 + i][jj >> 2] |= ((uint32_t)v & 0xFFu) << sh8;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) bw[i] |= (uint32_t)((a >> i) & 1) << j;
+            bw[8] |= (uint32_t)s << j;
+            sum += a;
+            mval = max(mval, a);
+        }
+#pragma unroll
+        for (int p = 0; p < NPLANES; p++) {
+            uint4 *dst = reinterpret_cast<uint4 *>(planes + ((int64_t)p * rows_pad + r) * Kp + kw * 32 + half * 16);
+            *dst = make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 9; i++) bitp[((int64_t)kw * 9 + i) * rows_pad + r] = bw[i];
+    if (sum) atomicAdd(reinterpret_cast<unsigned long long *>(l1 + r), (unsigned long long)sum);
+    if (mval) atomicMax(mx + r, mval);
+}
+
+// --- the tcgen05 GEMM: sum_k s (a w - C) / 64 per output -----------------------------------
+
+__global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                         const __grid_constant__ CUtensorMap tmB, int nkb,
+                                                         long long *__restrict__ SX, int Np,
+                                                         unsigned long long *__restrict__ err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    // bars[0..S): full, bars[S..2S): empty, bars[2S]: done; then the TMEM address
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
+    __shared__ int s_fail;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * TILE, n0 = blockIdx.x * TILE;
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(smem_u32(&bars[s]), 1);
+            mbar_init(smem_u32(&bars[STAGES + s]), 1);
+        }
+        mbar_init(smem_u32(&bars[2 * STAGES]), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int total = nkb * NPASS;
+
+    int issued = 0;
+    if (threadIdx.x == 0) {
+        // TMA producer
+        for (int it = 0; it < total; it++) {
+            const int s = it % STAGES, round = it / STAGES;
+            if (round > 0 && !mbar_wait(smem_u32(&bars[STAGES + s]), (round - 1) & 1)) {
+                s_fail = 1;
+                break;
+            }
+            if (*(volatile int *)&s_fail) break;
+            const int kb = it / NPASS, p = it % NPASS;
+            const uint32_t full = smem_u32(&bars[s]);
+            uint8_t *sa = smem + s * STAGE_BYTES;
+            mbar_expect_tx(full, STAGE_BYTES);
+            tma_load_3d(smem_u32(sa), &tmA, kb * TILE, m0, c_pass[p][0], full);
+            tma_load_3d(smem_u32(sa + TILE * TILE), &tmB, kb * TILE, n0, c_pass[p][1], full);
+            issued = it + 1;
+        }
+    } else if (threadIdx.x == 32) {
+        // MMA issuer
+        bool started[3] = {false, false, false};
+        for (int it = 0; it < total; it++) {
+            const int s = it % STAGES, round = it / STAGES;
+            if (!mbar_wait(smem_u32(&bars[s]), round & 1)) {
+                s_fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const int p = it % NPASS;
+            const int acc = c_pass[p][2];
+            const uint32_t id = idesc_i8(c_pass[p][3], c_pass[p][4]);
+            const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+            const uint32_t b_addr = a_addr + TILE * TILE;
+#pragma unroll
+            for (int kk = 0; kk < TILE / 32; kk++) {
+                mma_i8(tmem + acc * TILE, smem_desc(a_addr + kk * 32), smem_desc(b_addr + kk * 32), id,
+                       (started[acc] || kk > 0) ? 1u : 0u);
+            }
+            started[acc] = true;
+            mma_commit(smem_u32(&bars[STAGES + s]));
+        }
+        mma_commit(smem_u32(&bars[2 * STAGES]));
+    }
+    __syncwarp();
+    // epilogue: all warps
+    bool ok = mbar_wait(smem_u32(&bars[2 * STAGES]), 0);
+    tc_fence_after();
+    __syncthreads();
+    if (s_fail) ok = false;
+    if (ok) {
+        const int row = m0 + warp * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        long long *dst = SX + (int64_t)row * Np + n0;
+        for (int c = 0; c < TILE / 32; c++) {
+            int32_t d0[32], d1[32], d2[32];
+            tmem_ld32(tmem + lane_base + 0 * TILE + c * 32, d0);
+            tmem_ld32(tmem + lane_base + 1 * TILE + c * 32, d1);
+            tmem_ld32(tmem + lane_base + 2 * TILE + c * 32, d2);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const long long t = ((long long)d0[j] << 16) + ((long long)d1[j] << 8) + (long long)d2[j];
+                dst[c * 32 + j] = t >> 6;            // exact: the total is 64 sum s X
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        atomicAdd(err, 1ull);
+        // let this CTA's copies still in flight land before its shared memory is released
+        for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; it++)
+            (void)mbar_wait(smem_u32(&bars[it % STAGES]), (it / STAGES) & 1);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+}
+
+// --- the bit-sliced remainder, the combination and POP ---------------------------------------
+
+constexpr int RT = 64;     // output tile of the remainder kernel
+constexpr int KC = 8;      // 32-k words per shared-memory chunk
+
+__device__ __forceinline__ uint32_t maj3(uint32_t x, uint32_t y, uint32_t z) { return (x & y) | (z & (x ^ y)); }
+
+struct RemIn {
+    const uint32_t *bitsA, *bitsB;
+    const long long *SX, *rowL1, *colL1;
+    const int *rowMax, *colMax;
+    int Mp, Np, KW;
+    const int16_t *A, *B;
+    int64_t lda, ldb;
+    int M, N, K;
+    const int8_t *shift_arr;
+    int shift;
+    int64_t ssm, ssn;
+    int16_t *out;
+    uint8_t *flags;
+    Width w;
+    MxUnit u;
+    sfb_counts *counts;
+};
+
+// the exact chunk-by-chunk accumulation of one output (an output the bound
+// does not prove clip-free)
+__device__ long long exact_output(const RemIn &in, int m, int n, bool &clip) {
+    const long long lo = -(1ll << 31), hi = (1ll << 31) - 1;
+    long long acc = 0;
+    clip = false;
+    for (int k0 = 0; k0 < in.K; k0 += 8) {
+        long long g = 0;
+        for (int k = k0; k < min(in.K, k0 + 8); k++) {
+            const int ca = in.A[(int64_t)m * in.lda + k], cb = in.B[(int64_t)k * in.ldb + n];
+            const int t = mx_prod16(mx_mag(ca, in.w.bits, true), mx_mag(cb, in.w.bits, true), in.u);
+            g += ((ca ^ cb) < 0) ? -t : t;
+        }
+        long long s = acc + g;
+        if (s < lo || s > hi) clip = true;
+        acc = s < lo ? lo : (s > hi ? hi : s);
+    }
+    return acc;
+}
+
+__global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
+    extern __shared__ __align__(16) uint32_t rs[];
+    uint32_t *sA = rs;                      // [KC][9][RT]
+    uint32_t *sB = rs + KC * 9 * RT;        // [KC][9][RT]
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * RT, n0 = blockIdx.x * RT;
+    int acc1[4][4], acc2[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc1[i][j] = 0, acc2[i][j] = 0;
+
+    for (int kw0 = 0; kw0 < in.KW; kw0 += KC) {
+        const int nkw = min(KC, in.KW - kw0);
+        __syncthreads();
+        for (int e = tid; e < nkw * 9 * (RT / 4); e += 256) {
+            const int q = e % (RT / 4), p = (e / (RT / 4)) % 9, kk = e / (9 * (RT / 4));
+            const int64_t ga = ((int64_t)(kw0 + kk) * 9 + p) * in.Mp + m0 + q * 4;
+            const int64_t gb = ((int64_t)(kw0 + kk) * 9 + p) * in.Np + n0 + q * 4;
+            reinterpret_cast<uint4 *>(sA)[(kk * 9 + p) * (RT / 4) + q] = *reinterpret_cast<const uint4 *>(in.bitsA + ga);
+            reinterpret_cast<uint4 *>(sB)[(kk * 9 + p) * (RT / 4) + q] = *reinterpret_cast<const uint4 *>(in.bitsB + gb);
+        }
+        __syncthreads();
+        for (int kk = 0; kk < nkw; kk++) {
+            uint4 pa[9], pb[9];
+#pragma unroll
+            for (int p = 0; p < 9; p++) {
+                pa[p] = reinterpret_cast<const uint4 *>(sA)[(kk * 9 + p) * (RT / 4) + ty];
+                pb[p] = reinterpret_cast<const uint4 *>(sB)[(kk * 9 + p) * (RT / 4) + tx];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                uint32_t a[9];
+#pragma unroll
+                for (int p = 0; p < 9; p++) a[p] = (&pa[p].x)[i];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    uint32_t w[9];
+#pragma unroll
+                    for (int p = 0; p < 9; p++) w[p] = (&pb[p].x)[j];
+                    // P = sum_{i<=6} a_i w_{6-i} mod 4 by a carry-save tree
+                    const uint32_t t0 = a[0] & w[6], t1 = a[1] & w[5], t2 = a[2] & w[4], t3 = a[3] & w[3];
+                    const uint32_t t4 = a[4] & w[2], t5 = a[5] & w[1], t6 = a[6] & w[0];
+                    const uint32_t s1 = t0 ^ t1 ^ t2, c1 = maj3(t0, t1, t2);
+                    const uint32_t s2 = t3 ^ t4 ^ t5, c2 = maj3(t3, t4, t5);
+                    const uint32_t x0 = s1 ^ s2 ^ t6, c3 = maj3(s1, s2, t6);
+                    // r1 = X1 ^ X0 = P1 ^ Q0 ^ X0, Q0 the parity of sum_{i<=7} a_i w_{7-i}
+                    uint32_t r1 = c1 ^ c2 ^ c3 ^ x0;
+                    r1 ^= (a[0] & w[7]) ^ (a[1] & w[6]) ^ (a[2] & w[5]) ^ (a[3] & w[4]);
+                    r1 ^= (a[4] & w[3]) ^ (a[5] & w[2]) ^ (a[6] & w[1]) ^ (a[7] & w[0]);
+                    const uint32_t neg = a[8] ^ w[8];
+                    acc1[i][j] += __popc(x0) + 4 * __popc(r1 & neg);
+                    acc2[i][j] += __popc(x0 & neg) + __popc(r1);
+                }
+            }
+        }
+    }
+
+    Counts cnt;
+    const long long lim = (1ll << 31) - 1;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty * 4 + i;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx * 4 + j;
+            if (m < in.M && n < in.N) {
+                const long long R = (long long)acc1[i][j] - 2ll * acc2[i][j];
+                long long S = (in.SX[(int64_t)m * in.Np + n] + R) >> 2;     // exact: 4 | (SX + R)
+                const long long b1 = in.rowL1[m] * (long long)in.colMax[n];
+                const long long b2 = (long long)in.rowMax[m] * in.colL1[n];
+                const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
+                bool cl = false;
+                if (!safe) S = exact_output(in, m, n, cl);
+                const int sft = in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
+                bool over, under;
+                const int q = mx_pop(S, sft, in.u.F, in.w, over, under);
+                over |= cl;
+                in.out[(int64_t)m * in.N + n] = (int16_t)q;
+                if (in.flags)
+                    in.flags[(int64_t)m * in.N + n] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) |
+                                                                (under ? SFB_F_UNDERFLOW : 0u) |
+                                                                (cl ? SFB_F_ACC_CLIPPED : 0u));
+                cnt.over += over;
+                cnt.under += under;
+                cnt.clip += cl;
+            }
+        }
+    }
+    flush_counts(cnt, in.counts, sc);
+}
+
+// --- host side -------------------------------------------------------------------------------
+
+struct Layout {
+    int64_t Mp, Np, Kp, KW;
+    int64_t off_pa, off_pb, off_ba, off_bb, off_l1a, off_l1b, off_mxa, off_mxb, off_sx, total;
+};
+
+int64_t up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+Layout layout_for(int64_t M, int64_t N, int64_t K) {
+    Layout L;
+    L.Mp = up(M, TILE);
+    L.Np = up(N, TILE);
+    L.Kp = up(K, TILE);
+    L.KW = L.Kp / 32;
+    int64_t o = 0;
+    auto take = [&](int64_t bytes) {
+        const int64_t at = o;
+        o = up(o + bytes, 1024);
+        return at;
+    };
+    L.off_pa = take(NPLANES * L.Mp * L.Kp);
+    L.off_pb = take(NPLANES * L.Np * L.Kp);
+    L.off_ba = take(4 * 9 * L.KW * L.Mp);
+    L.off_bb = take(4 * 9 * L.KW * L.Np);
+    L.off_l1a = take(8 * L.Mp);
+    L.off_l1b = take(8 * L.Np);
+    L.off_mxa = take(4 * L.Mp);
+    L.off_mxb = take(4 * L.Np);
+    L.off_sx = take(8 * L.Mp * L.Np);
+    L.total = o + 1024;            // slack for aligning the caller's base
+    return L;
+}
+
+bool eligible(int bits, int mx, int64_t M, int64_t N, int64_t K) {
+    return mx == SFB_MX_V492 && bits >= 9 && bits <= 16 && K >= 1 && K <= KMAX && M >= 1 && N >= 1 &&
+           (double)M * (double)N * (double)K >= (double)(1 << 22) && up(M, TILE) <= (1 << 20) &&
+           up(N, TILE) <= (1 << 20);
+}
+
+typedef CUresult (*EncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static EncodeTiled fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+int make_map(CUtensorMap *map, void *base, int64_t rows_pad, int64_t Kp) {
+    EncodeTiled enc = encoder();
+    if (!enc) return set_error(SFB_ECUDA, "sfb_matmul_wide: cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows_pad, (cuuint64_t)NPLANES};
+    const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)(Kp * rows_pad)};
+    const cuuint32_t box[3] = {TILE, TILE, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(SFB_ECUDA, "sfb_matmul_wide: tensor map encoding failed (%d)", (int)r);
+    return SFB_OK;
+}
+
+}  // namespace
+
+int64_t wide_tc_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K) {
+    (void)batch;
+    if (!eligible(bits, mx, M, N, K)) return 0;
+    return layout_for(M, N, K).total;
+}
+
+int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
+                int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn, void *ws,
+                int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled) {
     *handled = false;
+    if (!eligible(bits, mx, M, N, K)) return SFB_OK;
+    const Layout L = layout_for(M, N, K);
+    if (ws == nullptr || ws_bytes < L.total)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide: workspace of %lld bytes is smaller than the %lld needed",
+                         (long long)ws_bytes, (long long)L.total);
+    if (counts == nullptr) return set_error(SFB_EINVAL, "sfb_matmul_wide: the tensor-core path needs counts");
+    static bool smem_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!smem_set[dev]) {
+        if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(wide_rem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * KC * 9 * RT * 4) != cudaSuccess)
+            return check_launch("sfb_matmul_wide (attributes)");
+        smem_set[dev] = true;
+    }
+    uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);
+    uint8_t *pa = base + L.off_pa, *pb = base + L.off_pb;
+    uint32_t *ba = reinterpret_cast<uint32_t *>(base + L.off_ba), *bb = reinterpret_cast<uint32_t *>(base + L.off_bb);
+    long long *l1a = reinterpret_cast<long long *>(base + L.off_l1a);
+    long long *l1b = reinterpret_cast<long long *>(base + L.off_l1b);
+    int *mxa = reinterpret_cast<int *>(base + L.off_mxa), *mxb = reinterpret_cast<int *>(base + L.off_mxb);
+    long long *SX = reinterpret_cast<long long *>(base + L.off_sx);
+    CUtensorMap tmA, tmB;
+    int rc = make_map(&tmA, pa, L.Mp, L.Kp);
+    if (rc) return rc;
+    rc = make_map(&tmB, pb, L.Np, L.Kp);
+    if (rc) return rc;
+    const Width w = width(bits);
+    for (int64_t z = 0; z < batch; z++) {
+        if (cudaMemsetAsync(base + L.off_l1a, 0, L.off_sx - L.off_l1a, st) != cudaSuccess)
+            return check_launch("sfb_matmul_wide (stats reset)");
+        prep_kernel<true><<<dim3((unsigned)(L.Mp / 128), (unsigned)L.KW), 128, 0, st>>>(
+            A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ba, l1a, mxa);
+        prep_kernel<false><<<dim3((unsigned)(L.Np / 128), (unsigned)L.KW), 128, 0, st>>>(
+            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, bb, l1b, mxb);
+        tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
+            tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
+        RemIn in;
+        in.bitsA = ba;
+        in.bitsB = bb;
+        in.SX = SX;
+        in.rowL1 = l1a;
+        in.colL1 = l1b;
+        in.rowMax = mxa;
+        in.colMax = mxb;
+        in.Mp = (int)L.Mp;
+        in.Np = (int)L.Np;
+        in.KW = (int)L.KW;
+        in.A = A + z * sa;
+        in.B = B + z * sb;
+        in.lda = lda;
+        in.ldb = ldb;
+        in.M = (int)M;
+        in.N = (int)N;
+        in.K = (int)K;
+        in.shift_arr = shift_arr ? shift_arr + z * ssb : nullptr;
+        in.shift = shift;
+        in.ssm = ssm;
+        in.ssn = ssn;
+        in.out = out + z * so;
+        in.flags = flags ? flags + z * so : nullptr;
+        in.w = w;
+        in.u = mx_unit(mx, true);
+        in.counts = counts;
+        wide_rem_kernel<<<dim3((unsigned)((N + RT - 1) / RT), (unsigned)((M + RT - 1) / RT)), 256,
+                          2 * KC * 9 * RT * 4, st>>>(in);
+        rc = check_launch("sfb_matmul_wide (tensor-core path)");
+        if (rc) return rc;
+    }
+    *handled = true;
     return SFB_OK;
 }
 

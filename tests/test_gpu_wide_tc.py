@@ -1,0 +1,99 @@
+"""The wide matmul's tensor-core path (tcgen05 int8 passes + bit-sliced
+remainder) against the oracle, bit for bit: ragged shapes, the SF16-block
+widths, shift arrays, batches, and outputs the clip bound does not prove safe
+(recomputed exactly on the CUDA cores)."""
+import numpy as np
+import pytest
+
+from oracle import native, sfref
+from superfloat.python_b200 import FORMATS, _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(gpu, bits, A, B, shift=0, flags=True):
+    import torch
+    o, cnt, fl = gpu.run_device("matmul_wide", FORMATS[bits], gpu.upload(A), gpu.upload(B), flags=flags,
+                                shift=shift)
+    c = cnt.cpu().numpy()
+    _lib.check_counts(c)
+    torch.cuda.synchronize()
+    return o.cpu().numpy(), c, (None if fl is None else fl.cpu().numpy())
+
+
+def _want(bits, A, B, shift):
+    return sfref.matmul_wide(bits, A, B, shift, acc_fn=native.wide_acc)
+
+
+def test_path_is_taken_for_large_problems(gpu):
+    assert _lib.wide_workspace(16, "v4.9.2", 1, 300, 260, 1000) > 0      # tensor-core path
+    assert _lib.wide_workspace(16, "v4.8.1", 1, 300, 260, 1000) == 0     # CUDA-core path
+    assert _lib.wide_workspace(8, "v4.9.2", 1, 300, 260, 1000) == 0      # SF8 block
+    assert _lib.wide_workspace(16, "v4.9.2", 1, 8, 8, 8) == 0            # too small to pay
+
+
+@pytest.mark.parametrize("bits", [16, 14, 12, 9])
+def test_ragged_random(gpu, bits):
+    rng = np.random.default_rng(bits)
+    M_ = (1 << (bits - 1)) - 1
+    for (M, N, K) in ((300, 260, 1000), (128, 128, 256), (129, 257, 130)):
+        A = rng.integers(-M_, M_ + 1, (M, K)) // rng.integers(1, 60)
+        B = rng.integers(-M_, M_ + 1, (K, N))
+        shift = int(rng.integers(-4, 5))
+        got, cnt, fl = _run(gpu, bits, A, B, shift)
+        want, ev = _want(bits, A, B, shift)
+        np.testing.assert_array_equal(got, want, err_msg=f"sf{bits} {M}x{N}x{K}")
+        np.testing.assert_array_equal((fl & 1) != 0, ev["overflow"])
+        np.testing.assert_array_equal((fl & 2) != 0, ev["underflow"])
+        assert int(cnt[0]) == int(ev["overflow"].sum()) and int(cnt[1]) == int(ev["underflow"].sum())
+
+
+def test_edge_codes_and_zero_rows(gpu):
+    rng = np.random.default_rng(7)
+    M, N, K = 200, 140, 600
+    A = rng.choice(np.array([0, 1, -1, 63, -64, 255, -256, 32767, -32767, 16384, 12345]), (M, K))
+    B = rng.choice(np.array([0, 1, -1, 64, -63, 256, -255, 32767, -32767, 8191]), (K, N))
+    A[5] = 0
+    B[:, 7] = 0
+    A = A // 64                                  # keep most outputs below the clip bound
+    got, _, _ = _run(gpu, 16, A, B, -3)
+    want, _ = _want(16, A, B, -3)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_shift_arrays(gpu):
+    rng = np.random.default_rng(11)
+    M, N, K = 256, 192, 512
+    A = rng.integers(-4000, 4001, (M, K))
+    B = rng.integers(-32767, 32768, (K, N))
+    for sh in (rng.integers(-8, 4, (M, 1)), rng.integers(-8, 4, (N,)), rng.integers(-32, 32, (M, N))):
+        got, _, _ = _run(gpu, 16, A, B, sh)
+        want, _ = _want(16, A, B, sh)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_outputs_beyond_the_clip_bound_are_exact(gpu):
+    """Full-range codes with K = 4096 are not proven clip-free: recomputed
+    exactly on the CUDA cores; same-sign operands clip for real."""
+    rng = np.random.default_rng(5)
+    M, N, K = 128, 128, 4096
+    A = rng.integers(-32767, 32768, (M, K))
+    B = rng.integers(-32767, 32768, (K, N))
+    A[:4] = np.abs(A[:4])
+    B[:, :4] = np.abs(B[:, :4])
+    got, cnt, fl = _run(gpu, 16, A, B, -12)
+    want, ev = _want(16, A, B, -12)
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal((fl & 1) != 0, ev["overflow"])
+    acc, clip, _ = native.wide_acc(16, A, B)
+    np.testing.assert_array_equal((fl & 16) != 0, clip)
+    assert clip[:4, :4].all() and int(cnt[4]) == int(clip.sum())
+
+
+def test_batched(gpu):
+    rng = np.random.default_rng(9)
+    A = rng.integers(-2000, 2001, (3, 130, 300))
+    B = rng.integers(-32767, 32768, (300, 140))
+    got, _, _ = _run(gpu, 16, A, B, -1)
+    want, _ = _want(16, A.reshape(-1, 300), B, -1)
+    np.testing.assert_array_equal(got.reshape(-1, 140), want)
