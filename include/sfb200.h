@@ -131,6 +131,25 @@ SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B
                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
                     void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
 
+/* sfb_matmul_wide without any device allocation, for callers that cannot
+ * allocate device memory while they run: a host program that has handed all
+ * of the GPU's memory to its own pool, a plugin host that forbids allocation
+ * after start-up, or a loop that cannot afford the device-wide synchronisation
+ * cudaMalloc / cudaFree can imply.  It has no counterpart in the reference.
+ * The same arguments and results as sfb_matmul_wide, minus the workspace: the
+ * scratch is a fixed 64 MiB array inside the library, held on every GPU that
+ * loads the library until the process exits.  The first call on a device
+ * looks up that array's address (with that device current).  Problems whose
+ * scratch exceeds 64 MiB (sfb_matmul_wide_workspace() > 64 MiB: 1536^3 fits, 2048^3
+ * needs about 105 MiB) are refused with SFB_ERANGE.  All calls share the one
+ * array, so calls whose kernels overlap on the GPU (other streams or host
+ * threads) race; serialise them. */
+SFB_API int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr,
+                                    int shift, int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N,
+                                    int64_t K, int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b,
+                                    int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
+                                    sfb_counts *counts, sfb_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,8 @@ SIGNATURES = {
     "sfb_matmul_wide_workspace": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64]),
     "sfb_matmul_wide": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                       _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
 }
 
 _lib = None

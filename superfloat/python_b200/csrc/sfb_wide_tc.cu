@@ -35,6 +35,8 @@
 // after freeing its TMEM.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "sfb_wide_simt.cuh"
 
 namespace sfb {
@@ -622,3 +624,61 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
 }
 
 }  // namespace sfb
+
+// --- the wide matmul without any device allocation ------------------------------------------
+//
+// For callers that cannot allocate device memory on their hot path: a host
+// program that has handed all of the GPU's memory to its own pool, a plugin
+// host that forbids allocations once it has started, or a loop that cannot
+// afford the device-wide synchronisation cudaMalloc / cudaFree can imply.
+// The tensor-core path's scratch (operand planes, remainder bit planes, row /
+// column statistics, partial sums) lives in the fixed array below instead of
+// a caller workspace.  Every GPU that loads this library holds the array until
+// the process exits.  The array keeps the previous call's contents; the path
+// clears what must start at zero (the row / column statistics) and overwrites
+// everything else.  Calls share the one array, so two calls whose kernels
+// overlap on the GPU (different streams, or different host threads) race.
+
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 64ll << 20;   // 64 MiB per device
+
+static __device__ __align__(256) unsigned char g_wide_scratch[kNoAllocScratchBytes];
+
+}  // namespace
+
+extern "C" int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const int16_t *B,
+                                       const int8_t *shift_arr, int shift, int16_t *out, uint8_t *flags,
+                                       int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                       int64_t stride_a, int64_t stride_b, int64_t stride_out, int64_t shift_sb,
+                                       int64_t shift_sm, int64_t shift_sn, sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    // the array's device address, looked up once per device with that device current
+    static void *scratch[64] = {};
+    static std::mutex lock;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return set_error(SFB_ECUDA, "sfb_matmul_wide_noalloc: no current CUDA device");
+    void *ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> g(lock);
+        if (scratch[dev] == nullptr) {
+            const cudaError_t e = cudaGetSymbolAddress(&scratch[dev], g_wide_scratch);
+            if (e != cudaSuccess) {
+                scratch[dev] = nullptr;
+                return set_error(SFB_ECUDA, "sfb_matmul_wide_noalloc: scratch lookup failed: %s", cudaGetErrorString(e));
+            }
+        }
+        ptr = scratch[dev];
+    }
+    const int64_t need = sfb_matmul_wide_workspace(bits, mx, batch, M, N, K);
+    if (need < 0) return (int)need;
+    if (need > kNoAllocScratchBytes)
+        return set_error(SFB_ERANGE,
+                         "sfb_matmul_wide_noalloc: %lld x %lld x %lld needs %lld bytes of scratch, more than the "
+                         "%lld this entry point holds; use sfb_matmul_wide with a workspace",
+                         (long long)M, (long long)N, (long long)K, (long long)need, (long long)kNoAllocScratchBytes);
+    return sfb_matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a,
+                           stride_b, stride_out, shift_sb, shift_sm, shift_sn, ptr, kNoAllocScratchBytes, counts,
+                           stream);
+}
