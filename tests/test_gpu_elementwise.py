@@ -150,3 +150,31 @@ def test_workload_full_size_2_26(gpu):
                 assert int(cnt[i]) == int(np.count_nonzero(evf.get(e, False))), (op, e)
         assert int((fl != 0).sum()) <= n
     torch.cuda.synchronize()
+
+
+def test_host_pipeline_and_plugin_contract(gpu, rng):
+    """Host-resident codes through the chunked two-stream pipeline, and the
+    int64 Device.run contract built on it, equal the oracle."""
+    import torch
+    from superfloat.python_b200._hostpath import HostPipeline, plugin_run
+    pipe = HostPipeline(gpu, chunk=1 << 12)
+    n = 3 * (1 << 12) + 77
+    for op in ("add", "mul", "div", "fma", "sqrt"):
+        xs = [edge_codes(16, n, rng) for _ in range(ARITY[op])]
+        hs = []
+        for v in xs:
+            t = torch.empty(n, dtype=torch.int16, pin_memory=True)
+            t.copy_(torch.from_numpy(v))
+            hs.append(t)
+        out = torch.empty(n, dtype=torch.int16, pin_memory=True)
+        fl = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+        counts = pipe.run(op, FORMATS[16], *hs, out=out, flags_out=fl)
+        want, ev = sfref.ew(op, 16, *xs)
+        np.testing.assert_array_equal(out.numpy(), want)
+        for i, e in enumerate(("overflow", "underflow", "divide", "invalid")):
+            assert int(counts[i]) == int(np.count_nonzero(ev.get(e, False))), (op, e)
+        codes, masks, _ = plugin_run(gpu, pipe, op, FORMATS[16], *xs)
+        np.testing.assert_array_equal(codes, want)
+        assert set(masks) == set(ev)
+        for e, m in ev.items():
+            np.testing.assert_array_equal(masks[e], m)
