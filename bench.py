@@ -183,6 +183,8 @@ def main():
     ap.add_argument("--no-matmul", action="store_true")
     ap.add_argument("--matmul-only", type=int, default=0, metavar="SIZE",
                     help="time only the wide and chain matmuls, wide at SIZE^3 (a small case for profiling)")
+    ap.add_argument("--gpt2-only", type=int, default=0, metavar="TOKENS",
+                    help="time only the converted GPT-2-small forward on 8 x TOKENS ids")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
@@ -195,6 +197,9 @@ def main():
     torch.cuda.set_device(local)
     if args.matmul_only:
         print(json.dumps(bench_matmuls(B200Device(local), FORMATS[16], torch, args.matmul_only)), flush=True)
+        return 0
+    if args.gpt2_only:
+        print(json.dumps(bench_gpt2(torch, seq=args.gpt2_only)), flush=True)
         return 0
     if world > 1:
         from datetime import timedelta
@@ -338,6 +343,7 @@ def main():
     # the matmuls beside it (rank 0 only, N = 1): not part of `value`
     if rank == 0 and world == 1 and not args.no_matmul:
         line["matmul"] = bench_matmuls(dev, fmt, torch)
+        line["matmul"]["gpt2_small_convert"] = bench_gpt2(torch)
 
     if world > 1:
         dist.barrier()
@@ -386,6 +392,36 @@ def bench_matmuls(dev, fmt, torch, n=8192):
     ms = e0.elapsed_time(e1) / reps
     res["chain_512"] = {"ms": ms, "TOPS": 2 * 512 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
     return res
+
+
+def bench_gpt2(torch, batch=8, seq=512, reps=3):
+    """sft.convert(dtype=sf16) GPT-2-small (12 layers, d_model 768, 12 heads,
+    FFN 3072, vocab 50257; random init, seed 0) forward on batch x seq token
+    ids, on the GPU; 49 SF layers (chain accumulation, headroom "bound")."""
+    import warnings
+    from transformers import GPT2Config, GPT2LMHeadModel
+    import superfloat.python_b200.torch as sft
+    torch.manual_seed(0)
+    cfg = GPT2Config(n_layer=12, n_embd=768, n_head=12, n_inner=3072, vocab_size=50257, n_positions=1024)
+    model = sft.convert(GPT2LMHeadModel(cfg).eval(), dtype="sf16").cuda()
+    ids = torch.randint(0, 50257, (batch, seq), generator=torch.Generator().manual_seed(0)).cuda()
+    with torch.no_grad(), warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        model(ids)                                        # prepares the weights (cached per weight)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            model(ids)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    R = batch * seq
+    products = R * (768 * 2304 + 768 * 768 + 768 * 3072 + 3072 * 768) * 12 + R * 768 * 50257
+    st = sft.last_status(model)
+    return {"ms_per_forward": ms, "tokens_per_s": R / (ms / 1e3), "sf_layers": len(st),
+            "sf16_TOPS": 2 * products / (ms / 1e3) / 1e12, "saturated": sum(v.saturated or 0 for v in st.values()),
+            "workload": f"GPT-2-small sft.convert(sf16) forward, {batch} x {seq} tokens, float parts on the GPU"}
 
 
 if __name__ == "__main__":

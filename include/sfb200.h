@@ -111,6 +111,22 @@ SFB_API int sfb_matmul_chain(int bits, const int16_t *A, const int16_t *B, const
                      int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_out,
                      sfb_counts *counts, sfb_stream stream);
 
+/* The chain matmul of a converted linear layer, fused with its bias add and
+ * its float64 dequantization: acc = X (R x K codes) @ WT (K x N codes) as in
+ * sfb_matmul_chain, one saturating add of bias[n] (NULL: none), then
+ * y = acc / 2^(N-1) * a * s_col[n] in float64, written as float32 (y32) and/or
+ * float64 (y64); codes / flags optional.  Replaces the matmul, the add and the
+ * dequantization of the reference's chain linear (src/sf/torch/_core.py:374-382).
+ * proven_no_saturation: the caller has shown (the reference's L1 bound,
+ * src/sf/_linalg.py:84-106) that no partial sum can reach +-max; the chain is
+ * then summed without per-step clips.  If that proof is wrong the outputs are
+ * not the reference's and counts->reserved[1] counts the outputs found out of
+ * range. */
+SFB_API int sfb_linear_chain(int bits, const int16_t *X, const int16_t *WT, const int16_t *bias, double a,
+                             const double *s_col, int proven_no_saturation, float *y32, double *y64, int16_t *codes,
+                             uint8_t *flags, int64_t R, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                             sfb_counts *counts, sfb_stream stream);
+
 /* Bytes of device workspace sfb_matmul_wide needs for this problem (0 when
  * it needs none); negative on a bad argument. */
 SFB_API int64_t sfb_matmul_wide_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K);

@@ -33,6 +33,8 @@ SIGNATURES = {
     "sfb_elementwise": (_i32, [_i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _p, _p]),
     "sfb_matmul_chain": (_i32, [_i32, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                 _i64, _p, _p]),
+    "sfb_linear_chain": (_i32, [_i32, _p, _p, _p, ctypes.c_double, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64,
+                                _i64, _i64, _p, _p]),
     "sfb_matmul_wide_workspace": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64]),
     "sfb_matmul_wide": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
@@ -84,6 +86,9 @@ def check_counts(counts) -> None:
     if int(counts[5]) != 0:
         raise SFDeviceError(f"a libsfb200 kernel gave up waiting on the device ({int(counts[5])} CTA(s)); "
                             "the outputs of that call are not valid")
+    if int(counts[6]) != 0:
+        raise SFDeviceError(f"{int(counts[6])} output(s) of a chain summed without clips left the range: the "
+                            "no-saturation proof passed in was wrong")
 
 
 def ensure_device(index: int) -> None:
@@ -115,6 +120,14 @@ def matmul_chain(bits, A, B, bias, out, flags, counts, batch, M, N, K, lda, ldb,
     rc = load().sfb_matmul_chain(bits, _ptr(A), _ptr(B), _ptr(bias), _ptr(out), _ptr(flags), batch, M, N, K,
                                  lda, ldb, sa, sb, so, _ptr(counts), _stream(stream))
     check(rc, "sf matmul (chain)")
+
+
+def linear_chain(bits, X, WT, bias, a, s_col, proven, y32, y64, codes, flags, counts, R, N, K, ldx, ldw,
+                 stream=None):
+    rc = load().sfb_linear_chain(bits, _ptr(X), _ptr(WT), _ptr(bias), float(a), _ptr(s_col), int(bool(proven)),
+                                 _ptr(y32), _ptr(y64), _ptr(codes), _ptr(flags), R, N, K, ldx, ldw, _ptr(counts),
+                                 _stream(stream))
+    check(rc, "sf linear (chain)")
 
 
 def wide_workspace(bits, mx, batch, M, N, K) -> int:

@@ -28,7 +28,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .. import _config, _errstate
+from .. import _config, _errstate, _lib
 from .._device import get_device
 from .._format import FORMATS, SFFormat
 
@@ -219,15 +219,19 @@ def _bound(fmt, kx: torch.Tensor, b_max_abs: int, b_max_col_l1: int) -> int:
     return min(row_l1 * b_max_abs, mx * b_max_col_l1) // fmt.scale
 
 
-def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_over_scale, headroom: str):
+def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_over_scale, headroom: str,
+               with_proof: bool = False):
     """The activation scale search (src/sf/torch/_core.py:306-331).
-    Returns (codes, events, a, a0)."""
+    Returns (codes, events, a, a0), plus with ``with_proof`` whether the L1
+    bound proved that no chain step can saturate."""
     m = fmt.max_code / fmt.scale
     amax = finite_absmax(x)
     a0 = amax / m if amax > 0 else 1.0
     a = a0
     kx, ev = cast(fmt, x / a)
     if headroom == "none":
+        if with_proof:
+            return kx, ev, a, a0, _bound(fmt, kx, b_max_abs, b_max_col_l1) <= fmt.max_code
         return kx, ev, a, a0
     a_bias = bias_over_scale(None)
     if a_bias is not None and math.isfinite(a_bias) and a_bias > a:
@@ -236,9 +240,10 @@ def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_ove
     for _ in range(_MAX_ITER):
         ratio = bias_over_scale(a)
         bias_codes = int(math.ceil(ratio)) if ratio is not None and math.isfinite(ratio) else 0
-        bound = _bound(fmt, kx, b_max_abs, b_max_col_l1) + bias_codes
+        chain = _bound(fmt, kx, b_max_abs, b_max_col_l1)
+        bound = chain + bias_codes
         if bound <= fmt.max_code:
-            return kx, ev, a, a0
+            return (kx, ev, a, a0, chain <= fmt.max_code) if with_proof else (kx, ev, a, a0)
         a *= max(bound / fmt.max_code, 1.0 + 2.0 ** -20)
         kx, ev = cast(fmt, x / a)
     raise RuntimeError("sf: headroom search did not converge")
@@ -247,9 +252,10 @@ def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_ove
 # --- linear ----------------------------------------------------------------------------------
 
 def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_tensor",
-           headroom: str = "bound", dev=None) -> CoreResult:
+           headroom: str = "bound", dev=None, out_dtype=torch.float32) -> CoreResult:
     """x: (R, K), w: (N, K), b: (N,) or None, any float dtype, any device;
-    the result ``y`` is float64 on the target's CUDA device."""
+    the result ``y`` (float32, or float64 when ``out_dtype`` is) is on the
+    target's CUDA device, rounded once from the float64 dequantization."""
     fmt = check_args(bits, wscale, headroom)
     dev = dev or target()
     cuda = dev.torch_device
@@ -272,19 +278,26 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
         def bias_over_scale(a):
             return None if a is None else 0.0
 
-    kx, ev_x, a, a0 = activation(fmt, x, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom)
+    kx, ev_x, a, a0, proven = activation(fmt, x, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom,
+                                         with_proof=True)
     bias_sat = 0
     kb = None
     if b is not None:
         kb, ev_b = cast(fmt, b / (a * pw.s_w))
         bias_sat = int(ev_b["overflow"])
-    acc, cnt, _ = dev.run_device("matmul", fmt, kx, pw.kwT, bias=kb)
-    c = cnt.cpu()
-    y = acc.to(torch.float64) / S * a * pw.s_w[None, :]
+    R, K = kx.shape
+    N = pw.kwT.shape[1]
+    y = torch.empty(R, N, dtype=torch.float64 if out_dtype == torch.float64 else torch.float32, device=cuda)
+    cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=cuda)
+    _lib.linear_chain(fmt.bits, kx, pw.kwT, kb, a, pw.s_w, proven,
+                      y if y.dtype == torch.float32 else None, y if y.dtype == torch.float64 else None,
+                      None, None, cnt, R, N, K, K, N)
+    c = cnt.cpu().numpy()
+    _lib.check_counts(c)
     return CoreResult(y=y, saturated=int(c[0]), exact=True, underflow=int(c[1]),
                       input_underflow=int(ev_x["underflow"]), weight_underflow=pw.w_under,
                       bias_saturated=bias_sat, headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
-                      outputs=int(acc.numel()), act_scale=a)
+                      outputs=R * N, act_scale=a)
 
 
 def matmul(a_val: torch.Tensor, b_val: torch.Tensor, bits: int, headroom: str = "bound", dev=None) -> CoreResult:

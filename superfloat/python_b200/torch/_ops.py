@@ -51,9 +51,10 @@ def linear_impl(x, weight, bias, bits, wscale, headroom, name):
         raise ValueError(f"sf.linear: input has {x.shape[-1]} features, weight expects {K}")
     dev = _core.target()
     lead = x.shape[:-1]
-    r = _core.linear(x.reshape(-1, K), weight, bias, bits, wscale, headroom, dev)
+    od = out_dtype(x.dtype)
+    r = _core.linear(x.reshape(-1, K), weight, bias, bits, wscale, headroom, dev, out_dtype=od)
     _record(name, "linear", dev.name, bits, r)
-    return r.y.reshape(*lead, N).to(device=x.device, dtype=out_dtype(x.dtype))
+    return r.y.reshape(*lead, N).to(device=x.device, dtype=od)
 
 
 def matmul_impl(a, b, bits, headroom, name):
