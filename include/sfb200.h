@@ -76,6 +76,21 @@ typedef struct sfb_counts {
 
 typedef void *sfb_stream; /* a cudaStream_t */
 
+/* float element types of sfb_scan / sfb_quantize */
+#define SFB_F32 0
+#define SFB_F64 1
+
+/* Statistics of a float tensor and of its quantization (device memory; the
+ * caller zeroes it): scan -> nan_count, inf_count, absmax (largest finite |x|);
+ * quantize -> overflow / underflow / invalid counts of the cast, the largest
+ * row L1 norm of the codes and the largest |code|. */
+typedef struct sfb_qstats {
+    unsigned long long nan_count, inf_count;
+    double absmax;
+    unsigned long long overflow, underflow, invalid;
+    long long max_row_l1, max_abs_code;
+} sfb_qstats;
+
 /* Library and device. */
 SFB_API int sfb_abi_version(void);
 SFB_API const char *sfb_last_error(void);
@@ -126,6 +141,20 @@ SFB_API int sfb_linear_chain(int bits, const int16_t *X, const int16_t *WT, cons
                              const double *s_col, int proven_no_saturation, float *y32, double *y64, int16_t *codes,
                              uint8_t *flags, int64_t R, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
                              sfb_counts *counts, sfb_stream stream);
+
+/* One pass over n floats (dtype SFB_F32 / SFB_F64): NaN and +-inf counts and
+ * the largest finite magnitude, the inputs of the reference's sanitize /
+ * finite_absmax (src/sf/torch/_core.py:200-236). */
+SFB_API int sfb_scan(const void *x, int dtype, int64_t n, sfb_qstats *stats, sfb_stream stream);
+
+/* codes[r, c] = cast(x[r, c] / s_r) for a rows x cols matrix (row stride ld,
+ * codes row stride ldc), s_r = row_scale[r] or the scalar `scale` when
+ * row_scale is NULL: the reference's cast of float64 values
+ * (src/sf/_vectorized.py:32-71; float32 inputs widen exactly) with its
+ * event counts, plus the largest row L1 norm and |code| of the result. */
+SFB_API int sfb_quantize(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, double scale,
+                         const double *row_scale, int bits, int16_t *codes, int64_t ldc, sfb_qstats *stats,
+                         sfb_stream stream);
 
 /* Bytes of device workspace sfb_matmul_wide needs for this problem (0 when
  * it needs none); negative on a bad argument. */

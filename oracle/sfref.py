@@ -132,6 +132,23 @@ def ew(op: str, bits: int, *operands, **kw):
 
 # --- chain accumulation (src/sf/_linalg.py:30-111) -----------------------------------------
 
+def cast_float(bits, values, scale=1.0):
+    """float -> codes of ``values / scale`` (scale a number or a per-row
+    column vector), src/sf/_vectorized.py:59-71: NaN -> 0 (invalid),
+    |v| >= 1 - 2^-N -> +-M (overflow, inf included), else round half to
+    even of v 2^(N-1), underflow where a nonzero value rounds to 0."""
+    M, S = consts(bits)
+    v = np.asarray(values).astype(np.float64) / np.asarray(scale, dtype=np.float64)
+    nan = np.isnan(v)
+    over = (np.abs(v) >= 1.0 - 2.0 ** -bits) & ~nan
+    fits = ~over & ~nan
+    k = np.zeros(v.shape, dtype=np.int64)
+    k[fits] = np.rint(v[fits] * S).astype(np.int64)
+    k[over] = np.sign(v[over]).astype(np.int64) * M
+    under = fits & (k == 0) & (v != 0)
+    return k, {"overflow": over, "underflow": under, "invalid": nan}
+
+
 def sum_chain(bits, a, axis=0):
     """Sequential saturating sum from index 0 (_linalg.py:30-40)."""
     a = np.moveaxis(_i64(a), axis, 0)

@@ -35,6 +35,8 @@ SIGNATURES = {
                                 _i64, _p, _p]),
     "sfb_linear_chain": (_i32, [_i32, _p, _p, _p, ctypes.c_double, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64,
                                 _i64, _i64, _p, _p]),
+    "sfb_scan": (_i32, [_p, _i32, _i64, _p, _p]),
+    "sfb_quantize": (_i32, [_p, _i32, _i64, _i64, _i64, ctypes.c_double, _p, _i32, _p, _i64, _p, _p]),
     "sfb_matmul_wide_workspace": (_i64, [_i32, _i32, _i64, _i64, _i64, _i64]),
     "sfb_matmul_wide": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
@@ -128,6 +130,37 @@ def linear_chain(bits, X, WT, bias, a, s_col, proven, y32, y64, codes, flags, co
                                  _ptr(y32), _ptr(y64), _ptr(codes), _ptr(flags), R, N, K, ldx, ldw, _ptr(counts),
                                  _stream(stream))
     check(rc, "sf linear (chain)")
+
+
+QSTATS_WORDS = 8                   # sfb_qstats: 8 x 64-bit fields
+_FDT = {"float32": 0, "float64": 1}
+
+
+def _fdtype(t):
+    name = str(t.dtype).split(".")[-1]
+    if name not in _FDT:
+        raise TypeError(f"expected a float32 or float64 tensor, got {t.dtype}")
+    return _FDT[name]
+
+
+def scan(x, stats, stream=None):
+    rc = load().sfb_scan(_ptr(x), _fdtype(x), x.numel(), _ptr(stats), _stream(stream))
+    check(rc, "sf scan")
+
+
+def quantize(x, rows, cols, ld, scale, row_scale, bits, codes, ldc, stats, stream=None):
+    rc = load().sfb_quantize(_ptr(x), _fdtype(x), rows, cols, ld, float(scale), _ptr(row_scale), bits, _ptr(codes),
+                             ldc, _ptr(stats), _stream(stream))
+    check(rc, "sf quantize")
+
+
+def qstats_view(t):
+    """Host view of one sfb_qstats held in an int64[8] tensor already on the host."""
+    import numpy as np
+    raw = t.numpy()
+    return {"nan": int(raw[0]), "inf": int(raw[1]), "absmax": float(raw[2:3].view(np.float64)[0]),
+            "overflow": int(raw[3]), "underflow": int(raw[4]), "invalid": int(raw[5]),
+            "max_row_l1": int(raw[6]), "max_abs": int(raw[7])}
 
 
 def wide_workspace(bits, mx, batch, M, N, K) -> int:

@@ -26,6 +26,7 @@ import weakref
 from collections import OrderedDict
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from .. import _config, _errstate, _lib
@@ -151,16 +152,21 @@ class PreparedWeight:
     max_col_l1: int       # max_n sum_k |W_code[n, k]|
 
 
+def _stats_buf(dev, n=1):
+    return torch.zeros(n, _lib.QSTATS_WORDS, dtype=torch.int64, device=dev)
+
+
 def prepare_weight(fmt: SFFormat, w: torch.Tensor, wscale: str) -> PreparedWeight:
+    """W_code = cast(W / s_w) per output row, with the statistics the bound
+    needs (one fused pass, sfb_quantize)."""
     s = weight_scales(fmt, w, wscale)
-    codes, ev = cast(fmt, w / s[:, None])
-    kwT = codes.t().contiguous()
-    if codes.numel():
-        stats = torch.stack([codes.abs().max().to(torch.int64), codes.abs().to(torch.int64).sum(1).max()]).cpu()
-        mx, l1 = int(stats[0]), int(stats[1])
-    else:
-        mx = l1 = 0
-    return PreparedWeight(kwT, s, int(ev["underflow"]), mx, l1)
+    N, K = w.shape
+    codes = torch.empty(N, K, dtype=torch.int16, device=w.device)
+    st = _stats_buf(w.device)
+    if w.numel():
+        _lib.quantize(w.contiguous(), N, K, K, 1.0, s.contiguous(), fmt.bits, codes, K, st[0])
+    q = _lib.qstats_view(st[0].cpu())
+    return PreparedWeight(codes.t().contiguous(), s, q["underflow"], q["max_abs"], q["max_row_l1"])
 
 
 class WeightCache:
@@ -208,45 +214,68 @@ weight_cache = WeightCache()
 
 # --- the activation scale ------------------------------------------------------------------
 
-def _bound(fmt, kx: torch.Tensor, b_max_abs: int, b_max_col_l1: int) -> int:
-    """The reference's L1 bound (src/sf/_linalg.py:84-106), with the right
-    operand's statistics precomputed."""
-    if kx.numel() == 0 or kx.shape[-1] == 0:
-        return 0
-    ax = kx.abs().to(torch.int64)
-    st = torch.stack([ax.sum(-1).max(), ax.max()]).cpu()
-    row_l1, mx = int(st[0]), int(st[1])
-    return min(row_l1 * b_max_abs, mx * b_max_col_l1) // fmt.scale
+class _Quantized:
+    """Codes of x / a from one sfb_quantize pass, with the cast's underflow
+    count and the L1 statistics (the events dict of ``cast``)."""
+
+    def __init__(self, fmt, x2d: torch.Tensor, a: float):
+        R, K = x2d.shape
+        self.codes = torch.empty(R, K, dtype=torch.int16, device=x2d.device)
+        st = _stats_buf(x2d.device)
+        _lib.quantize(x2d, R, K, x2d.stride(0), a, None, fmt.bits, self.codes, K, st[0])
+        q = _lib.qstats_view(st[0].cpu())
+        self.events = {"overflow": q["overflow"], "underflow": q["underflow"], "invalid": q["invalid"]}
+        self.row_l1, self.max_abs = q["max_row_l1"], q["max_abs"]
+
+    def bound(self, fmt, b_max_abs, b_max_col_l1) -> int:
+        if self.codes.numel() == 0:
+            return 0
+        return min(self.row_l1 * b_max_abs, self.max_abs * b_max_col_l1) // fmt.scale
 
 
-def activation(fmt, x: torch.Tensor, b_max_abs: int, b_max_col_l1: int, bias_over_scale, headroom: str,
-               with_proof: bool = False):
-    """The activation scale search (src/sf/torch/_core.py:306-331).
-    Returns (codes, events, a, a0), plus with ``with_proof`` whether the L1
-    bound proved that no chain step can saturate."""
+def activation_fused(fmt, x2d: torch.Tensor, amax: float, b_max_abs: int, b_max_col_l1: int, bias_over_scale,
+                     headroom: str):
+    """The activation scale search (src/sf/torch/_core.py:306-331) on a
+    float32 / float64 (R, K) device tensor, each cast one sfb_quantize pass.
+    Returns (codes, events, a, a0, proven): ``proven`` when the L1 bound shows
+    that no chain step can saturate."""
     m = fmt.max_code / fmt.scale
-    amax = finite_absmax(x)
     a0 = amax / m if amax > 0 else 1.0
     a = a0
-    kx, ev = cast(fmt, x / a)
+    q = _Quantized(fmt, x2d, a)
     if headroom == "none":
-        if with_proof:
-            return kx, ev, a, a0, _bound(fmt, kx, b_max_abs, b_max_col_l1) <= fmt.max_code
-        return kx, ev, a, a0
+        return q.codes, q.events, a, a0, q.bound(fmt, b_max_abs, b_max_col_l1) <= fmt.max_code
     a_bias = bias_over_scale(None)
     if a_bias is not None and math.isfinite(a_bias) and a_bias > a:
         a = a_bias
-        kx, ev = cast(fmt, x / a)
+        q = _Quantized(fmt, x2d, a)
     for _ in range(_MAX_ITER):
         ratio = bias_over_scale(a)
         bias_codes = int(math.ceil(ratio)) if ratio is not None and math.isfinite(ratio) else 0
-        chain = _bound(fmt, kx, b_max_abs, b_max_col_l1)
+        chain = q.bound(fmt, b_max_abs, b_max_col_l1)
         bound = chain + bias_codes
         if bound <= fmt.max_code:
-            return (kx, ev, a, a0, chain <= fmt.max_code) if with_proof else (kx, ev, a, a0)
+            return q.codes, q.events, a, a0, chain <= fmt.max_code
         a *= max(bound / fmt.max_code, 1.0 + 2.0 ** -20)
-        kx, ev = cast(fmt, x / a)
+        q = _Quantized(fmt, x2d, a)
     raise RuntimeError("sf: headroom search did not converge")
+
+
+def _scanned(x: torch.Tensor, cuda, fmt, what: str):
+    """x on the device as contiguous float32 / float64, with its finite
+    max |x|: one sfb_scan pass; the error policy (``sanitize``) runs only when
+    the scan found a NaN or an inf."""
+    x = x.detach().to(device=cuda)
+    if x.dtype not in (torch.float32, torch.float64):
+        x = x.to(torch.float32)                            # float16 / bfloat16 widen exactly
+    x = x.contiguous()
+    st = _stats_buf(cuda)
+    _lib.scan(x, st[0])
+    sc = _lib.qstats_view(st[0].cpu())
+    if sc["nan"] or sc["inf"]:
+        x = sanitize(x.to(torch.float64), fmt, what)
+        return x, finite_absmax(x)
+    return x, sc["absmax"]
 
 
 # --- linear ----------------------------------------------------------------------------------
@@ -260,32 +289,31 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
     dev = dev or target()
     cuda = dev.torch_device
     S, M = fmt.scale, fmt.max_code
-    x = sanitize(x.detach().to(device=cuda, dtype=torch.float64), fmt, "linear input")
+    x, amax = _scanned(x, cuda, fmt, "linear input")
     pw = weight_cache.get(fmt, w, wscale, cuda)
     if b is not None:
         b = sanitize(b.detach().to(device=cuda, dtype=torch.float64), fmt, "linear bias")
     if b is not None and b.numel():
-        need = b.abs() / pw.s_w                                     # may hold inf
-        fin = torch.isfinite(need)
-        a_bias = float(torch.where(fin, need, torch.zeros((), dtype=need.dtype, device=cuda)).max()) / (M / S) \
-            if bool(fin.any()) else 0.0
+        need = (b.abs() / pw.s_w).cpu().numpy()            # may hold inf; host float64, as the reference
+        fin = np.isfinite(need)
+        a_bias = float(need[fin].max()) / (M / S) if fin.any() else 0.0
 
         def bias_over_scale(a):
             if a is None:
                 return a_bias
-            return float((need / a).max() * S)
+            with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+                return float((need / a).max() * S)
     else:
         def bias_over_scale(a):
             return None if a is None else 0.0
 
-    kx, ev_x, a, a0, proven = activation(fmt, x, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom,
-                                         with_proof=True)
+    R, K = x.shape
+    kx, ev_x, a, a0, proven = activation_fused(fmt, x, amax, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom)
     bias_sat = 0
     kb = None
     if b is not None:
         kb, ev_b = cast(fmt, b / (a * pw.s_w))
         bias_sat = int(ev_b["overflow"])
-    R, K = kx.shape
     N = pw.kwT.shape[1]
     y = torch.empty(R, N, dtype=torch.float64 if out_dtype == torch.float64 else torch.float32, device=cuda)
     cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=cuda)
@@ -308,7 +336,7 @@ def matmul(a_val: torch.Tensor, b_val: torch.Tensor, bits: int, headroom: str = 
     cuda = dev.torch_device
     S, M = fmt.scale, fmt.max_code
     m = M / S
-    a_val = sanitize(a_val.detach().to(device=cuda, dtype=torch.float64), fmt, "matmul left operand")
+    a_val, _amax = _scanned(a_val, cuda, fmt, "matmul left operand")
     b_val = sanitize(b_val.detach().to(device=cuda, dtype=torch.float64), fmt, "matmul right operand")
     bmax = finite_absmax(b_val)
     s_b = bmax / m if bmax > 0 else 1.0
@@ -319,7 +347,10 @@ def matmul(a_val: torch.Tensor, b_val: torch.Tensor, bits: int, headroom: str = 
         b_max, b_l1 = int(st[0]), int(st[1])
     else:
         b_max = b_l1 = 0
-    ka, ev_a, a, a0 = activation(fmt, a_val, b_max, b_l1, lambda _a: None if _a is None else 0.0, headroom)
+    K = a_val.shape[-1]
+    ka, ev_a, a, a0, _ = activation_fused(fmt, a_val.reshape(-1, K), _amax, b_max, b_l1,
+                                          lambda _a: None if _a is None else 0.0, headroom)
+    ka = ka.reshape(a_val.shape)
     acc, cnt, _ = dev.run_device("matmul", fmt, ka, kb)
     c = cnt.cpu()
     y = acc.to(torch.float64) / S * a * s_b

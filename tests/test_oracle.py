@@ -38,6 +38,15 @@ def test_elementwise_golden_vectors():
         assert _event_of(ev) == c["event"], c
 
 
+def test_float_cast_reference_run():
+    for c in golden("ref_runs.json")["cast"]:
+        vals = np.array([float(v) for v in c["values"]])
+        k, ev = sfref.cast_float(c["bits"], vals)
+        assert k.tolist() == c["codes"]
+        for e in ("overflow", "underflow", "invalid"):
+            assert ev[e].astype(int).tolist() == c[e], (c["bits"], e)
+
+
 def test_chain_golden_vectors():
     for c in CHAIN:
         if c["op"] == "dot":
