@@ -25,9 +25,29 @@
 // dropped and the chain is a plain sum, any order; otherwise every step
 // clips in k order and overflow is tracked per step.
 //
-// Tiling: a 256-thread CTA owns a 128 x 64 output tile, 8 x 4 outputs per
-// thread; k-tiles of 32 staged through double-buffered shared memory.  Zero
-// padding past K is neutral (a 0 product changes nothing, raises nothing).
+// General mode (chain2_kernel): a 256-thread CTA owns a 64 x 64 output tile,
+// 4 x 4 outputs per thread; k-tiles of 32 staged through double-buffered
+// shared memory.  Zero padding past K is neutral (a 0 product changes
+// nothing, raises nothing).
+//
+// Proven mode (chain_pk_kernel): every partial sum stays within [-M, M], so
+// two outputs (n, n+1) share one 32-bit accumulator as two 16-bit lanes and
+// two products cost two IMADs, one byte permute, one LOP3, one add and one
+// LOP3 for the underflow test.  Per product (lane), with c = 0x7FFF + [a == 0]:
+//     p2 = |a| (|b| << (17 - N)) + (c << 16),   lane u = p2 >> 16 = t + c
+// (t = trunc(|a| |b| / 2^(N-1)) < 2^15, so u < 2^16 and bit 15 of u is set
+// exactly when t >= 1 or a == 0).  The byte permute gathers the two lanes'
+// upper halves into one word pk; the step adds x = pk ^ sa ^ sb (sa a full
+// word mask, sb per-lane 0xFFFF masks: x = u, or 0xFFFF - u when the product
+// is negative) and ANDs pk | zb (zb: 0xFFFF per lane where b == 0) into the
+// underflow word.  The sum of x over a 32-k block equals the wanted signed
+// sum plus 32 * 0x7FFF plus popc(w_a ^ w_b) per lane, with w_a the row's
+// bits (a < 0 or a == 0) and w_b the column's bits (b < 0): that correction
+// is subtracted per block (lane carries only move whole units of 2^16 that
+// the decode accounts for), and the final word decodes as lo = int16(low
+// half), hi = (word - lo) >> 16.  Underflow of lane L: bit 15 + 16 L of the
+// underflow word is clear.  A 256-thread CTA owns a 128 x 128 tile, 8 rows x
+// 4 lane pairs per thread.
 #include "sfb_common.cuh"
 
 namespace sfb {
@@ -59,6 +79,26 @@ struct Epi {
     int16_t *codes;           // nullable
     uint8_t *flags;           // nullable
 };
+
+// One output of either kernel: the optional saturating bias add, codes,
+// flags, float64 dequantization, event counts.
+__device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, int gn, int v, bool o, bool un,
+                                     Counts &cnt) {
+    if (e.bias) {
+        const int s = v + (int)e.bias[gn];
+        o |= (s > w.M || s < -w.M);
+        v = clampi(s, -w.M, w.M);
+    }
+    if (e.codes) e.codes[idx] = (int16_t)v;
+    if (e.flags) e.flags[idx] = (uint8_t)((o ? SFB_F_OVERFLOW : 0u) | (un ? SFB_F_UNDERFLOW : 0u));
+    if (e.y32 || e.y64) {
+        const double y = (double)v / (double)(1 << w.sh) * e.a * e.s_col[gn];
+        if (e.y32) e.y32[idx] = (float)y;
+        if (e.y64) e.y64[idx] = y;
+    }
+    cnt.over += o;
+    cnt.under += un;
+}
 
 // TM rows per thread: 8 when the clip is proven unnecessary (BM = 128), 4 with
 // the per-step clip and overflow tracking (BM = 64), to stay within registers.
@@ -211,27 +251,11 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
             const int gn = n0 + tx * TN + j;
             if (gm < M && gn < N) {
                 int v = acc[i][j];
-                bool o = ov[i][j] != 0;
                 if (SAFE && (v > w.M || v < -w.M)) {           // the caller's proof did not hold
                     bad++;
                     v = clampi(v, -w.M, w.M);
                 }
-                if (e.bias) {
-                    const int s = v + (int)e.bias[gn];
-                    o |= (s > w.M || s < -w.M);
-                    v = clampi(s, -w.M, w.M);
-                }
-                const bool un = um[i][j] < unit_m1;
-                const int64_t idx = z * so + (int64_t)gm * N + gn;
-                if (e.codes) e.codes[idx] = (int16_t)v;
-                if (e.flags) e.flags[idx] = (uint8_t)((o ? SFB_F_OVERFLOW : 0u) | (un ? SFB_F_UNDERFLOW : 0u));
-                if (e.y32 || e.y64) {
-                    const double y = (double)v / (double)(1 << w.sh) * e.a * e.s_col[gn];
-                    if (e.y32) e.y32[idx] = (float)y;
-                    if (e.y64) e.y64[idx] = y;
-                }
-                cnt.over += o;
-                cnt.under += un;
+                emit(e, w, z * so + (int64_t)gm * N + gn, gn, v, ov[i][j] != 0, um[i][j] < unit_m1, cnt);
             }
         }
     }
@@ -239,31 +263,232 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
     flush_counts(cnt, counts, sc);
 }
 
+constexpr int PK_BM = 128, PK_BN = 128, PK_BK = 32, PK_TM = 8, PK_TP = 4;   // PK_TP lane pairs per thread
+
+struct PkStage {
+    uint32_t a_mag[PK_BK][PK_BM];         // |a|
+    uint32_t a_add[PK_BK][PK_BM];         // (0x7FFF + [a == 0]) << 16
+    uint32_t a_sgn[PK_BK][PK_BM];         // 0 or 0xFFFFFFFF
+    uint32_t b_mag[PK_BK][PK_BN];         // |b| << (17 - N)
+    uint32_t b_sgn[PK_BK][PK_BN / 2];     // 0xFFFF per negative lane
+    uint32_t b_zero[PK_BK][PK_BN / 2];    // 0xFFFF per zero lane
+    uint32_t a_w[PK_BM];                  // bit k: a < 0 or a == 0
+    uint32_t b_w[PK_BN];                  // bit k: b < 0
+};
+
+constexpr int PK_SMEM = 2 * (int)sizeof(PkStage);
+
+__global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__restrict__ A,
+                                                             const int16_t *__restrict__ B, int M, int N, int K,
+                                                             int64_t lda, int64_t ldb, int64_t sa, int64_t sb,
+                                                             int64_t so, Width w, Epi e, int vec,
+                                                             sfb_counts *counts) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    PkStage *st = reinterpret_cast<PkStage *>(smem_raw);
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;               // lane pairs tx*4.., rows ty*8..
+    const int m0 = blockIdx.y * PK_BM, n0 = blockIdx.x * PK_BN;
+    const int64_t z = blockIdx.z;
+    A += z * sa;
+    B += z * sb;
+    const int bshift = 17 - w.bits;
+    const int nk = (K + PK_BK - 1) / PK_BK;
+
+    uint32_t acc[PK_TM][PK_TP], uf[PK_TM][PK_TP];
+    const uint32_t acc0 = 0u - (uint32_t)nk * (32u * 0x7FFFu * 0x10001u);
+#pragma unroll
+    for (int i = 0; i < PK_TM; i++)
+#pragma unroll
+        for (int p = 0; p < PK_TP; p++) acc[i][p] = acc0, uf[i][p] = 0xFFFFFFFFu;
+
+    // loaders: A row tid/2, 16 k from (tid&1)*16; B k-row tid/8, 16 columns from (tid&7)*16
+    const int ar = tid >> 1, ak = (tid & 1) * 16;
+    const int bk = tid >> 3, bc = (tid & 7) * 16;
+    Pack8 ra[2], rb[2];
+    auto load_regs = [&](int k0) {
+        const int gm = m0 + ar;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int kq = k0 + ak + q * 8;
+            if (vec && gm < M && kq + 8 <= K) {
+                ra[q].u = __ldg(reinterpret_cast<const uint4 *>(A + (int64_t)gm * lda + kq));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    ra[q].h[j] = (gm < M && kq + j < K) ? A[(int64_t)gm * lda + kq + j] : (int16_t)0;
+            }
+        }
+        const int gk = k0 + bk;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            const int gn = n0 + bc + q * 8;
+            if (vec && gk < K && gn + 8 <= N) {
+                rb[q].u = __ldg(reinterpret_cast<const uint4 *>(B + (int64_t)gk * ldb + gn));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    rb[q].h[j] = (gk < K && gn + j < N) ? B[(int64_t)gk * ldb + gn + j] : (int16_t)0;
+            }
+        }
+    };
+    auto store_regs = [&](PkStage &s) {
+        uint32_t bits = 0;
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int v = ra[q].h[j];
+                const int kk = ak + q * 8 + j;
+                s.a_mag[kk][ar] = (uint32_t)abs(v);
+                s.a_add[kk][ar] = (0x7FFFu + (uint32_t)(v == 0)) << 16;
+                s.a_sgn[kk][ar] = (uint32_t)(v >> 31);
+                bits |= (uint32_t)(v <= 0) << kk;
+            }
+        bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+        if ((tid & 1) == 0) s.a_w[ar] = bits;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            uint32_t mag[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) mag[j] = (uint32_t)abs((int)rb[q].h[j]) << bshift;
+            *reinterpret_cast<uint4 *>(&s.b_mag[bk][bc + q * 8]) = make_uint4(mag[0], mag[1], mag[2], mag[3]);
+            *reinterpret_cast<uint4 *>(&s.b_mag[bk][bc + q * 8 + 4]) = make_uint4(mag[4], mag[5], mag[6], mag[7]);
+            uint32_t sg[4], zr[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int lo = rb[q].h[2 * j], hi = rb[q].h[2 * j + 1];
+                sg[j] = (lo < 0 ? 0xFFFFu : 0u) | (hi < 0 ? 0xFFFF0000u : 0u);
+                zr[j] = (lo == 0 ? 0xFFFFu : 0u) | (hi == 0 ? 0xFFFF0000u : 0u);
+            }
+            *reinterpret_cast<uint4 *>(&s.b_sgn[bk][(bc + q * 8) / 2]) = make_uint4(sg[0], sg[1], sg[2], sg[3]);
+            *reinterpret_cast<uint4 *>(&s.b_zero[bk][(bc + q * 8) / 2]) = make_uint4(zr[0], zr[1], zr[2], zr[3]);
+        }
+    };
+
+    if (nk > 0) {
+        load_regs(0);
+        store_regs(st[0]);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        PkStage &cur = st[kt & 1];
+        if (tid < PK_BN) {                    // column sign words of this k-tile
+            const uint32_t lane_bit = (tid & 1) ? 31u : 15u;
+            uint32_t bits = 0;
+#pragma unroll 8
+            for (int k = 0; k < PK_BK; k++) bits |= ((cur.b_sgn[k][tid >> 1] >> lane_bit) & 1u) << k;
+            cur.b_w[tid] = bits;
+        }
+        if (kt + 1 < nk) load_regs((kt + 1) * PK_BK);
+        __syncthreads();
+#pragma unroll 2
+        for (int k = 0; k < PK_BK; k++) {
+            uint32_t am[PK_TM], ad[PK_TM], as_[PK_TM];
+#pragma unroll
+            for (int q = 0; q < PK_TM / 4; q++) {
+                const uint4 m4 = *reinterpret_cast<const uint4 *>(&cur.a_mag[k][ty * PK_TM + 4 * q]);
+                const uint4 d4 = *reinterpret_cast<const uint4 *>(&cur.a_add[k][ty * PK_TM + 4 * q]);
+                const uint4 s4 = *reinterpret_cast<const uint4 *>(&cur.a_sgn[k][ty * PK_TM + 4 * q]);
+                am[4 * q] = m4.x, am[4 * q + 1] = m4.y, am[4 * q + 2] = m4.z, am[4 * q + 3] = m4.w;
+                ad[4 * q] = d4.x, ad[4 * q + 1] = d4.y, ad[4 * q + 2] = d4.z, ad[4 * q + 3] = d4.w;
+                as_[4 * q] = s4.x, as_[4 * q + 1] = s4.y, as_[4 * q + 2] = s4.z, as_[4 * q + 3] = s4.w;
+            }
+            const uint4 bm0 = *reinterpret_cast<const uint4 *>(&cur.b_mag[k][tx * 2 * PK_TP]);
+            const uint4 bm1 = *reinterpret_cast<const uint4 *>(&cur.b_mag[k][tx * 2 * PK_TP + 4]);
+            const uint4 bs4 = *reinterpret_cast<const uint4 *>(&cur.b_sgn[k][tx * PK_TP]);
+            const uint4 bz4 = *reinterpret_cast<const uint4 *>(&cur.b_zero[k][tx * PK_TP]);
+            const uint32_t bm[2 * PK_TP] = {bm0.x, bm0.y, bm0.z, bm0.w, bm1.x, bm1.y, bm1.z, bm1.w};
+            const uint32_t bs[PK_TP] = {bs4.x, bs4.y, bs4.z, bs4.w};
+            const uint32_t bz[PK_TP] = {bz4.x, bz4.y, bz4.z, bz4.w};
+#pragma unroll
+            for (int i = 0; i < PK_TM; i++)
+#pragma unroll
+                for (int p = 0; p < PK_TP; p++) {
+                    const uint32_t plo = am[i] * bm[2 * p] + ad[i];
+                    const uint32_t phi = am[i] * bm[2 * p + 1] + ad[i];
+                    const uint32_t pk2 = __byte_perm(plo, phi, 0x7632);
+                    acc[i][p] += pk2 ^ as_[i] ^ bs[p];
+                    uf[i][p] &= pk2 | bz[p];
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < PK_TM; i++) {
+            const uint32_t wa = cur.a_w[ty * PK_TM + i];
+#pragma unroll
+            for (int p = 0; p < PK_TP; p++) {
+                const uint32_t nlo = __popc(wa ^ cur.b_w[tx * 2 * PK_TP + 2 * p]);
+                const uint32_t nhi = __popc(wa ^ cur.b_w[tx * 2 * PK_TP + 2 * p + 1]);
+                acc[i][p] -= nlo + (nhi << 16);
+            }
+        }
+        if (kt + 1 < nk) store_regs(st[(kt + 1) & 1]);
+        __syncthreads();
+    }
+
+    Counts cnt;
+    unsigned bad = 0;
+#pragma unroll
+    for (int i = 0; i < PK_TM; i++) {
+        const int gm = m0 + ty * PK_TM + i;
+#pragma unroll
+        for (int p = 0; p < PK_TP; p++) {
+            const int lo = (int)(int16_t)(acc[i][p] & 0xFFFFu);
+            const int hi = ((int)acc[i][p] - lo) >> 16;
+#pragma unroll
+            for (int l = 0; l < 2; l++) {
+                const int gn = n0 + tx * 2 * PK_TP + 2 * p + l;
+                if (gm < M && gn < N) {
+                    int v = l ? hi : lo;
+                    if (v > w.M || v < -w.M) {                // the caller's proof did not hold
+                        bad++;
+                        v = clampi(v, -w.M, w.M);
+                    }
+                    const bool un = ((uf[i][p] >> (15 + 16 * l)) & 1u) == 0;
+                    emit(e, w, z * so + (int64_t)gm * N + gn, gn, v, false, un, cnt);
+                }
+            }
+        }
+    }
+    if (bad && counts) atomicAdd(&counts->reserved[1], (unsigned long long)bad);
+    flush_counts(cnt, counts, sc);
+}
+
 int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int64_t batch, int64_t M, int64_t N,
                  int64_t K, int64_t lda, int64_t ldb, int64_t sa, int64_t sb, int64_t so, bool safe,
                  sfb_counts *counts, cudaStream_t st, const char *what) {
-    const int BM = safe ? 128 : 64;
-    const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
+    const int BM = safe ? PK_BM : 64, BNL = safe ? PK_BN : BN;
+    const int64_t mt = (M + BM - 1) / BM, nt = (N + BNL - 1) / BNL;
     if (mt > 65535 || nt > 0x7fffffff || batch > 65535 || K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff)
         return set_error(SFB_ERANGE, "%s: %lld x %lld x %lld (batch %lld) exceeds the launch limits", what,
                          (long long)M, (long long)N, (long long)K, (long long)batch);
     dim3 grid((unsigned)nt, (unsigned)mt, (unsigned)batch);
-    const int smem = safe ? 2 * (int)sizeof(Stage<128>) : 2 * (int)sizeof(Stage<64>);
-    static bool attr[64][4] = {};
+    static bool attr[64][3] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     const Width w = width(bits);
-    const bool b16 = bits == 16;
-    const int which = (safe ? 2 : 0) + (b16 ? 1 : 0);
-    auto kern = safe ? (b16 ? chain2_kernel<true, true, 8> : chain2_kernel<true, false, 8>)
-                     : (b16 ? chain2_kernel<false, true, 4> : chain2_kernel<false, false, 4>);
     const int vec = (lda % 8 == 0) && (ldb % 8 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0) &&
                     (sa % 8 == 0) && (sb % 8 == 0);
-    if (!attr[dev][which]) {
+    if (safe) {
+        if (!attr[dev][2]) {
+            if (cudaFuncSetAttribute(chain_pk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PK_SMEM) !=
+                cudaSuccess)
+                return check_launch(what);
+            attr[dev][2] = true;
+        }
+        chain_pk_kernel<<<grid, THREADS, PK_SMEM, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e,
+                                                        vec, counts);
+        return check_launch(what);
+    }
+    const int smem = 2 * (int)sizeof(Stage<64>);
+    const bool b16 = bits == 16;
+    auto kern = b16 ? chain2_kernel<false, true, 4> : chain2_kernel<false, false, 4>;
+    if (!attr[dev][b16]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch(what);
-        attr[dev][which] = true;
+        attr[dev][b16] = true;
     }
     kern<<<grid, THREADS, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
     return check_launch(what);
