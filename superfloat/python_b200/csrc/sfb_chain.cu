@@ -46,8 +46,8 @@
 // is subtracted per block (lane carries only move whole units of 2^16 that
 // the decode accounts for), and the final word decodes as lo = int16(low
 // half), hi = (word - lo) >> 16.  Underflow of lane L: bit 15 + 16 L of the
-// underflow word is clear.  A 256-thread CTA owns a 128 x 128 tile, 8 rows x
-// 4 lane pairs per thread.
+// underflow word is clear.  A 384-thread CTA owns a 192 x 128 tile, 8 rows x
+// 4 lane pairs per thread, one CTA per SM.
 #include "sfb_common.cuh"
 
 namespace sfb {
@@ -263,32 +263,39 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
     flush_counts(cnt, counts, sc);
 }
 
-constexpr int PK_BM = 128, PK_BN = 128, PK_BK = 32, PK_TM = 8, PK_TP = 4;   // PK_TP lane pairs per thread
+constexpr int PK_BN = 128, PK_BK = 32, PK_TP = 4;   // PK_TP lane pairs (8 columns) per thread
 
+template <int BM>
 struct PkStage {
-    uint32_t a_mag[PK_BK][PK_BM];         // |a|
-    uint32_t a_add[PK_BK][PK_BM];         // (0x7FFF + [a == 0]) << 16
-    uint32_t a_sgn[PK_BK][PK_BM];         // 0 or 0xFFFFFFFF
+    uint32_t a_mag[PK_BK][BM];            // |a|
+    uint32_t a_add[PK_BK][BM];            // (0x7FFF + [a == 0]) << 16
+    uint32_t a_sgn[PK_BK][BM];            // 0 or 0xFFFFFFFF
     uint32_t b_mag[PK_BK][PK_BN];         // |b| << (17 - N)
     uint32_t b_sgn[PK_BK][PK_BN / 2];     // 0xFFFF per negative lane
     uint32_t b_zero[PK_BK][PK_BN / 2];    // 0xFFFF per zero lane
-    uint32_t a_w[PK_BM];                  // bit k: a < 0 or a == 0
+    uint32_t a_w[BM];                     // bit k: a < 0 or a == 0
     uint32_t b_w[PK_BN];                  // bit k: b < 0
 };
 
-constexpr int PK_SMEM = 2 * (int)sizeof(PkStage);
+template <int TM, int NT>
+constexpr int pk_smem() { return 2 * (int)sizeof(PkStage<TM * NT / 16>); }
 
-__global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__restrict__ A,
-                                                             const int16_t *__restrict__ B, int M, int N, int K,
-                                                             int64_t lda, int64_t ldb, int64_t sa, int64_t sb,
-                                                             int64_t so, Width w, Epi e, int vec,
-                                                             sfb_counts *counts) {
+// NT threads with TM rows each: a CTA owns a (TM NT / 16) x 128 tile, one CTA
+// per SM.  The running sums are added with an IMAD by a runtime one, which
+// keeps that add on the FMA pipe beside the two product IMADs while the byte
+// permute and the two LOP3s use the ALU pipe.
+template <int TM, int NT>
+__global__ void __launch_bounds__(NT, 1) chain_pk_kernel(const int16_t *__restrict__ A,
+                                                         const int16_t *__restrict__ B, int M, int N, int K,
+                                                         int64_t lda, int64_t ldb, int64_t sa, int64_t sb, int64_t so,
+                                                         Width w, Epi e, int vec, uint32_t one, sfb_counts *counts) {
+    constexpr int PK_TM = TM, PK_BM = TM * NT / 16;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    PkStage *st = reinterpret_cast<PkStage *>(smem_raw);
+    PkStage<PK_BM> *st = reinterpret_cast<PkStage<PK_BM> *>(smem_raw);
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;               // lane pairs tx*4.., rows ty*8..
+    const int tx = tid & 15, ty = tid >> 4;               // lane pairs tx*4.., rows ty*TM..
     const int m0 = blockIdx.y * PK_BM, n0 = blockIdx.x * PK_BN;
     const int64_t z = blockIdx.z;
     A += z * sa;
@@ -303,14 +310,20 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
 #pragma unroll
         for (int p = 0; p < PK_TP; p++) acc[i][p] = acc0, uf[i][p] = 0xFFFFFFFFu;
 
-    // loaders: A row tid/2, 16 k from (tid&1)*16; B k-row tid/8, 16 columns from (tid&7)*16
-    const int ar = tid >> 1, ak = (tid & 1) * 16;
-    const int bk = tid >> 3, bc = (tid & 7) * 16;
-    Pack8 ra[2], rb[2];
+    // loaders: A row tid / TPR, PER k from (tid % TPR) * PER; B k-row tid / TPB, BPER columns from
+    // (tid % TPB) * BPER
+    constexpr int TPR = NT / PK_BM, PER = PK_BK / TPR;
+    constexpr int NTB = NT < 512 ? 256 : 512;               // threads that load B
+    constexpr int BPER = PK_BK * PK_BN / NTB, TPB = PK_BN / BPER;
+    static_assert(PER % 8 == 0 && BPER % 8 == 0 && NT % PK_BM == 0 && NT >= NTB, "loader widths");
+    const int ar = tid / TPR, ak = (tid % TPR) * PER;
+    const int bk = tid / TPB, bc = (tid % TPB) * BPER;
+    const bool bload = tid < NTB;
+    Pack8 ra[PER / 8], rb[BPER / 8];
     auto load_regs = [&](int k0) {
         const int gm = m0 + ar;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
+        for (int q = 0; q < PER / 8; q++) {
             const int kq = k0 + ak + q * 8;
             if (vec && gm < M && kq + 8 <= K) {
                 ra[q].u = __ldg(reinterpret_cast<const uint4 *>(A + (int64_t)gm * lda + kq));
@@ -322,8 +335,9 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
         }
         const int gk = k0 + bk;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
+        for (int q = 0; q < BPER / 8; q++) {
             const int gn = n0 + bc + q * 8;
+            if (!bload) continue;
             if (vec && gk < K && gn + 8 <= N) {
                 rb[q].u = __ldg(reinterpret_cast<const uint4 *>(B + (int64_t)gk * ldb + gn));
             } else {
@@ -333,10 +347,10 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
             }
         }
     };
-    auto store_regs = [&](PkStage &s) {
+    auto store_regs = [&](PkStage<PK_BM> &s) {
         uint32_t bits = 0;
 #pragma unroll
-        for (int q = 0; q < 2; q++)
+        for (int q = 0; q < PER / 8; q++)
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int v = ra[q].h[j];
@@ -346,10 +360,12 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
                 s.a_sgn[kk][ar] = (uint32_t)(v >> 31);
                 bits |= (uint32_t)(v <= 0) << kk;
             }
-        bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
-        if ((tid & 1) == 0) s.a_w[ar] = bits;
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
+        for (int o = 1; o < TPR; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
+        if (tid % TPR == 0) s.a_w[ar] = bits;
+#pragma unroll
+        for (int q = 0; q < BPER / 8; q++) {
+            if (!bload) continue;
             uint32_t mag[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) mag[j] = (uint32_t)abs((int)rb[q].h[j]) << bshift;
@@ -373,7 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
     }
     __syncthreads();
     for (int kt = 0; kt < nk; kt++) {
-        PkStage &cur = st[kt & 1];
+        PkStage<PK_BM> &cur = st[kt & 1];
         if (tid < PK_BN) {                    // column sign words of this k-tile
             const uint32_t lane_bit = (tid & 1) ? 31u : 15u;
             uint32_t bits = 0;
@@ -409,7 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
                     const uint32_t plo = am[i] * bm[2 * p] + ad[i];
                     const uint32_t phi = am[i] * bm[2 * p + 1] + ad[i];
                     const uint32_t pk2 = __byte_perm(plo, phi, 0x7632);
-                    acc[i][p] += pk2 ^ as_[i] ^ bs[p];
+                    acc[i][p] = (pk2 ^ as_[i] ^ bs[p]) * one + acc[i][p];
                     uf[i][p] &= pk2 | bz[p];
                 }
         }
@@ -458,7 +474,8 @@ __global__ void __launch_bounds__(THREADS, 1) chain_pk_kernel(const int16_t *__r
 int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int64_t batch, int64_t M, int64_t N,
                  int64_t K, int64_t lda, int64_t ldb, int64_t sa, int64_t sb, int64_t so, bool safe,
                  sfb_counts *counts, cudaStream_t st, const char *what) {
-    const int BM = safe ? PK_BM : 64, BNL = safe ? PK_BN : BN;
+    constexpr int TMP = 8, NTP = 384;            // proven mode: 192 x 128 tiles, 12 warps per SM
+    const int BM = safe ? TMP * NTP / 16 : 64, BNL = safe ? PK_BN : BN;
     const int64_t mt = (M + BM - 1) / BM, nt = (N + BNL - 1) / BNL;
     if (mt > 65535 || nt > 0x7fffffff || batch > 65535 || K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff)
         return set_error(SFB_ERANGE, "%s: %lld x %lld x %lld (batch %lld) exceeds the launch limits", what,
@@ -473,13 +490,13 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
                     (sa % 8 == 0) && (sb % 8 == 0);
     if (safe) {
         if (!attr[dev][2]) {
-            if (cudaFuncSetAttribute(chain_pk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PK_SMEM) !=
-                cudaSuccess)
+            if (cudaFuncSetAttribute(chain_pk_kernel<TMP, NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pk_smem<TMP, NTP>()) != cudaSuccess)
                 return check_launch(what);
             attr[dev][2] = true;
         }
-        chain_pk_kernel<<<grid, THREADS, PK_SMEM, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e,
-                                                        vec, counts);
+        chain_pk_kernel<TMP, NTP><<<grid, NTP, pk_smem<TMP, NTP>(), st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa,
+                                                                          sb, so, w, e, vec, 1u, counts);
         return check_launch(what);
     }
     const int smem = 2 * (int)sizeof(Stage<64>);
