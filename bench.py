@@ -181,6 +181,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-matmul", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--matmul-only", type=int, default=0, metavar="SIZE",
                     help="time only the wide and chain matmuls, wide at SIZE^3 (a small case for profiling)")
     ap.add_argument("--gpt2-only", type=int, default=0, metavar="TOKENS",
@@ -340,10 +341,20 @@ def main():
         line["cpu_baseline"] = {"value": v, "unit": "Gelem/s", "cores": 1, "kind": "port",
                                 "sample": f"{n_sample} elements x 5 ops, NumPy, median of {reps}"}
 
-    # the matmuls beside it (rank 0 only, N = 1): not part of `value`
-    if rank == 0 and world == 1 and not args.no_matmul:
-        line["matmul"] = bench_matmuls(dev, fmt, torch)
-        line["matmul"]["gpt2_small_convert"] = bench_gpt2(torch)
+    # the exhaustive pair sweep beside it, row-sharded over all ranks: not part of `value`
+    if not args.no_sweep:
+        sw = bench_sweep(torch, dist, rank, world, cpu=(rank == 0 and world == 1 and not args.no_cpu))
+        if rank == 0:
+            line["sweep"] = sw
+
+    # the matmuls beside it: not part of `value`.  The wide one row-sharded over all
+    # ranks; chain 512^3 and the converted GPT-2 forward on rank 0 at N = 1.
+    if not args.no_matmul:
+        mm = bench_matmuls(dev, fmt, torch, rank=rank, world=world, dist=dist)
+        if rank == 0 and world == 1:
+            mm["gpt2_small_convert"] = bench_gpt2(torch)
+        if rank == 0:
+            line["matmul"] = mm
 
     if world > 1:
         dist.barrier()
@@ -353,29 +364,49 @@ def main():
     return 0
 
 
-def bench_matmuls(dev, fmt, torch, n=8192):
-    from superfloat.python_b200 import workloads
+def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
+    """The wide n^3 matmul (MX v4.9.2, shift 0), rows of A split over the
+    ranks with B replicated: device time of the compute as the max over
+    ranks, then the all-gather of the int16 row blocks timed apart; the
+    gathered output's checksum on rank 0.  Chain 512^3 on rank 0."""
+    from superfloat.python_b200 import _shard, workloads
     res = {}
     stream = torch.cuda.current_stream()
-    # wide n^3 (the MX engine, v4.9.2, shift 0)
     A, B = workloads.wide_square(n, n, n, 0)
-    tA, tB = dev.upload(A), dev.upload(B)
+    cuts = _shard.row_cuts(n, world)
+    lo, hi = cuts[rank], cuts[rank + 1]
+    tA, tB = dev.upload(A[lo:hi]), dev.upload(B)
     del A, B
-    out = torch.empty(n, n, dtype=torch.int16, device=dev.torch_device)
+    out = torch.empty(hi - lo, n, dtype=torch.int16, device=dev.torch_device)
     cnt = torch.zeros(8, dtype=torch.int64, device=dev.torch_device)
     for _ in range(2):
         dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     reps = 3
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     e0.record(stream)
     for _ in range(reps):
         dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
     e1.record(stream)
+    full = _shard.gather_rows(out, cuts, dist, world)
+    e2.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    res[f"wide_{n}"] = {"ms": ms, "TOPS": 2 * n ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
-    del tA, tB, out
+    ms = _shard.max_over_ranks(e0.elapsed_time(e1) / reps, "cuda", dist, world)
+    gms = _shard.max_over_ranks(e1.elapsed_time(e2), "cuda", dist, world)
+    cnt.zero_()
+    dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
+    _shard.sum_counts(cnt, dist, world)
+    res[f"wide_{n}"] = {"ms": ms, "TOPS": 2 * n ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)",
+                        "gather_ms": gms, "sharding": f"rows of A over {world} GPU(s), B replicated",
+                        "overflow_outputs": int(cnt[0]), "underflow_outputs": int(cnt[1])}
+    if rank == 0:
+        import hashlib
+        res[f"wide_{n}"]["codes_sha256"] = hashlib.sha256(full.cpu().numpy().astype("<i2").tobytes()).hexdigest()[:16]
+    del tA, tB, out, full
+    if rank != 0:
+        return res
     # chain 512^3
     A, B = workloads.chain_square(512, 0)
     tA, tB = dev.upload(A), dev.upload(B)
@@ -391,6 +422,60 @@ def bench_matmuls(dev, fmt, torch, n=8192):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     res["chain_512"] = {"ms": ms, "TOPS": 2 * 512 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
+    return res
+
+
+def bench_sweep(torch, dist, rank, world, bits=16, cpu=False):
+    """Every sf16 code pair through add, sub, mul and div (4 x 65535^2 =
+    1.7e10 pairs), the a-rows split evenly over the ranks; each row folds
+    into two 64-bit digests on the device.  Device time is the max over
+    ranks; rank 0 gathers the row digests and checks their sha256 against
+    the reference's (tests/golden/sweep.json) when that file is present."""
+    from superfloat.python_b200 import _shard, sweep
+    M = (1 << (bits - 1)) - 1
+    n = 2 * M + 1
+    cuts = _shard.row_cuts(n, world, -M)
+    lo, hi = cuts[rank], cuts[rank + 1]
+    for op in sweep.OPS:                                   # warm-up on a few rows
+        sweep.run_device(op, bits, lo, min(hi, lo + 64))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    outs = {op: sweep.run_device(op, bits, lo, hi) for op in sweep.OPS}
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _shard.max_over_ranks(e0.elapsed_time(e1), "cuda", dist, world)
+    res = {"ms": ms, "value": len(sweep.OPS) * n * n / (ms / 1e3) / 1e9, "unit": "Gpairs/s (add, sub, mul, div)",
+           "pairs": len(sweep.OPS) * n * n, "bits": bits, "sharding": f"a-rows over {world} GPU(s)"}
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "sweep.json")
+    ref = json.load(open(golden))["widths"][str(bits)] if os.path.exists(golden) else None
+    match = True
+    for op, (rc, rf, cnt) in outs.items():
+        rows = _shard.gather_rows(torch.stack([rc, rf], 1), cuts, dist, world)
+        _shard.sum_counts(cnt, dist, world)
+        if rank == 0:
+            rows = rows.cpu().numpy()
+            sha = sweep.digest(rows[:, 0].view(np.uint64), rows[:, 1].view(np.uint64))
+            c = cnt.cpu().numpy()
+            ok = ref is not None and sha == ref[op]["sha"] and all(
+                int(c[i]) == ref[op][f"n_{e}"] for i, e in enumerate(("overflow", "underflow", "divide", "invalid")))
+            match &= ok
+            res[op] = {"sha256": sha[:16], "overflow": int(c[0]), "underflow": int(c[1]), "divide": int(c[2])}
+    if rank == 0:
+        res["digests_match_reference"] = bool(match) if ref is not None else None
+    if cpu:
+        from oracle import sfref
+        rows = np.arange(-3, 3)
+        b = np.arange(-M, M + 1)
+        ka, kb = np.repeat(rows, n), np.tile(b, rows.size)
+        t0 = time.perf_counter()
+        for op in sweep.OPS:
+            sfref.ew(op, bits, ka, kb)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": len(sweep.OPS) * ka.size / dt / 1e9, "unit": "Gpairs/s", "cores": 1,
+                               "kind": "port", "sample": f"{rows.size} a-rows x {n} b, 4 ops, NumPy oracle"}
     return res
 
 

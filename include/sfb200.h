@@ -195,6 +195,18 @@ SFB_API int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const in
                                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
                                     sfb_counts *counts, sfb_stream stream);
 
+/* Exhaustive sweep of every operand pair of one width.  No counterpart in
+ * the reference's Device API: the GPU form of its exhaustive check,
+ * tools/exhaustive.py:146-181.  For op in SFB_OP_ADD / SUB / MUL / DIV and
+ * the rows a = a_lo .. a_hi - 1 (codes, -M <= a_lo <= a_hi <= M + 1), entry
+ * a - a_lo of row_codes and of row_flags has ADDED to it
+ *     sum over j = 0 .. 2M of  code(a, j - M) * w_j     (mod 2^64)
+ *     sum over j = 0 .. 2M of  flags(a, j - M) * w_j    (mod 2^64)
+ * with w_j = splitmix64(j) and flags the SFB_F_* bits of that pair; zero
+ * both buffers first.  Event totals add into counts.  Device buffers. */
+SFB_API int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint64_t *row_codes, uint64_t *row_flags,
+                      sfb_counts *counts, sfb_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,7 @@ SIGNATURES = {
                                _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
+    "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
 }
 
 _lib = None
@@ -168,6 +169,14 @@ def wide_workspace(bits, mx, batch, M, N, K) -> int:
     if n < 0:
         check(int(n), "sf matmul (wide) workspace")
     return int(n)
+
+
+def sweep(op, bits, a_lo, a_hi, row_codes, row_flags, counts, stream=None):
+    if op not in ("add", "sub", "mul", "div"):
+        raise ValueError(f"the sweep covers add, sub, mul and div, not {op!r}")
+    rc = load().sfb_sweep(OPS[op], bits, a_lo, a_hi, _ptr(row_codes), _ptr(row_flags), _ptr(counts),
+                          _stream(stream))
+    check(rc, "sf sweep")
 
 
 def matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so,

@@ -1,0 +1,68 @@
+"""Row sharding across ranks (one process per GPU, torch.distributed).
+
+The hot path partitions cleanly: elementwise ranges, matmul output rows and
+sweep a-rows are independent, so a rank computes its block with no exchange
+and only results meet: event counts are summed (all-reduce), row blocks are
+gathered (all-gather of equal, padded blocks), and device times take the max
+over ranks.  Every rank calls these in the same order.  The functions take
+the process group's module (``torch.distributed``) so the same code runs
+over NCCL on GPUs and over gloo on CPU tensors.
+"""
+from __future__ import annotations
+
+
+def row_cuts(n: int, world: int, start: int = 0) -> list[int]:
+    """world + 1 cut points splitting [start, start + n) into near-equal blocks."""
+    return [start + (n * r) // world for r in range(world + 1)]
+
+
+def block(n: int, world: int, rank: int, start: int = 0) -> tuple[int, int]:
+    c = row_cuts(n, world, start)
+    return c[rank], c[rank + 1]
+
+
+def sum_counts(counts, dist=None, world: int = 1):
+    """Event counts summed over ranks, in place."""
+    if dist is not None and world > 1:
+        dist.all_reduce(counts)
+    return counts
+
+
+def max_over_ranks(value: float, device, dist=None, world: int = 1) -> float:
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    if dist is not None and world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_rows(local, cuts, dist=None, world: int = 1):
+    """Concatenate every rank's row block (dim 0; blocks sized by ``cuts``),
+    on every rank."""
+    import torch
+    if dist is None or world == 1:
+        return local
+    rows_max = max(cuts[r + 1] - cuts[r] for r in range(world))
+    pad = torch.zeros((rows_max,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[:local.shape[0]] = local
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    return torch.cat([parts[r][:cuts[r + 1] - cuts[r]] for r in range(world)])
+
+
+def sharded_matmul(compute, A, B, rank: int, world: int, dist=None):
+    """Row-sharded matmul: this rank computes rows [lo, hi) of A @ B with
+    ``compute(A_block, B) -> (codes, flags, counts)`` (B replicated), then
+    the codes and flags are gathered and the counts summed, so every rank
+    ends with the whole result."""
+    M = A.shape[-2]
+    cuts = row_cuts(M, world)
+    lo, hi = cuts[rank], cuts[rank + 1]
+    codes, flags, counts = compute(A[..., lo:hi, :], B)
+    if A.dim() > 2:       # batched: rows are the second-to-last dim, gather along it
+        codes = gather_rows(codes.movedim(-2, 0).contiguous(), cuts, dist, world).movedim(0, -2)
+        flags = gather_rows(flags.movedim(-2, 0).contiguous(), cuts, dist, world).movedim(0, -2)
+    else:
+        codes = gather_rows(codes, cuts, dist, world)
+        flags = gather_rows(flags, cuts, dist, world)
+    return codes, flags, sum_counts(counts, dist, world)

@@ -1,14 +1,7 @@
 // Elementwise sfN ops with per-output events, HBM-streaming on sm_100a.
 //
-// Semantics follow the reference's vectorised ops (src/sf/_vectorized.py:94-156):
-//   add/sub  clip(a +- b, +-M), overflow where |a +- b| > M          (:94-99, :25-27)
-//   mul      trunc(a b / S), underflow where a b != 0 truncates to 0  (:110-113)
-//   div      b == 0: sign(a) M, divide; a != 0, |a| >= |b|: +-M, overflow;
-//            else trunc(a S / b)                                      (:116-125)
-//   fma      add(mul(a, b), c); underflow only where the add did not overflow (:128-131)
-//   neg/abs  exact                                                    (:102-107)
-//   sqrt     floor(sqrt(a S)), a < 0 -> 0 and invalid                 (:134-142)
-//   pow      chain of mul, underflow if any step underflowed          (:145-156)
+// The per-element arithmetic (the reference's vectorised ops,
+// src/sf/_vectorized.py:94-156) lives in sfb_ew_ops.cuh.
 //
 // Layout: int16 codes, 8 per 128-bit vector.  Each thread streams pairs of
 // vectors (grid-stride, grid = SMs x resident blocks), counts events in
@@ -19,120 +12,14 @@
 #include <math.h>
 
 #include "sfb_common.cuh"
+#include "sfb_ew_ops.cuh"
 
 namespace sfb {
 namespace {
 
+using namespace ewops;
+
 constexpr int kThreads = 256;
-
-// floor(ua 2^sh / ub) for 0 <= ua < ub < 2^15, sh <= 15 (the quotient is < 2^15).
-// Reciprocal estimate, then one exact integer correction:
-//   x = ua 2^sh / ub.  ua 2^sh and ub convert to float exactly with the
-//   exponent-bias trick (ua < 2^23 placed in the mantissa under exponent
-//   23 + sh); rcp.approx has relative error < 2^-22 and the product rounds
-//   once, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding
-//   it to the nearest integer (the 1.5 * 2^23 bias) gives floor(x) or
-//   floor(x) + 1, and the sign of the remainder tells which.
-// Outside the precondition (ua >= ub) the result is meaningless but every
-// step stays defined (unsigned arithmetic); callers discard it there.
-__device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
-    const float fa = __int_as_float(((150 + sh) << 23) | ua) - __int_as_float((150 + sh) << 23);
-    const float fb = __int_as_float(0x4B000000 | ub) - 8388608.0f;
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fb));
-    const unsigned q0 = (unsigned)__float_as_int(fa * r + 12582912.0f) - 0x4B400000u;
-    const unsigned rem = (ua << sh) - q0 * ub;
-    return q0 + (unsigned)((int)rem >> 31);                            // q0 - 1 when rem < 0
-}
-
-// Events one output raised; each op sets only the ones it can raise, so the
-// compiler drops the others from the tally.
-struct Ev {
-    bool over = false, under = false, div0 = false, inval = false;
-};
-
-// Width constants, folded at compile time for BITS != 0 (the sf16 kernels).
-template <int BITS>
-__device__ __forceinline__ Width wfix(Width w) {
-    if constexpr (BITS != 0) return Width{BITS, BITS - 1, (1 << (BITS - 1)) - 1};
-    return w;
-}
-
-// 0 < |p| < 2^sh: a nonzero product that truncates to 0.
-__device__ __forceinline__ bool small_nonzero(int p, int sh) {
-    return (unsigned)(p + ((1 << sh) - 1)) <= (unsigned)((2 << sh) - 2) && p != 0;
-}
-
-template <int OP, int BITS>
-__device__ __forceinline__ int ew_one(int a, int b, int c, Width w0, int pow_n, Ev &ev) {
-    const Width w = wfix<BITS>(w0);
-    const int M = w.M, sh = w.sh;
-    if constexpr (OP == SFB_OP_ADD || OP == SFB_OP_SUB) {
-        const int s = (OP == SFB_OP_ADD) ? a + b : a - b;
-        const int r = clampi(s, -M, M);
-        ev.over = r != s;
-        return r;
-    } else if constexpr (OP == SFB_OP_MUL) {
-        const int p = a * b;
-        ev.under = small_nonzero(p, sh);
-        return tdiv_pow2(p, sh);
-    } else if constexpr (OP == SFB_OP_FMA) {
-        // a product that truncates to 0 leaves c unchanged and in range, so
-        // the fma's underflow needs no "and not overflow" term
-        const int p = a * b;
-        const int s = tdiv_pow2(p, sh) + c;
-        const int r = clampi(s, -M, M);
-        ev.over = r != s;
-        ev.under = small_nonzero(p, sh);
-        return r;
-    } else if constexpr (OP == SFB_OP_DIV) {
-        // branch-free: every lane computes the quotient (meaningless where
-        // |a| >= |b| or b == 0, and discarded there), then selects
-        const bool z = b == 0;
-        const unsigned ua = (unsigned)abs(a), ub = (unsigned)abs(b);
-        const bool ov = !z && a != 0 && ua >= ub;
-        const unsigned q = udiv_small(ua, ub + z, sh);
-        const int s = (a ^ b) >> 31;                 // -1 where the quotient is negative
-        const int sq = ((int)q ^ s) - s;
-        const int sat = a == 0 ? 0 : ((M ^ s) - s);  // +-M with the quotient's sign; 0/0 -> 0
-        ev.over = ov;
-        ev.div0 = z;
-        return (z || ov) ? sat : sq;
-    } else if constexpr (OP == SFB_OP_NEG) {
-        return -a;
-    } else if constexpr (OP == SFB_OP_ABS) {
-        return abs(a);
-    } else if constexpr (OP == SFB_OP_SQRT) {
-        ev.inval = a < 0;
-        const int x = max(a, 0) << sh;      // < 2^30
-        int r = (int)sqrtf((float)x);       // within 1 of floor(sqrt(x)) for x < 2^30
-        r -= (r * r > x);
-        r += ((r + 1) * (r + 1) <= x);
-        return r;
-    } else {  // SFB_OP_POW
-        int k = a;
-        bool un = false;
-        for (int i = 1; i < pow_n; i++) {
-            const int p = k * a;
-            un |= small_nonzero(p, sh);
-            k = tdiv_pow2(p, sh);
-        }
-        ev.under = un;
-        return k;
-    }
-}
-
-__device__ __forceinline__ void tally(Counts &c, const Ev &e) {
-    c.over += e.over;
-    c.under += e.under;
-    c.div0 += e.div0;
-    c.inval += e.inval;
-}
-
-__device__ __forceinline__ unsigned flag_byte(const Ev &e) {
-    return (e.over ? SFB_F_OVERFLOW : 0u) | (e.under ? SFB_F_UNDERFLOW : 0u) | (e.div0 ? SFB_F_DIVIDE : 0u) |
-           (e.inval ? SFB_F_INVALID : 0u);
-}
 
 union Vec8 {
     uint4 u;

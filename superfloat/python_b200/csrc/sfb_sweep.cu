@@ -1,0 +1,113 @@
+// Exhaustive sweep of every operand pair of one width (the reference's
+// tools/exhaustive.py:146-181, on the GPU).
+//
+// Rows are the a codes of [a_lo, a_hi); every row pairs a with all 2M+1
+// codes b_j = j - M and evaluates the op with the elementwise kernels' own
+// per-element arithmetic (sfb_ew_ops.cuh).  Nothing per pair is stored: each
+// row folds into two 64-bit digests, sum_j code * w_j and sum_j flags * w_j
+// (mod 2^64, w_j = splitmix64(j)), and the events are totalled.
+//
+// A CTA owns RB consecutive rows; its threads stride over j, compute w_j
+// once and apply it to the RB rows, keeping 2 RB running digests in
+// registers; a warp shuffle reduction and one 64-bit atomic add per row and
+// warp finish the row.  The sweep is ALU-bound (about 2^32 pairs per op at
+// sf16), with 16 bytes written per row.
+#include "sfb_common.cuh"
+#include "sfb_ew_ops.cuh"
+
+namespace sfb {
+namespace {
+
+using namespace ewops;
+
+constexpr int SW_THREADS = 256, RB = 8;
+
+__device__ __forceinline__ unsigned long long splitmix64(unsigned long long x) {
+    unsigned long long z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+template <int OP, int BITS>
+__global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, int a_hi,
+                                                          unsigned long long *__restrict__ row_codes,
+                                                          unsigned long long *__restrict__ row_flags,
+                                                          sfb_counts *counts) {
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    const int M = w.M, n = 2 * w.M + 1;
+    const int r0 = a_lo + blockIdx.x * RB;
+    unsigned long long dc[RB], df[RB];
+#pragma unroll
+    for (int r = 0; r < RB; r++) dc[r] = 0, df[r] = 0;
+    Counts cnt;
+    for (int j = threadIdx.x; j < n; j += SW_THREADS) {
+        const unsigned long long wj = splitmix64((unsigned long long)j);
+        const int b = j - M;
+#pragma unroll
+        for (int r = 0; r < RB; r++) {
+            const int a = r0 + r;
+            if (a < a_hi) {
+                Ev ev;
+                const int k = ew_one<OP, BITS>(a, b, 0, w, 0, ev);
+                dc[r] += (unsigned long long)(long long)k * wj;
+                df[r] += (unsigned long long)flag_byte(ev) * wj;
+                tally(cnt, ev);
+            }
+        }
+    }
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int r = 0; r < RB; r++) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            dc[r] += __shfl_xor_sync(0xffffffffu, dc[r], o);
+            df[r] += __shfl_xor_sync(0xffffffffu, df[r], o);
+        }
+        const int a = r0 + r;
+        if (lane == 0 && a < a_hi) {
+            atomicAdd(&row_codes[a - a_lo], dc[r]);
+            atomicAdd(&row_flags[a - a_lo], df[r]);
+        }
+    }
+    flush_counts(cnt, counts, sc);
+}
+
+template <int OP>
+void launch_sweep(int bits, int a_lo, int a_hi, unsigned long long *rc, unsigned long long *rf, sfb_counts *counts,
+                  cudaStream_t st) {
+    const int grid = (a_hi - a_lo + RB - 1) / RB;
+    const Width w = width(bits);
+    if (bits == 16)
+        sweep_kernel<OP, 16><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rc, rf, counts);
+    else
+        sweep_kernel<OP, 0><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rc, rf, counts);
+}
+
+}  // namespace
+}  // namespace sfb
+
+extern "C" int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint64_t *row_codes, uint64_t *row_flags,
+                         sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_sweep: width %d is not 4..16", bits);
+    const int64_t M = (1 << (bits - 1)) - 1;
+    if (a_lo < -M || a_hi > M + 1 || a_lo > a_hi)
+        return set_error(SFB_EINVAL, "sfb_sweep: rows [%lld, %lld) are not within [-%lld, %lld]", (long long)a_lo,
+                         (long long)a_hi, (long long)M, (long long)M);
+    if (a_lo == a_hi) return SFB_OK;
+    if (row_codes == nullptr || row_flags == nullptr)
+        return set_error(SFB_EINVAL, "sfb_sweep: null row digest buffer");
+    cudaStream_t st = (cudaStream_t)stream;
+    auto rc = reinterpret_cast<unsigned long long *>(row_codes);
+    auto rf = reinterpret_cast<unsigned long long *>(row_flags);
+    switch (op) {
+        case SFB_OP_ADD: launch_sweep<SFB_OP_ADD>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
+        case SFB_OP_SUB: launch_sweep<SFB_OP_SUB>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
+        case SFB_OP_MUL: launch_sweep<SFB_OP_MUL>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
+        case SFB_OP_DIV: launch_sweep<SFB_OP_DIV>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
+        default: return set_error(SFB_EINVAL, "sfb_sweep: op %d is not add, sub, mul or div", op);
+    }
+    return check_launch("sfb_sweep");
+}

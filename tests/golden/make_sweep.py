@@ -1,0 +1,114 @@
+"""Digests of the exhaustive pair sweep, from the reference's vectorised ops.
+
+Run in a container that has the reference tree (default /root/reference):
+
+    SF_CACHE_DIR=/tmp/sfcache python tests/golden/make_sweep.py [reference_root] [--procs 8]
+
+For each width in WIDTHS and op in add / sub / mul / div, every pair of
+codes (a, b) in [-M, M]^2 goes through the reference's ``vec.OPS[op]``
+(src/sf/_vectorized.py, the path tools/exhaustive.py:157-162 sweeps), and
+each a-row is folded into the row digests that
+``superfloat.python_b200.sweep.fold_rows`` defines.  sweep.json keeps the
+sha256 of all row digests, the event totals, and the row digests of a few
+sample rows.  About 5 minutes for sf16 on 8 processes.
+"""
+from __future__ import annotations
+
+import json
+import multiprocessing as mp
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from superfloat.python_b200 import sweep  # noqa: E402
+
+WIDTHS = (16, 8, 4)
+SAMPLE_ROWS = 8
+
+
+def _work(args):
+    ref, bits, op, r0, r1 = args
+    sys.path.insert(0, os.path.join(ref, "src"))
+    from sf import _vectorized as vec          # the reference
+    from sf._format import FORMATS
+    fmt = FORMATS[bits]
+    M = fmt.max_code
+    n = 2 * M + 1
+    codes = np.arange(-M, M + 1, dtype=np.int64)
+    w = sweep.weights(bits)
+    dc = np.empty(r1 - r0, np.uint64)
+    df = np.empty(r1 - r0, np.uint64)
+    counts = dict.fromkeys(sweep.FLAG_BITS, 0)
+    step = max(1, (1 << 22) // n)
+    for s in range(r0, r1, step):
+        e = min(r1, s + step)
+        ka = np.repeat(codes[s:e], n)
+        kb = np.tile(codes, e - s)
+        rk, rev = vec.OPS[op](fmt, ka, kb)
+        fl = np.zeros(ka.size, np.uint64)
+        for name, bit in sweep.FLAG_BITS.items():
+            m = rev.get(name)
+            if m is not None:
+                m = np.broadcast_to(m, ka.shape)
+                fl |= m.astype(np.uint64) * np.uint64(bit)
+                counts[name] += int(np.count_nonzero(m))
+        c, f = sweep.fold_rows(np.broadcast_to(rk, ka.shape).reshape(e - s, n), fl.reshape(e - s, n), w)
+        dc[s - r0:e - r0] = c
+        df[s - r0:e - r0] = f
+    return r0, dc, df, counts
+
+
+def main(argv):
+    ref = "/root/reference"
+    procs = 8
+    args = list(argv)
+    if "--procs" in args:
+        i = args.index("--procs")
+        procs = int(args[i + 1])
+        del args[i:i + 2]
+    if args:
+        ref = args[0]
+    os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
+    out = {"source": "reference src/sf/_vectorized.py OPS over every code pair",
+           "fold": "row digests of superfloat.python_b200.sweep.fold_rows; sha256 of codes then flags, "
+                   "little-endian uint64, rows a = -M..M",
+           "widths": {}}
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(procs) as pool:
+        for bits in WIDTHS:
+            M = (1 << (bits - 1)) - 1
+            n = 2 * M + 1
+            out["widths"][str(bits)] = {}
+            for op in sweep.OPS:
+                t0 = time.time()
+                cuts = np.linspace(0, n, procs * 4 + 1).astype(int)
+                jobs = [(ref, bits, op, int(cuts[i]), int(cuts[i + 1])) for i in range(len(cuts) - 1)
+                        if cuts[i + 1] > cuts[i]]
+                dc = np.empty(n, np.uint64)
+                df = np.empty(n, np.uint64)
+                tot = dict.fromkeys(sweep.FLAG_BITS, 0)
+                for r0, c, f, cnt in pool.imap_unordered(_work, jobs):
+                    dc[r0:r0 + c.size] = c
+                    df[r0:r0 + f.size] = f
+                    for k, v in cnt.items():
+                        tot[k] += v
+                rows = np.linspace(0, n - 1, SAMPLE_ROWS).astype(int)
+                out["widths"][str(bits)][op] = {
+                    "pairs": n * n, "sha": sweep.digest(dc, df),
+                    **{f"n_{k}": v for k, v in tot.items()},
+                    "sample_a": [int(r) - M for r in rows], "sample_codes": [int(dc[r]) for r in rows],
+                    "sample_flags": [int(df[r]) for r in rows]}
+                print(f"sf{bits} {op}: {n * n:,} pairs in {time.time() - t0:.0f}s", flush=True)
+    with open(os.path.join(HERE, "sweep.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print("wrote sweep.json")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
