@@ -11,6 +11,12 @@ over NCCL on GPUs and over gloo on CPU tensors.
 from __future__ import annotations
 
 
+def _nccl_type(dt) -> bool:
+    import torch
+    return dt in (torch.uint8, torch.int8, torch.int32, torch.int64, torch.float16, torch.bfloat16, torch.float32,
+                  torch.float64)
+
+
 def row_cuts(n: int, world: int, start: int = 0) -> list[int]:
     """world + 1 cut points splitting [start, start + n) into near-equal blocks."""
     return [start + (n * r) // world for r in range(world + 1)]
@@ -45,8 +51,13 @@ def gather_rows(local, cuts, dist=None, world: int = 1):
     rows_max = max(cuts[r + 1] - cuts[r] for r in range(world))
     pad = torch.zeros((rows_max,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
     pad[:local.shape[0]] = local
-    parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad)
+    wire = pad
+    if not _nccl_type(pad.dtype):                    # NCCL has no int16: send the bytes
+        wire = pad.reshape(rows_max, -1).view(torch.uint8)
+    parts = [torch.empty_like(wire) for _ in range(world)]
+    dist.all_gather(parts, wire)
+    if wire is not pad:
+        parts = [p.view(pad.dtype).reshape(pad.shape) for p in parts]
     return torch.cat([parts[r][:cuts[r + 1] - cuts[r]] for r in range(world)])
 
 

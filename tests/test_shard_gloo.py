@@ -35,6 +35,9 @@ def _worker(rank, world, port, out):
             cnt = torch.tensor([int(ev["overflow"].sum()), int(ev["underflow"].sum())], dtype=torch.int64)
             return torch.from_numpy(k), torch.from_numpy(fl), cnt
 
+        lo16, hi16 = _shard.block(9, world, rank)
+        c16 = (torch.arange(lo16, hi16, dtype=torch.int16)[:, None] * 1000 - 4000).repeat(1, 3)
+        g16 = _shard.gather_rows(c16, _shard.row_cuts(9, world), dist, world)
         codes, flags, cnt = _shard.sharded_matmul(compute, torch.from_numpy(A), torch.from_numpy(B), rank, world,
                                                   dist)
         t = _shard.max_over_ranks(1.5 + rank, "cpu", dist, world)
@@ -42,7 +45,7 @@ def _worker(rank, world, port, out):
         rows = torch.arange(lo, hi, dtype=torch.int64)[:, None].repeat(1, 2)
         allrows = _shard.gather_rows(rows, _shard.row_cuts(255, world, -127), dist, world)
         if rank == 0:
-            np.save(out, {"codes": codes.numpy(), "flags": flags.numpy(), "cnt": cnt.numpy(), "t": t,
+            np.save(out, {"g16": g16.numpy(), "codes": codes.numpy(), "flags": flags.numpy(), "cnt": cnt.numpy(), "t": t,
                           "rows": allrows.numpy()}, allow_pickle=True)
     finally:
         dist.destroy_process_group()
@@ -63,6 +66,8 @@ def test_sharded_matmul_and_gathers_over_gloo(tmp_path):
     assert r["cnt"].tolist() == [int(ev["overflow"].sum()), int(ev["underflow"].sum())]
     assert r["t"] == 2.5
     np.testing.assert_array_equal(r["rows"][:, 0], np.arange(-127, 128))
+    assert r["g16"].dtype == np.int16
+    np.testing.assert_array_equal(r["g16"], (np.arange(9)[:, None] * 1000 - 4000).repeat(3, 1))
 
 
 def test_row_cuts_cover_every_row():
