@@ -184,6 +184,9 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--matmul-only", type=int, default=0, metavar="SIZE",
                     help="time only the wide and chain matmuls, wide at SIZE^3 (a small case for profiling)")
+    ap.add_argument("--chain-only", action="store_true",
+                    help="time only the proven chain kernel on the GPT-2-small projection shapes")
+    ap.add_argument("--sweep-only", action="store_true", help="time only the exhaustive sf16 pair sweep")
     ap.add_argument("--gpt2-only", type=int, default=0, metavar="TOKENS",
                     help="time only the converted GPT-2-small forward on 8 x TOKENS ids")
     args = ap.parse_args()
@@ -198,6 +201,12 @@ def main():
     torch.cuda.set_device(local)
     if args.matmul_only:
         print(json.dumps(bench_matmuls(B200Device(local), FORMATS[16], torch, args.matmul_only)), flush=True)
+        return 0
+    if args.chain_only:
+        print(json.dumps(bench_chain_shapes(torch)), flush=True)
+        return 0
+    if args.sweep_only:
+        print(json.dumps(bench_sweep(torch, None, 0, 1)), flush=True)
         return 0
     if args.gpt2_only:
         print(json.dumps(bench_gpt2(torch, seq=args.gpt2_only)), flush=True)
@@ -352,6 +361,7 @@ def main():
     if not args.no_matmul:
         mm = bench_matmuls(dev, fmt, torch, rank=rank, world=world, dist=dist)
         if rank == 0 and world == 1:
+            mm["chain_gpt2_projections"] = bench_chain_shapes(torch)
             mm["gpt2_small_convert"] = bench_gpt2(torch)
         if rank == 0:
             line["matmul"] = mm
@@ -476,6 +486,46 @@ def bench_sweep(torch, dist, rank, world, bits=16, cpu=False):
         dt = time.perf_counter() - t0
         res["cpu_baseline"] = {"value": len(sweep.OPS) * ka.size / dt / 1e9, "unit": "Gpairs/s", "cores": 1,
                                "kind": "port", "sample": f"{rows.size} a-rows x {n} b, 4 ops, NumPy oracle"}
+    return res
+
+
+GPT2_SHAPES = ((4096, 768, 2304), (4096, 768, 768), (4096, 768, 3072), (4096, 3072, 768), (4096, 768, 50257))
+
+
+def bench_chain_shapes(torch, reps=10):
+    """sfb_linear_chain in proven mode (the converted layer's chain, bias-free,
+    float32 output) on the GPT-2-small projection shapes at 8 x 512 tokens:
+    activation codes in [-40, 40] and weight codes over the full sf16 range
+    (seed 0), which the L1 bound proves clip-free.  Products per second and
+    INT lane-instructions per second against SMs x 128 lanes x clock."""
+    from superfloat.python_b200 import _lib
+    _lib.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    props = torch.cuda.get_device_properties(0)
+    res = {}
+    for (R, K, N) in GPT2_SHAPES:
+        X = torch.randint(-40, 41, (R, K), dtype=torch.int16, device="cuda", generator=g)
+        WT = torch.randint(-32767, 32768, (K, N), dtype=torch.int16, device="cuda", generator=g)
+        s = torch.ones(N, dtype=torch.float64, device="cuda")
+        y = torch.empty(R, N, dtype=torch.float32, device="cuda")
+        cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device="cuda")
+
+        def f():
+            _lib.linear_chain(16, X, WT, None, 1.0, s, True, y, None, None, None, cnt, R, N, K, K, N)
+        for _ in range(3):
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[f"{R}x{K}x{N}"] = {"ms": ms, "Tproducts_per_s": R * K * N / (ms / 1e3) / 1e12}
+        del X, WT, y
+    res["note"] = (f"{props.multi_processor_count} SMs; proven-mode kernel, two outputs per 32-bit word; "
+                   "issue-bound on the INT pipes")
     return res
 
 
