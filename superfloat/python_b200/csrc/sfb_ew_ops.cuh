@@ -18,7 +18,8 @@
 namespace sfb {
 namespace ewops {
 
-// floor(ua 2^sh / ub) for 0 <= ua < ub < 2^15, sh <= 15 (the quotient is < 2^15).
+// floor(ua 2^sh / ub) for 0 <= ua <= ub < 2^15, ub >= 1, sh <= 15 (the
+// quotient is at most 2^sh, reached exactly when ua == ub).
 // Reciprocal estimate, then one exact integer correction:
 //   x = ua 2^sh / ub.  ua 2^sh and ub convert to float exactly with the
 //   exponent-bias trick (ua < 2^23 placed in the mantissa under exponent
@@ -26,8 +27,6 @@ namespace ewops {
 //   once, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding
 //   it to the nearest integer (the 1.5 * 2^23 bias) gives floor(x) or
 //   floor(x) + 1, and the sign of the remainder tells which.
-// Outside the precondition (ua >= ub) the result is meaningless but every
-// step stays defined (unsigned arithmetic); callers discard it there.
 __device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
     const float fa = __int_as_float(((150 + sh) << 23) | ua) - __int_as_float((150 + sh) << 23);
     const float fb = __int_as_float(0x4B000000 | ub) - 8388608.0f;
@@ -79,18 +78,19 @@ __device__ __forceinline__ int ew_one(int a, int b, int c, Width w0, int pow_n, 
         ev.under = small_nonzero(p, sh);
         return r;
     } else if constexpr (OP == SFB_OP_DIV) {
-        // branch-free: every lane computes the quotient (meaningless where
-        // |a| >= |b| or b == 0, and discarded there), then selects
-        const bool z = b == 0;
+        // One quotient path for every case: with the dividend clamped to
+        // the divisor (and a zero divisor taken as 1) the quotient is at most
+        // 2^sh, reached exactly when |a| >= |b| > 0 (overflow) or b == 0 with
+        // a != 0 (divide); min(q, M) with the sign of a b then gives +-M
+        // there, 0 for 0 / 0, and trunc(a S / b) everywhere else.
         const unsigned ua = (unsigned)abs(a), ub = (unsigned)abs(b);
-        const bool ov = !z && a != 0 && ua >= ub;
-        const unsigned q = udiv_small(ua, ub + z, sh);
+        const unsigned ub1 = max(ub, 1u);
+        const unsigned q = udiv_small(min(ua, ub1), ub1, sh);
         const int s = (a ^ b) >> 31;                 // -1 where the quotient is negative
-        const int sq = ((int)q ^ s) - s;
-        const int sat = a == 0 ? 0 : ((M ^ s) - s);  // +-M with the quotient's sign; 0/0 -> 0
-        ev.over = ov;
-        ev.div0 = z;
-        return (z || ov) ? sat : sq;
+        const int m = (int)min(q, (unsigned)M);
+        ev.over = (q >> sh) != 0 && b != 0;
+        ev.div0 = b == 0;
+        return (m ^ s) - s;
     } else if constexpr (OP == SFB_OP_NEG) {
         return -a;
     } else if constexpr (OP == SFB_OP_ABS) {
