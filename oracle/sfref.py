@@ -338,3 +338,168 @@ def t16_closed(am, wm):
     for i in range(6):
         C = C + ((x >> i) & 1) * ((y << i) & 63)
     return (am * wm + 80 - C) >> 8
+
+
+# --- the wide sft linear: exponents, guard, shift rule, bias after POP, redo ---------------
+# (src/sf/_heuristic.py:32-169, src/sf/torch/_core.py:55-99, :177-190, :463-600)
+
+WIDE_MARGIN = 2
+
+
+def h_for(K: int) -> int:
+    """Bits taken back below the L2 bound for dot length K (_heuristic.py:32-37)."""
+    K = int(K)
+    return 0 if K < 1 else max(0, (K.bit_length() - 1) // 2 - WIDE_MARGIN)
+
+
+def pow2_exp(m):
+    """Smallest integer e with m / 2^e < 1, 0 where m == 0 (_heuristic.py:40-48)."""
+    m = np.asarray(m, dtype=np.float64)
+    out = np.zeros(m.shape, np.int64)
+    nz = m > 0
+    out[nz] = np.frexp(m[nz])[1]
+    return out
+
+
+def _pow2_codes(bits, x, e):
+    M, S = consts(bits)
+    P = bits - 1
+    return np.clip(np.rint(np.ldexp(x, (P - e).astype(np.int64))), -M, M).astype(np.int64)
+
+
+def quantize_pow2(bits, x, axis=-1):
+    """One power-of-two exponent per slice: e = pow2_exp(max |x|), codes =
+    rint(x 2^(N-1-e)) clamped (_heuristic.py:51-66).  Returns (q, e, underflow)."""
+    x = np.asarray(x, dtype=np.float64)
+    mx = np.abs(x).max(axis=axis) if x.shape[axis] else np.zeros(np.delete(x.shape, axis))
+    e = pow2_exp(mx)
+    q = _pow2_codes(bits, x, np.expand_dims(e, axis))
+    return q, e, int(np.count_nonzero((q == 0) & (x != 0)))
+
+
+def code_norms(codes, axis):
+    """L2 norms of integer code vectors (exact sums of squares, _heuristic.py:69-72)."""
+    c = np.moveaxis(np.asarray(codes, dtype=np.float64), axis, -1)
+    return np.sqrt(np.einsum("...i,...i->...", c, c))
+
+
+def col_norm_max(bits, qb):
+    """Largest column norm of the block magnitudes of (K, N) codes (_heuristic.py:75-82)."""
+    bm = mx_mags(bits, qb).astype(np.float64)
+    return float(np.sqrt((bm * bm).sum(axis=-2)).max()) if bm.size else 0.0
+
+
+def acc_guard(bits, x, qa, ea, bmax, mx=MX_DEFAULT):
+    """Raise token exponents until the Cauchy-Schwarz bound of every
+    accumulator is below the unit's limit (_heuristic.py:85-120).
+    Returns (qa, ea, raised)."""
+    blk = mx_block(bits)
+    u = MX_UNITS[mx][blk]
+    hi = (1 << (u["W"] - 1)) - 1
+    K = qa.shape[-1]
+    raised = np.zeros(ea.shape, bool)
+    for _ in range(64):
+        am = mx_mags(bits, qa).astype(np.float64)
+        an = np.sqrt((am * am).sum(axis=-1))
+        prod = an * bmax
+        bound = (prod / float(1 << (30 - u["F"])) + K) if blk == 16 else prod
+        bad = bound * (1 + 1e-12) + 1 > hi
+        if not bad.any():
+            return qa, ea, int(np.count_nonzero(raised))
+        ea = np.where(bad, ea + 1, ea)
+        raised |= bad
+        qa = np.where(bad[:, None], _pow2_codes(bits, x, ea[:, None]), qa)
+    raise RuntimeError("accumulator guard did not converge")
+
+
+def wide_plan(bits, na, nb, ea, eb, K, bias_abs=None):
+    """Per output shift and redo shift (_heuristic.py:123-169) from the
+    dequantized row / column norms.  Returns (shift, shift_l2, h)."""
+    h = h_for(K)
+    prod = na[:, None] * nb[None, :]
+    l2 = pow2_exp(prod)
+    base = ea[:, None] + eb[None, :]
+    if bias_abs is None:
+        target = l2 - h
+    else:
+        ba = np.broadcast_to(np.asarray(bias_abs, dtype=np.float64), base.shape)
+        target = np.where(ba > 0, np.maximum(l2 - h, pow2_exp(ba)), l2 - h)
+    shift = np.clip(base - target, SHIFT_MIN, SHIFT_MAX)
+    l2_redo = l2 if bias_abs is None else pow2_exp(prod + np.asarray(bias_abs, dtype=np.float64))
+    return shift, np.clip(base - l2_redo, SHIFT_MIN, SHIFT_MAX), h
+
+
+def bias_codes(bits, b, fe):
+    """The bias at each output's exponent: rint(b 2^(N-1-fe)) clamped
+    (_core.py:182-190).  Returns (codes, clamped)."""
+    M, _ = consts(bits)
+    with np.errstate(over="ignore"):
+        raw = np.rint(np.ldexp(np.asarray(b, dtype=np.float64), (bits - 1 - fe).astype(np.int64)))
+    return np.clip(raw, -M, M).astype(np.int64), np.abs(raw) > M
+
+
+def wide_finish(bits, acc, F, base, shift, shift_redo, bias=None):
+    """POP at ``shift``, the bias added with the saturating add, and a second
+    POP at ``shift_redo`` where the code or the sum reached +-M or the bias
+    code clamped, on a nonzero output (_core.py:68-98, :162-179).
+    Returns (y codes, used shift, saturated, flushed, redo mask)."""
+    M, _ = consts(bits)
+    acc = _i64(acc)
+
+    def post(sh):
+        """(sum, pop overflow, pop underflow, add saturated, nonzero, pop codes) at shift ``sh``."""
+        q, over, under = wide_pop(bits, acc, sh, F)
+        if bias is None:
+            return q, over, under, np.zeros(q.shape, bool), acc != 0, q
+        bq, clamped = bias_codes(bits, np.broadcast_to(bias, q.shape), base - sh)
+        y, ev = add(bits, q, bq)
+        return y, over, under, ev["overflow"] | clamped, (acc != 0) | (bq != 0), q
+
+    y, over, under, add_sat, nz, q = post(shift)
+    used = np.broadcast_to(shift, acc.shape).copy()
+    redo = np.zeros(acc.shape, bool)
+    if shift_redo is not None:
+        redo = ((np.abs(q) >= M) | (np.abs(y) >= M) | add_sat) & nz
+        if redo.any():
+            y2, over2, under2, add_sat2, _, _ = post(shift_redo)
+            y = np.where(redo, y2, y)
+            add_sat = np.where(redo, add_sat2, add_sat)
+            over = np.where(redo, over2, over)
+            under = np.where(redo, under2, under)
+            used = np.where(redo, shift_redo, used)
+    return y, used, over | add_sat, under, redo
+
+
+def wide_linear(x, w, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
+    """y = x W^T + b on the MX engine with the wide rule (_core.py:463-600):
+    per-token and per-channel power-of-two exponents, the guard, the plan,
+    one accumulation, POP + bias + redo, float64 dequantization.  ``acc_fn``
+    replaces ``wide_acc`` (the C oracle).  Returns (y float64, status dict)."""
+    x = np.asarray(x, dtype=np.float64)
+    w = np.asarray(w, dtype=np.float64)
+    P = bits - 1
+    qa, ea, in_under = quantize_pow2(bits, x, -1)
+    qw, ew, w_under = quantize_pow2(bits, w, -1)
+    qb = qw.T
+    qa, ea, raised = acc_guard(bits, x, qa, ea, col_norm_max(bits, qb), mx)
+    base = ea[:, None] + ew[None, :]
+    bias = None if b is None else np.asarray(b, dtype=np.float64)
+    if shift is None:
+        na = code_norms(qa, -1) * np.ldexp(1.0, (ea - P).astype(np.int64))
+        nb = code_norms(qb, -2) * np.ldexp(1.0, (ew - P).astype(np.int64))
+        sh, sh_redo, h = wide_plan(bits, na, nb, ea, ew, x.shape[-1], None if bias is None else np.abs(bias))
+    else:
+        sh, sh_redo, h = np.full(base.shape, int(check_shift(shift))), None, None
+    acc, clipped, F = (acc_fn or wide_acc)(bits, qa, qb, mx)
+    y, used, sat, under, redo = wide_finish(bits, acc, F, base, sh, sh_redo, bias)
+    fe = base - used
+    with np.errstate(over="ignore"):
+        yf = np.ldexp(y.astype(np.float64), (fe - P).astype(np.int64))
+    bsat = 0 if bias is None else int(np.count_nonzero(bias_codes(bits, np.broadcast_to(bias, fe.shape), fe)[1]))
+    return yf, {"saturated": int(sat.sum()), "exact": True, "underflow": int(under.sum()),
+                "input_underflow": in_under, "weight_underflow": w_under, "bias_saturated": bsat,
+                "headroom_bits": 0.0, "outputs": int(y.size),
+                "act_scale": float(np.ldexp(1.0, int(ea.max()))) if ea.size else 1.0, "accumulate": "wide",
+                "shift_min": int(used.min()) if used.size else None,
+                "shift_max": int(used.max()) if used.size else None, "h": h, "redone": int(redo.sum()),
+                "flushed": int(under.sum()), "acc_clipped": int(clipped.sum()), "guard_raised": raised}
