@@ -195,6 +195,33 @@ SFB_API int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const in
                                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
                                     sfb_counts *counts, sfb_stream stream);
 
+/* The wide matmul's accumulators before POP: the reference's
+ * _linalg.matmul_wide_acc (src/sf/_linalg.py:261-308).  Same operands,
+ * strides and workspace as sfb_matmul_wide; acc[b * stride_acc + m * N + n]
+ * receives the W-bit accumulator (int32 on both chips), clipped (nullable)
+ * SFB_F_ACC_CLIPPED where it saturated; counts->acc_clipped adds those. */
+SFB_API int sfb_matmul_wide_acc(int bits, int mx, const int16_t *A, const int16_t *B, int32_t *acc,
+                                uint8_t *clipped, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_acc, void *workspace,
+                                int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
+
+/* The wide sft linear after accumulation, per output of an (M, N) block of
+ * accumulators (the reference's host runner, src/sf/torch/_core.py:68-98
+ * and :162-190, with the shift rule of src/sf/_heuristic.py:123-169):
+ * shift from the rule (use_rule = 1: row / column exponents, dequantized
+ * row / column L2 norms, h) or the one explicit shift (use_rule = 0, no
+ * redo); POP; the bias (N float64, nullable) at each output's exponent with
+ * the saturating add; the redo POP; y = code 2^(exponent - (N-1)) written as
+ * float32 (y32) and / or float64 (y64).  flags (nullable): SFB_F_OVERFLOW
+ * where the POP or the bias add saturated, SFB_F_UNDERFLOW where a nonzero
+ * total flushed to 0.  counts->overflow / underflow add those; stats (int64
+ * x 4) receives redone += , bias codes clamped += , and the min / max shift
+ * used by atomic min / max (start them at 127 and -128). */
+SFB_API int sfb_wide_finish(int bits, int mx, const int32_t *acc, int64_t M, int64_t N, const int32_t *row_exp,
+                            const int32_t *col_exp, const double *row_norm, const double *col_norm, int h,
+                            int use_rule, int shift, const double *bias, float *y32, double *y64, uint8_t *flags,
+                            int64_t *stats, sfb_counts *counts, sfb_stream stream);
+
 /* Exhaustive sweep of every operand pair of one width.  No counterpart in
  * the reference's Device API: the GPU form of its exhaustive check,
  * tools/exhaustive.py:146-181.  For op in SFB_OP_ADD / SUB / MUL / DIV and

@@ -470,24 +470,16 @@ def wide_finish(bits, acc, F, base, shift, shift_redo, bias=None):
     return y, used, over | add_sat, under, redo
 
 
-def wide_linear(x, w, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
-    """y = x W^T + b on the MX engine with the wide rule (_core.py:463-600):
-    per-token and per-channel power-of-two exponents, the guard, the plan,
-    one accumulation, POP + bias + redo, float64 dequantization.  ``acc_fn``
-    replaces ``wide_acc`` (the C oracle).  Returns (y float64, status dict)."""
-    x = np.asarray(x, dtype=np.float64)
-    w = np.asarray(w, dtype=np.float64)
+def _wide_core(bits, x, qa, ea, in_under, qb, eb, w_under, bias, shift, mx, acc_fn):
+    """Guard, plan, accumulation, finish and dequantization shared by the
+    linear and the activation matmul (_core.py:463-534)."""
     P = bits - 1
-    qa, ea, in_under = quantize_pow2(bits, x, -1)
-    qw, ew, w_under = quantize_pow2(bits, w, -1)
-    qb = qw.T
     qa, ea, raised = acc_guard(bits, x, qa, ea, col_norm_max(bits, qb), mx)
-    base = ea[:, None] + ew[None, :]
-    bias = None if b is None else np.asarray(b, dtype=np.float64)
+    base = ea[:, None] + eb[None, :]
     if shift is None:
         na = code_norms(qa, -1) * np.ldexp(1.0, (ea - P).astype(np.int64))
-        nb = code_norms(qb, -2) * np.ldexp(1.0, (ew - P).astype(np.int64))
-        sh, sh_redo, h = wide_plan(bits, na, nb, ea, ew, x.shape[-1], None if bias is None else np.abs(bias))
+        nb = code_norms(qb, -2) * np.ldexp(1.0, (eb - P).astype(np.int64))
+        sh, sh_redo, h = wide_plan(bits, na, nb, ea, eb, x.shape[-1], None if bias is None else np.abs(bias))
     else:
         sh, sh_redo, h = np.full(base.shape, int(check_shift(shift))), None, None
     acc, clipped, F = (acc_fn or wide_acc)(bits, qa, qb, mx)
@@ -503,3 +495,24 @@ def wide_linear(x, w, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
                 "shift_min": int(used.min()) if used.size else None,
                 "shift_max": int(used.max()) if used.size else None, "h": h, "redone": int(redo.sum()),
                 "flushed": int(under.sum()), "acc_clipped": int(clipped.sum()), "guard_raised": raised}
+
+
+def wide_linear(x, w, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
+    """y = x W^T + b on the MX engine with the wide rule (_core.py:569-600):
+    per-token and per-channel power-of-two exponents, the guard, the plan,
+    one accumulation, POP + bias + redo, float64 dequantization.  ``acc_fn``
+    replaces ``wide_acc`` (the C oracle).  Returns (y float64, status dict)."""
+    x = np.asarray(x, dtype=np.float64)
+    qa, ea, in_under = quantize_pow2(bits, x, -1)
+    qw, ew, w_under = quantize_pow2(bits, np.asarray(w, dtype=np.float64), -1)
+    bias = None if b is None else np.asarray(b, dtype=np.float64)
+    return _wide_core(bits, x, qa, ea, in_under, qw.T, ew, w_under, bias, shift, mx, acc_fn)
+
+
+def wide_matmul(a, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
+    """(M, K) @ (K, N) of two activations on the MX engine: one exponent per
+    row of a and per column of b (_core.py:537-557)."""
+    a = np.asarray(a, dtype=np.float64)
+    qa, ea, ua = quantize_pow2(bits, a, -1)
+    qb, eb, ub = quantize_pow2(bits, np.asarray(b, dtype=np.float64), -2)
+    return _wide_core(bits, a, qa, ea, ua + ub, qb, eb, 0, None, shift, mx, acc_fn)

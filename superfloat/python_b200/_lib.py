@@ -43,6 +43,10 @@ SIGNATURES = {
     "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
+    "sfb_matmul_wide_acc": (_i32, [_i32, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                   _i64, _p, _i64, _p, _p]),
+    "sfb_wide_finish": (_i32, [_i32, _i32, _p, _i64, _i64, _p, _p, _p, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p,
+                               _p, _p]),
 }
 
 _lib = None
@@ -177,6 +181,21 @@ def sweep(op, bits, a_lo, a_hi, row_codes, row_flags, counts, stream=None):
     rc = load().sfb_sweep(OPS[op], bits, a_lo, a_hi, _ptr(row_codes), _ptr(row_flags), _ptr(counts),
                           _stream(stream))
     check(rc, "sf sweep")
+
+
+def matmul_wide_acc(bits, mx, A, B, acc, clipped, counts, M, N, K, lda, ldb, workspace, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_matmul_wide_acc(bits, MX[mx], _ptr(A), _ptr(B), _ptr(acc), _ptr(clipped), 1, M, N, K, lda, ldb,
+                                    0, 0, M * N, _ptr(workspace), ws_bytes, _ptr(counts), _stream(stream))
+    check(rc, "sf matmul (wide accumulators)")
+
+
+def wide_finish(bits, mx, acc, M, N, row_exp, col_exp, row_norm, col_norm, h, use_rule, shift, bias, y32, y64,
+                flags, stats, counts, stream=None):
+    rc = load().sfb_wide_finish(bits, MX[mx], _ptr(acc), M, N, _ptr(row_exp), _ptr(col_exp), _ptr(row_norm),
+                                _ptr(col_norm), int(h), int(bool(use_rule)), int(shift), _ptr(bias), _ptr(y32),
+                                _ptr(y64), _ptr(flags), _ptr(stats), _ptr(counts), _stream(stream))
+    check(rc, "sf wide finish")
 
 
 def matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so,

@@ -16,7 +16,8 @@ namespace sfb {
 int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
                 int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
                 int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn,
-                void *ws, int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled);
+                void *ws, int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled,
+                int32_t *acc_out = nullptr);
 int64_t wide_tc_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K);
 
 namespace {
@@ -29,7 +30,8 @@ __global__ void __launch_bounds__(THREADS) wide_simt_kernel(const int16_t *__res
                                                            int16_t *__restrict__ out, uint8_t *__restrict__ flags,
                                                            int M, int N, int K, int64_t lda, int64_t ldb, int64_t sa,
                                                            int64_t sb, int64_t so, int64_t ssb, int64_t ssm,
-                                                           int64_t ssn, Width w, MxUnit u, sfb_counts *counts) {
+                                                           int64_t ssn, Width w, MxUnit u, sfb_counts *counts,
+                                                           int32_t *__restrict__ acc_out) {
     __shared__ int4 As4[BK][BM / 4];  // signed magnitudes: sign(code) * mag
     __shared__ int4 Bs4[BK][BN / 4];
     __shared__ unsigned sc[5];
@@ -42,7 +44,8 @@ __global__ void __launch_bounds__(THREADS) wide_simt_kernel(const int16_t *__res
     const int64_t z = blockIdx.z;
     A += z * sa;
     B += z * sb;
-    out += z * so;
+    if (out) out += z * so;
+    if (acc_out) acc_out += z * so;
     if (flags) flags += z * so;
     const long long lo = -(1ll << (u.W - 1)), hi = (1ll << (u.W - 1)) - 1;
 
@@ -115,7 +118,12 @@ __global__ void __launch_bounds__(THREADS) wide_simt_kernel(const int16_t *__res
 #pragma unroll
         for (int j = 0; j < TN; j++) {
             const int gn = n0 + tx * TN + j;
-            if (gm < M && gn < N) {
+            if (gm < M && gn < N && acc_out) {          // the accumulator itself, no POP
+                const bool cl = clip[i][j] != 0;
+                acc_out[(int64_t)gm * N + gn] = acc[i][j];
+                if (flags) flags[(int64_t)gm * N + gn] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
+                cnt.clip += cl;
+            } else if (gm < M && gn < N) {
                 const int sft = shift_arr ? (int)shift_arr[z * ssb + (int64_t)gm * ssm + (int64_t)gn * ssn] : shift;
                 bool over, under;
                 const int q = mx_pop(acc[i][j], sft, u.F, w, over, under);
@@ -140,7 +148,7 @@ __global__ void __launch_bounds__(THREADS) wide_simt_kernel(const int16_t *__res
 int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
               int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
               int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn,
-              sfb_counts *counts, cudaStream_t st) {
+              sfb_counts *counts, cudaStream_t st, int32_t *acc_out) {
     const int64_t mt = (M + BM - 1) / BM, nt = (N + BN - 1) / BN;
     if (mt > 65535 || nt > 0x7fffffff || batch > 65535 || K > 0x7fffffff || M > 0x7fffffff || N > 0x7fffffff)
         return set_error(SFB_ERANGE, "sfb_matmul_wide: %lld x %lld x %lld (batch %lld) exceeds the launch limits",
@@ -151,10 +159,11 @@ int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t
     const Width w = width(bits);
     if (blk16)
         wide_simt_kernel<true><<<grid, THREADS, 0, st>>>(A, B, shift_arr, shift, out, flags, (int)M, (int)N, (int)K,
-                                                         lda, ldb, sa, sb, so, ssb, ssm, ssn, w, u, counts);
+                                                         lda, ldb, sa, sb, so, ssb, ssm, ssn, w, u, counts, acc_out);
     else
         wide_simt_kernel<false><<<grid, THREADS, 0, st>>>(A, B, shift_arr, shift, out, flags, (int)M, (int)N,
-                                                          (int)K, lda, ldb, sa, sb, so, ssb, ssm, ssn, w, u, counts);
+                                                          (int)K, lda, ldb, sa, sb, so, ssb, ssm, ssn, w, u, counts,
+                                                          acc_out);
     return check_launch("sfb_matmul_wide");
 }
 
@@ -190,5 +199,29 @@ extern "C" int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t
                                st, &handled);
     if (rc != SFB_OK || handled) return rc;
     return wide_simt(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a, stride_b,
-                     stride_out, shift_sb, shift_sm, shift_sn, counts, st);
+                     stride_out, shift_sb, shift_sm, shift_sn, counts, st, nullptr);
+}
+
+extern "C" int sfb_matmul_wide_acc(int bits, int mx, const int16_t *A, const int16_t *B, int32_t *acc,
+                                   uint8_t *clipped, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                   int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_acc,
+                                   void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: width %d is not 4..16", bits);
+    if (mx != SFB_MX_V492 && mx != SFB_MX_V481)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: unknown mx %d", mx);
+    if (batch < 0 || M < 0 || N < 0 || K < 0) return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: negative size");
+    if (batch == 0 || M == 0 || N == 0) return SFB_OK;
+    if (acc == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: null operand or output");
+    if (K > 0 && (lda < K || ldb < N)) return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: lda < K or ldb < N");
+    if (stride_acc < M * N && batch > 1)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_acc: output batch entries overlap");
+    cudaStream_t st = (cudaStream_t)stream;
+    bool handled = false;
+    const int rc = wide_tc_try(bits, mx, A, B, nullptr, 0, nullptr, clipped, batch, M, N, K, lda, ldb, stride_a,
+                               stride_b, stride_acc, 0, 0, 0, workspace, workspace_bytes, counts, st, &handled, acc);
+    if (rc != SFB_OK || handled) return rc;
+    return wide_simt(bits, mx, A, B, nullptr, 0, nullptr, clipped, batch, M, N, K, lda, ldb, stride_a, stride_b,
+                     stride_acc, 0, 0, 0, counts, st, acc);
 }

@@ -44,7 +44,7 @@ namespace sfb {
 int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
               int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
               int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn,
-              sfb_counts *counts, cudaStream_t st);
+              sfb_counts *counts, cudaStream_t st, int32_t *acc_out);
 
 namespace {
 
@@ -342,6 +342,7 @@ struct RemIn {
     int shift;
     int64_t ssm, ssn;
     int16_t *out;
+    int32_t *acc_out;     // set: store the accumulator instead of POP
     uint8_t *flags;
     Width w;
     MxUnit u;
@@ -444,6 +445,12 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
                 const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
                 bool cl = false;
                 if (!safe) S = exact_output(in, m, n, cl);
+                if (in.acc_out) {
+                    in.acc_out[(int64_t)m * in.N + n] = (int32_t)S;
+                    if (in.flags) in.flags[(int64_t)m * in.N + n] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
+                    cnt.clip += cl;
+                    continue;
+                }
                 const int sft = in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
                 bool over, under;
                 const int q = mx_pop(S, sft, in.u.F, in.w, over, under);
@@ -545,7 +552,7 @@ int64_t wide_tc_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N,
 int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
                 int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
                 int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn, void *ws,
-                int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled) {
+                int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled, int32_t *acc_out) {
     *handled = false;
     if (!eligible(bits, mx, M, N, K)) return SFB_OK;
     const Layout L = layout_for(M, N, K);
@@ -609,7 +616,8 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.shift = shift;
         in.ssm = ssm;
         in.ssn = ssn;
-        in.out = out + z * so;
+        in.out = out ? out + z * so : nullptr;
+        in.acc_out = acc_out ? acc_out + z * so : nullptr;
         in.flags = flags ? flags + z * so : nullptr;
         in.w = w;
         in.u = mx_unit(mx, true);

@@ -15,7 +15,7 @@ from dataclasses import dataclass, field
 import torch
 from torch._dynamo import register_backend
 
-from ._ops import SF_OP_ARGS, SF_OPS, linear_impl, matmul_impl
+from ._ops import SF_OP_ARGS, SF_OPS, linear_impl, linear_wide_impl, matmul_impl, matmul_wide_impl
 
 _UNCONVERTED = {"linear", "matmul", "mm", "bmm", "conv2d", "conv1d", "conv3d", "addmm", "baddbmm", "einsum",
                 "__matmul__", "scaled_dot_product_attention"}
@@ -87,6 +87,22 @@ def _device_matmul(device):
     return run
 
 
+def _device_linear_wide(device):
+    def run(x, weight, bias, bits, shift, name):
+        _require_no_grad(x, weight, bias)
+        return linear_wide_impl(x, weight, bias, bits, shift, name)
+    run.__name__ = f"sf_linear_wide_on_{device}"
+    return run
+
+
+def _device_matmul_wide(device):
+    def run(a, b, bits, shift, name):
+        _require_no_grad(a, b)
+        return matmul_wide_impl(a, b, bits, shift, name)
+    run.__name__ = f"sf_matmul_wide_on_{device}"
+    return run
+
+
 def _arg(node, i, key):
     return node.args[i] if len(node.args) > i else node.kwargs.get(key)
 
@@ -102,7 +118,8 @@ def superfloat(gm: torch.fx.GraphModule, example_inputs, **kwargs):
     from .._device import get_device
     dev = get_device(_config.get("default_device"))
     report = GraphReport()
-    impl = {"linear": _device_linear(dev.name), "matmul": _device_matmul(dev.name)}
+    impl = {"linear": _device_linear(dev.name), "matmul": _device_matmul(dev.name),
+            "linear_wide": _device_linear_wide(dev.name), "matmul_wide": _device_matmul_wide(dev.name)}
     for node in gm.graph.nodes:
         if node.op not in ("call_function", "call_method", "call_module"):
             continue

@@ -38,8 +38,13 @@ class SFConfig:
 
     def __post_init__(self):
         _core.check_args(self.bits, self.scale, self.headroom, self.accumulate)
-        if self.shift is not None and self.accumulate != "wide":
-            raise ValueError("shift= only applies to accumulate=\"wide\"")
+        if self.shift is not None:
+            if self.accumulate != "wide":
+                raise ValueError("shift= only applies to accumulate=\"wide\"")
+            if isinstance(self.shift, bool) or not isinstance(self.shift, int):
+                raise TypeError(f"shift must be an int, got {type(self.shift).__name__}")
+            if not -32 <= self.shift <= 31:
+                raise ValueError(f"shift must be between -32 and 31, got {self.shift}")
 
     @property
     def dtype_name(self) -> str:
@@ -231,16 +236,25 @@ def _custom_forward(m, base) -> bool:
 
 
 def convert(model: nn.Module, dtype="sf16", scale: str = "per_tensor", headroom: str = "bound",
-            inplace: bool = False, *, accumulate: str = "chain", shift=None, keep_sf16="auto",
+            inplace: bool = False, *, accumulate: str = "chain", shift=None, calibration: str = "heuristic",
+            keep_sf16="auto", attention="auto", nonlinear: str = "float",
             widths: dict | None = None) -> nn.Module:
     """Swap ``nn.Linear``, ``nn.Conv2d`` and Hugging Face ``Conv1D`` for SF
     layers (src/sf/torch/_modules.py:295-537).  ``keep_sf16`` ("auto": the LM
     head; False; or module names) keeps layers at sf16 when ``dtype`` is
     narrower; ``widths`` ({name: dtype}) gives layers their own width."""
-    if accumulate == "wide":
+    if calibration not in ("heuristic",):
+        raise ValueError(f"calibration must be 'heuristic', got {calibration!r}")
+    if attention not in ("auto", False, None):
+        raise ValueError(f"attention must be \"auto\" or False, got {attention!r}")
+    if nonlinear != "float":
         from .._errors import SFUnsupportedError
-        raise SFUnsupportedError("convert(accumulate=\"wide\") is not available in this package yet; "
-                                 "the chain accumulation (the default) is")
+        raise SFUnsupportedError("nonlinear must be \"float\" here: the integer non-linear ops are not built")
+    if accumulate == "wide" and attention == "auto":
+        from .._errors import SFUnsupportedError
+        raise SFUnsupportedError("accumulate=\"wide\" with attention=\"auto\" runs scaled-dot-product attention "
+                                 "on the MX engine, which is not built here; pass attention=False to keep "
+                                 "attention in float (the layers still run wide)")
     cfg = SFConfig(_bits_of(dtype), scale, headroom, accumulate, shift)
     if not inplace:
         model = copy.deepcopy(model)

@@ -6,7 +6,11 @@ the reference's (src/sf/torch/_ops.py:184-417):
 * ``sf::linear(x, weight, bias, bits, wscale, headroom, name)``: the SF linear
   with the scale policy;
 * ``sf::matmul(a, b, bits, headroom, name)``: the SF matmul of two
-  activations.
+  activations;
+* ``sf::linear_wide(x, weight, bias, bits, shift, name)`` and
+  ``sf::matmul_wide(a, b, bits, shift, name)``: the same on the MX engine
+  (``accumulate="wide"``) with the wide-mode shift rule; ``shift`` (an int)
+  overrides it (src/sf/torch/_ops.py:305-365).
 
 Each op is one opaque node in a ``torch.compile`` graph (what lets the
 ``superfloat`` backend find it).  Both eager execution and the compiled graph
@@ -22,7 +26,7 @@ from typing import Optional
 
 import torch
 
-from . import _core
+from . import _core, _wide
 from ._status import SFLayerStatus, record
 
 if hasattr(torch.ops, "sf") and hasattr(torch.ops.sf, "linear"):
@@ -66,6 +70,30 @@ def matmul_impl(a, b, bits, headroom, name):
     r = _core.matmul(a, b, bits, headroom, dev)
     _record(name, "matmul", dev.name, bits, r)
     return r.y.to(device=a.device, dtype=out_dtype(torch.promote_types(a.dtype, b.dtype)))
+
+
+def linear_wide_impl(x, weight, bias, bits, shift, name):
+    K, N = weight.shape[1], weight.shape[0]
+    if x.shape[-1] != K:
+        raise ValueError(f"sf.linear: input has {x.shape[-1]} features, weight expects {K}")
+    dev = _core.target()
+    lead = x.shape[:-1]
+    od = out_dtype(x.dtype)
+    r = _wide.wide_linear(x.reshape(-1, K), weight, bias, bits, shift, dev, out_dtype=od)
+    _record(name, "linear", dev.name, bits, r)
+    return r.y.reshape(*lead, N).to(device=x.device, dtype=od)
+
+
+def matmul_wide_impl(a, b, bits, shift, name):
+    if a.dim() < 2 or b.dim() < 2:
+        raise ValueError("sf.matmul expects operands with at least 2 dimensions")
+    if a.shape[-1] != b.shape[-2]:
+        raise ValueError(f"sf.matmul: shapes {tuple(a.shape)} and {tuple(b.shape)} are not aligned")
+    dev = _core.target()
+    od = out_dtype(torch.promote_types(a.dtype, b.dtype))
+    r = _wide.wide_matmul(a, b, bits, shift, dev, out_dtype=od)
+    _record(name, "matmul", dev.name, bits, r)
+    return r.y.to(device=a.device, dtype=od)
 
 
 # --- sf::quantize -------------------------------------------------------------------------
@@ -187,22 +215,79 @@ def _matmul_backward(ctx, g):
 torch.library.register_autograd("sf::matmul", _matmul_backward, setup_context=_matmul_setup)
 
 
+# --- wide mode: sf::linear_wide, sf::matmul_wide ----------------------------------------------
+
+@torch.library.custom_op("sf::linear_wide", mutates_args=())
+def linear_wide(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], bits: int,
+                shift: Optional[int], name: str) -> torch.Tensor:
+    return linear_wide_impl(x, weight, bias, bits, shift, name)
+
+
+@linear_wide.register_fake
+def _(x, weight, bias, bits, shift, name):
+    return x.new_empty(tuple(x.shape[:-1]) + (weight.shape[0],), dtype=out_dtype(x.dtype))
+
+
+def _linear_wide_setup(ctx, inputs, output):
+    x, weight, bias, bits, shift, name = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.has_bias = bias is not None
+    ctx.bits = bits
+
+
+def _linear_wide_backward(ctx, g):
+    """Straight-through: the gradient of x @ W_q^T + b with W_q the weights as
+    wide mode quantizes them, one power-of-two exponent per output channel
+    (src/sf/torch/_ops.py:325-339)."""
+    x, weight = ctx.saved_tensors
+    from .._format import FORMATS
+    fmt = FORMATS[ctx.bits]
+    w = weight.detach().to(torch.float64)
+    if not w.is_cuda:
+        w = w.to(_core.target().torch_device)
+    e = _wide.row_exponents(w)
+    qw, _ = _wide.quantize_rows(fmt, w.contiguous(), e)
+    w_q = (qw.to(torch.float64) * _wide.exp2(e - (fmt.bits - 1))[:, None]).to(device=g.device, dtype=g.dtype)
+    g2 = g.reshape(-1, g.shape[-1])
+    x2 = x.detach().reshape(-1, x.shape[-1]).to(g.dtype)
+    grad_x = (g2 @ w_q).reshape(x.shape).to(x.dtype) if ctx.needs_input_grad[0] else None
+    grad_w = (g2.T @ x2).to(weight.dtype) if ctx.needs_input_grad[1] else None
+    grad_b = g2.sum(0).to(weight.dtype) if (ctx.has_bias and ctx.needs_input_grad[2]) else None
+    return grad_x, grad_w, grad_b, None, None, None
+
+
+torch.library.register_autograd("sf::linear_wide", _linear_wide_backward, setup_context=_linear_wide_setup)
+
+
+@torch.library.custom_op("sf::matmul_wide", mutates_args=())
+def matmul_wide(a: torch.Tensor, b: torch.Tensor, bits: int, shift: Optional[int], name: str) -> torch.Tensor:
+    return matmul_wide_impl(a, b, bits, shift, name)
+
+
+@matmul_wide.register_fake
+def _(a, b, bits, shift, name):
+    batch = torch.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    return a.new_empty(tuple(batch) + (a.shape[-2], b.shape[-1]),
+                       dtype=out_dtype(torch.promote_types(a.dtype, b.dtype)))
+
+
+torch.library.register_autograd("sf::matmul_wide", lambda ctx, g: _matmul_backward(ctx, g)[:2] + (None, None, None),
+                                setup_context=lambda ctx, inputs, output: ctx.save_for_backward(inputs[0], inputs[1]))
+
+
 def call_linear(x, weight, bias, cfg, name):
     if cfg.accumulate == "wide":
-        from .._errors import SFUnsupportedError
-        raise SFUnsupportedError("accumulate=\"wide\" layers (sf::linear_wide) are not available in this "
-                                 "package yet; convert with the default accumulate=\"chain\"")
+        return torch.ops.sf.linear_wide(x, weight, bias, cfg.bits, cfg.shift, name)
     return torch.ops.sf.linear(x, weight, bias, cfg.bits, cfg.scale, cfg.headroom, name)
 
 
 def call_matmul(a, b, cfg, name):
     if cfg.accumulate == "wide":
-        from .._errors import SFUnsupportedError
-        raise SFUnsupportedError("accumulate=\"wide\" matmuls (sf::matmul_wide) are not available in this "
-                                 "package yet")
+        return torch.ops.sf.matmul_wide(a, b, cfg.bits, cfg.shift, name)
     return torch.ops.sf.matmul(a, b, cfg.bits, cfg.headroom, name)
 
 
 SF_OPS = {"sf.linear": "linear", "sf.linear.default": "linear", "sf.matmul": "matmul",
-          "sf.matmul.default": "matmul"}
-SF_OP_ARGS = {"linear": (3, 6), "matmul": (2, 4)}      # (bits, name) argument positions
+          "sf.matmul.default": "matmul", "sf.linear_wide": "linear_wide", "sf.linear_wide.default": "linear_wide",
+          "sf.matmul_wide": "matmul_wide", "sf.matmul_wide.default": "matmul_wide"}
+SF_OP_ARGS = {"linear": (3, 6), "matmul": (2, 4), "linear_wide": (3, 5), "matmul_wide": (2, 4)}

@@ -14,8 +14,9 @@ Three parts:
    at the l2 exponent, bias codes clamped, POP flushes, an explicit shift,
    zero rows / columns, sf16 / sf12 / sf8 / sf4 and both MX chips;
 3. GPT-2-small (12 layers, d_model 768, FFN 3072, vocab 50257; random init,
-   torch.manual_seed(0)) converted with ``accumulate="wide"`` on one sequence
-   of 8 token ids: every SF layer's status, its output hash, the inputs and
+   torch.manual_seed(0)) converted with ``accumulate="wide"`` and
+   ``attention=False`` (scaled-dot-product attention stays in float) on one
+   sequence of 8 token ids: every SF layer's status, its output hash, the inputs and
    outputs of the first block's layers, and the logits hash.
 """
 from __future__ import annotations
@@ -117,7 +118,7 @@ def main(ref: str = "/root/reference") -> None:
     torch.manual_seed(0)
     cfg = GPT2Config(n_layer=12, n_embd=768, n_head=12, n_inner=3072, vocab_size=50257, n_positions=1024)
     gpt = GPT2LMHeadModel(cfg).eval()
-    conv = sft.convert(gpt, dtype="sf16", accumulate="wide")
+    conv = sft.convert(gpt, dtype="sf16", accumulate="wide", attention=False)
     ids = torch.randint(0, 50257, (1, 8), generator=torch.Generator().manual_seed(0))
     recs = []
     hooks = [m.register_forward_hook(lambda mod, inp, out: recs.append((mod.sf_name, inp[0].detach().clone(),

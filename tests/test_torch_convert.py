@@ -76,8 +76,12 @@ def test_config_validation():
         sft.SFConfig(3)
     with pytest.raises(ValueError):
         sft.SFConfig(16, shift=2)
-    with pytest.raises(sf.SFUnsupportedError):
+    with pytest.raises(ValueError):
+        sft.SFConfig(16, accumulate="wide", shift=40)
+    c = sft.convert(Net(), accumulate="wide", shift=-3, attention=False)
+    with pytest.raises(sf.SFUnsupportedError, match="attention=False"):
         sft.convert(Net(), accumulate="wide")
+    assert c.fc.sf.accumulate == "wide" and c.fc.sf.shift == -3
 
 
 def test_lm_head_rules():
