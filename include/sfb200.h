@@ -222,6 +222,25 @@ SFB_API int sfb_wide_finish(int bits, int mx, const int32_t *acc, int64_t M, int
                             int use_rule, int shift, const double *bias, float *y32, double *y64, uint8_t *flags,
                             int64_t *stats, sfb_counts *counts, sfb_stream stream);
 
+/* Saturating sequential sum along one axis of int16 codes viewed as
+ * (outer, K, inner), reduced over K from index 0: the reference's
+ * _linalg.sum_codes (src/sf/_linalg.py:30-39), the Device "sum" op
+ * (src/sf/_device.py:176-178).  out (outer * inner codes), flags (nullable):
+ * SFB_F_OVERFLOW where some step saturated; counts->overflow adds those.
+ * Computed as an ordered parallel reduction of clamp-add maps, the
+ * sequential chain's bits.  inner == 1 with few outputs splits each K
+ * across CTAs and needs sfb_reduce_workspace(outer, K) bytes of workspace
+ * (0: none). */
+SFB_API int64_t sfb_reduce_workspace(int64_t outputs, int64_t K);
+SFB_API int sfb_sum(int bits, const int16_t *x, int64_t outer, int64_t K, int64_t inner, int16_t *out,
+                    uint8_t *flags, void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
+
+/* 1-D dot as the reference's chain of fma (src/sf/_linalg.py:42-58): one
+ * code to out[0]; flags[0] (nullable) SFB_F_OVERFLOW / SFB_F_UNDERFLOW;
+ * workspace as sfb_reduce_workspace(1, n). */
+SFB_API int sfb_dot(int bits, const int16_t *a, const int16_t *b, int64_t n, int16_t *out, uint8_t *flags,
+                    void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
+
 /* Exhaustive sweep of every operand pair of one width.  No counterpart in
  * the reference's Device API: the GPU form of its exhaustive check,
  * tools/exhaustive.py:146-181.  For op in SFB_OP_ADD / SUB / MUL / DIV and

@@ -28,7 +28,7 @@ from ._format import FORMATS, SFFormat
 from ._status import SFStatus
 
 _SYM = {"add": "+", "sub": "-", "mul": "*", "div": "/", "fma": "fma", "neg": "-", "abs": "abs",
-        "sqrt": "sqrt", "pow": "**", "matmul": "@", "matmul_wide": "@ (wide)"}
+        "sqrt": "sqrt", "pow": "**", "matmul": "@", "matmul_wide": "@ (wide)", "sum": "sum"}
 _EVENT_ORDER = ("invalid", "divide", "overflow", "underflow")
 _CAN_UNDERFLOW = ("mul", "fma", "matmul", "matmul_wide", "pow")
 _COUNT_INDEX = {"overflow": 0, "underflow": 1, "divide": 2, "invalid": 3}
@@ -259,6 +259,9 @@ class SFArray:
     def __neg__(self): return _elementwise("neg", self)
     def __pos__(self): return self
     def __abs__(self): return _elementwise("abs", self)
+    def sum(self, axis=None):
+        return sum_(self, axis)
+
     def __matmul__(self, o): return matmul(self, o)
     def __rmatmul__(self, o): return matmul(o, self)
 
@@ -501,6 +504,29 @@ def dot(a, b, *, accumulate=None, shift=None):
     if a.ndim == 1 and b.ndim == 1 and a.shape != b.shape:
         raise SFShapeError(f"sf.dot: shapes {a.shape} and {b.shape} differ")
     return matmul(a, b, accumulate=accumulate, shift=shift)
+
+
+def sum_(x, axis=None):
+    """Saturating sum along ``axis`` (every element when None), index 0 first:
+    the reference's sequential order (src/sf/_array.py:636-656)."""
+    x = _as_sfarray(x, "sum")
+    fmt = FORMATS[x.dtype.bits]
+    codes = x.codes
+    if axis is None:
+        codes, axis = codes.reshape(-1), 0
+    elif axis < 0:
+        axis += codes.ndim
+    if not 0 <= axis < codes.ndim:
+        raise SFShapeError(f"axis {axis} is out of bounds for an array of dimension {codes.ndim}")
+    out_shape = codes.shape[:axis] + codes.shape[axis + 1:]
+    kw = {"axis": axis}
+    if x.device == HOST and not _should_offload(codes.size, "sum", fmt):
+        dev = get_device(_config.get("default_device"))
+        res, counts = _launch(dev, "sum", fmt, [codes], out_shape, kw)
+        _handle_events(counts, fmt, "sum", int(np.prod(out_shape)) if out_shape else 1)
+        return SFArray._wrap(res, x.dtype)
+    target = x.device if x.device != HOST else _config.get("default_device")
+    return _run_heavy("sum", fmt, x.dtype, target, [codes], out_shape, kw)
 
 
 def addmm(a, b, d, *, accumulate=None, shift=None):

@@ -34,12 +34,12 @@ HOST = "host"
 OP_EVENTS = {
     "add": ("overflow",), "sub": ("overflow",), "mul": ("underflow",), "div": ("overflow", "divide"),
     "fma": ("overflow", "underflow"), "neg": (), "abs": (), "sqrt": ("invalid",), "pow": ("underflow",),
-    "matmul": ("overflow", "underflow"), "matmul_wide": ("overflow", "underflow"),
+    "matmul": ("overflow", "underflow"), "matmul_wide": ("overflow", "underflow"), "sum": ("overflow",),
 }
 _EVENT_BIT = {"overflow": _lib.F_OVERFLOW, "underflow": _lib.F_UNDERFLOW, "divide": _lib.F_DIVIDE,
               "invalid": _lib.F_INVALID}
 ARITY = {"add": 2, "sub": 2, "mul": 2, "div": 2, "fma": 3, "neg": 1, "abs": 1, "sqrt": 1, "pow": 1,
-         "matmul": 2, "matmul_wide": 2}
+         "matmul": 2, "matmul_wide": 2, "sum": 1}
 
 
 class Device:
@@ -101,7 +101,7 @@ class B200Device(Device):
     max_elements = 1 << 34
     mx = "v4.9.2"
     supported_ops = frozenset({"add", "sub", "mul", "div", "fma", "neg", "abs", "sqrt", "pow",
-                               "matmul", "matmul_wide"})
+                               "matmul", "matmul_wide", "sum"})
 
     def __init__(self, index: int = 0, *, mx=None, name=None):
         if mx is not None:
@@ -158,6 +158,8 @@ class B200Device(Device):
         bits = fmt.bits
         if op in ("matmul", "matmul_wide"):
             return self._matmul_device(op, fmt, xs[0], xs[1], flags, cnt, out, stream, **kw)
+        if op == "sum":
+            return self._sum_device(fmt, xs[0], _axis(kw.get("axis", 0), xs[0].dim()), flags, cnt, out, stream)
         shape = torch.broadcast_shapes(*(x.shape for x in xs))
         xs = [x if (tuple(x.shape) == tuple(shape) and x.is_contiguous()) else x.expand(shape).contiguous()
               for x in xs]
@@ -184,7 +186,12 @@ class B200Device(Device):
         o = out if out is not None else torch.empty(tuple(batch_shape) + (M, N), dtype=torch.int16,
                                                     device=A.device)
         fl = torch.empty(tuple(batch_shape) + (M, N), dtype=torch.uint8, device=A.device) if flags else None
-        if op == "matmul":
+        if op == "matmul" and nb == 1 and M == 1 and N == 1 and bias is None and K > 0:
+            # one chain: the ordered parallel reduction (same bits as the chain kernel)
+            a1, b1 = A3.reshape(K).contiguous(), B3.reshape(K).contiguous()
+            ws = self.workspace(_lib.reduce_workspace(1, K))
+            _lib.dot(fmt.bits, a1, b1, K, o, fl, ws, cnt, stream=stream)
+        elif op == "matmul":
             _lib.matmul_chain(fmt.bits, A3, B3, bias, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
                               sa, sb, M * N, stream=stream)
         else:
@@ -203,6 +210,21 @@ class B200Device(Device):
             ws = self.workspace(_lib.wide_workspace(fmt.bits, mxv, nb, M, N, K))
             _lib.matmul_wide(fmt.bits, mxv, A3, B3, sh_t, sh_int, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
                              sa, sb, M * N, ss[0], ss[1], ss[2], ws, stream=stream)
+        return o, cnt, fl
+
+    def _sum_device(self, fmt, X, axis, flags, cnt, out, stream):
+        """Saturating sequential sum of int16 codes along ``axis``."""
+        torch = _torch()
+        X = X.contiguous()
+        shape = tuple(X.shape)
+        K = shape[axis]
+        outer = int(np.prod(shape[:axis])) if axis else 1
+        inner = int(np.prod(shape[axis + 1:])) if axis + 1 < len(shape) else 1
+        oshape = shape[:axis] + shape[axis + 1:]
+        o = out if out is not None else torch.empty(oshape, dtype=torch.int16, device=X.device)
+        fl = torch.empty(oshape, dtype=torch.uint8, device=X.device) if flags else None
+        ws = self.workspace(_lib.reduce_workspace(outer, K) if inner == 1 else 0)
+        _lib.sum_codes(fmt.bits, X, outer, K, inner, o, fl, ws, cnt, stream=stream)
         return o, cnt, fl
 
     # --- the reference's plug-in contract --------------------------------------------------
@@ -224,6 +246,10 @@ class B200Device(Device):
         if op in ("matmul", "matmul_wide"):
             out_shape = np.broadcast_shapes(ops[0].shape[:-2], ops[1].shape[:-2]) + (ops[0].shape[-2],
                                                                                        ops[1].shape[-1])
+        elif op == "sum":
+            axis = _axis(kw.get("axis", 0), ops[0].ndim)
+            kw = {"axis": axis}
+            out_shape = ops[0].shape[:axis] + ops[0].shape[axis + 1:]
         else:
             out_shape = np.broadcast_shapes(*(o.shape for o in ops))
         if int(np.prod(out_shape)) == 0:
@@ -238,6 +264,15 @@ class B200Device(Device):
         fl = fl.cpu().numpy()
         masks = {e: (fl & _EVENT_BIT[e]) != 0 for e in OP_EVENTS[op]}
         return codes, masks
+
+
+def _axis(axis, ndim) -> int:
+    a = int(axis)
+    if a < 0:
+        a += ndim
+    if not 0 <= a < max(ndim, 1):
+        raise SFShapeError(f"axis {axis} is out of bounds for an array of dimension {ndim}")
+    return a
 
 
 def _ld(T):

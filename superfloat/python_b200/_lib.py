@@ -43,6 +43,9 @@ SIGNATURES = {
     "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
+    "sfb_reduce_workspace": (_i64, [_i64, _i64]),
+    "sfb_sum": (_i32, [_i32, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p]),
+    "sfb_dot": (_i32, [_i32, _p, _p, _i64, _p, _p, _p, _i64, _p, _p]),
     "sfb_matmul_wide_acc": (_i32, [_i32, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                    _i64, _p, _i64, _p, _p]),
     "sfb_wide_finish": (_i32, [_i32, _i32, _p, _i64, _i64, _p, _p, _p, _p, _i32, _i32, _i32, _p, _p, _p, _p, _p,
@@ -173,6 +176,27 @@ def wide_workspace(bits, mx, batch, M, N, K) -> int:
     if n < 0:
         check(int(n), "sf matmul (wide) workspace")
     return int(n)
+
+
+def reduce_workspace(outputs, K) -> int:
+    n = load().sfb_reduce_workspace(outputs, K)
+    if n < 0:
+        check(int(n), "sf reduction workspace")
+    return int(n)
+
+
+def sum_codes(bits, x, outer, K, inner, out, flags, workspace, counts, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_sum(bits, _ptr(x), outer, K, inner, _ptr(out), _ptr(flags), _ptr(workspace), ws_bytes,
+                        _ptr(counts), _stream(stream))
+    check(rc, "sf sum")
+
+
+def dot(bits, a, b, n, out, flags, workspace, counts, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_dot(bits, _ptr(a), _ptr(b), n, _ptr(out), _ptr(flags), _ptr(workspace), ws_bytes,
+                        _ptr(counts), _stream(stream))
+    check(rc, "sf dot")
 
 
 def sweep(op, bits, a_lo, a_hi, row_codes, row_flags, counts, stream=None):

@@ -115,6 +115,12 @@ def check(op, fmt: SFFormat, *ops, **kw) -> Verdict:
         if chain_bound(fmt, ops[0], ops[1]) <= M:
             return Verdict("safe", "L1 bound: no partial sum can exceed max", ev)
         return Verdict("unknown", "", ev)
+    if op == "sum":                                 # src/sf/_preflight.py:105-109
+        a = np.asarray(ops[0])
+        K = a.shape[kw.get("axis", 0)] if a.ndim else 1
+        if K * _maxabs(a) <= M:
+            return Verdict("safe", "K * max|a| <= max", ev)
+        return Verdict("unknown", "", ev)
     return Verdict("unknown", "", ev)
 
 
