@@ -241,6 +241,22 @@ SFB_API int sfb_sum(int bits, const int16_t *x, int64_t outer, int64_t K, int64_
 SFB_API int sfb_dot(int bits, const int16_t *a, const int16_t *b, int64_t n, int16_t *out, uint8_t *flags,
                     void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
 
+/* The chip's memory format (src/sf/_vectorized.py:78-89; spec/ops.py,
+ * "Memory format"): a 16-bit word with the sign at bit N-1 and |k| in the
+ * low N-1 bits; the word with only the sign set reads as 0.
+ * sfb_to_bits: codes -> words.  sfb_from_bits: words -> codes, and
+ * counts->reserved[2] += the words with bits at or above N (the reference
+ * rejects them with ValueError; their codes here are those of the low N
+ * bits).  sfb_elementwise_signmag: sfb_elementwise on words in and out, the
+ * conversion done in the kernel's loads and stores (no extra pass); words
+ * that do not fit are counted the same way (counts is required). */
+SFB_API int sfb_to_bits(int bits, const int16_t *codes, uint16_t *out, int64_t n, sfb_stream stream);
+SFB_API int sfb_from_bits(int bits, const uint16_t *patterns, int16_t *codes, int64_t n, sfb_counts *counts,
+                          sfb_stream stream);
+SFB_API int sfb_elementwise_signmag(int op, int bits, const uint16_t *a, const uint16_t *b, const uint16_t *c,
+                                    uint16_t *out, uint8_t *flags, int64_t n, int pow_n, sfb_counts *counts,
+                                    sfb_stream stream);
+
 /* Exhaustive sweep of every operand pair of one width.  No counterpart in
  * the reference's Device API: the GPU form of its exhaustive check,
  * tools/exhaustive.py:146-181.  For op in SFB_OP_ADD / SUB / MUL / DIV and

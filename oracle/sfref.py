@@ -516,3 +516,20 @@ def wide_matmul(a, b, bits, shift=None, mx=MX_DEFAULT, acc_fn=None):
     qa, ea, ua = quantize_pow2(bits, a, -1)
     qb, eb, ub = quantize_pow2(bits, np.asarray(b, dtype=np.float64), -2)
     return _wide_core(bits, a, qa, ea, ua + ub, qb, eb, 0, None, shift, mx, acc_fn)
+
+
+# --- the chip's sign-magnitude memory format (src/sf/_vectorized.py:78-89) ----------------
+
+def to_bits(bits, codes):
+    """Signed codes -> sign-magnitude words: sign at bit N-1, |k| below it."""
+    k = _i64(codes)
+    return np.where(k < 0, (1 << (bits - 1)) | (-k), k).astype(np.uint16)
+
+
+def from_bits(bits, words):
+    """Sign-magnitude words -> codes (the sign-only word reads as 0).
+    Returns (codes, fits): ``fits`` False where a word has bits at or above N."""
+    M, _ = consts(bits)
+    b = _i64(words)
+    mag = b & M
+    return np.where((b >> (bits - 1)) & 1, -mag, mag), (b >= 0) & (b < (1 << bits))

@@ -15,6 +15,7 @@ from __future__ import annotations
 
 from ._array import (DTYPES, SFArray, SFDType, addmm, array, asarray, div, dot, fma, from_codes, full, matmul,
                      resolve_dtype, sqrt, zeros)
+from ._array import from_bits
 from ._array import sum_ as sum  # noqa: A001
 from ._config import accumulate, config, getaccumulate, getconfig, setaccumulate
 from ._device import HOST, B200Device, Device, devices, get_device, register_device
@@ -42,5 +43,5 @@ def device(name="b200"):
 __all__ = ["SFFormat", "FORMATS", "MIN_BITS", "MAX_BITS", "SFStatus", "SFArray", "SFDType", "Device",
            "B200Device", "HOST", "devices", "get_device", "register_device", "device", "errstate", "geterr",
            "seterr", "config", "getconfig", "accumulate", "getaccumulate", "setaccumulate", "array", "asarray",
-           "from_codes", "zeros", "full", "matmul", "dot", "addmm", "fma", "div", "sqrt", "sum", "dtype", "dtypes",
+           "from_codes", "zeros", "full", "matmul", "dot", "addmm", "fma", "div", "sqrt", "sum", "from_bits", "dtype", "dtypes",
            "__version__"] + [f"sf{b}" for b in DTYPES] + list(_errors_all)

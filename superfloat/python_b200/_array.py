@@ -309,6 +309,23 @@ def from_codes(codes, dt, device: str = HOST) -> SFArray:
     return out if device == HOST else out.to(device)
 
 
+def from_bits(bits, dt, device: str = HOST) -> SFArray:
+    """Sign-magnitude words (the chip's memory format) -> an SF array: sign at
+    bit N-1, |k| in the low N-1 bits, the sign-only word reads as 0;
+    ValueError for a word that does not fit (src/sf/_vectorized.py:84-89,
+    src/sf/_functions.py:136-144)."""
+    dt = resolve_dtype(dt)
+    fmt = FORMATS[dt.bits]
+    b = np.asarray(bits)
+    if b.dtype == bool or not np.issubdtype(b.dtype, np.integer):
+        raise TypeError(f"bits must be integers, got {b.dtype}")
+    b = b.astype(np.int64)
+    if np.any((b < 0) | (b >= (1 << fmt.bits))):
+        raise ValueError(f"bit pattern does not fit in {fmt.bits} bits")
+    mag = b & fmt.max_code
+    return SFArray._wrap(np.where(b >> fmt.frac_bits, -mag, mag).astype(np.int64), dt, device)
+
+
 def zeros(shape, dtype="sf16", device: str = HOST) -> SFArray:
     out = SFArray._wrap(np.zeros(shape, np.int64), resolve_dtype(dtype))
     return out if device == HOST else out.to(device)

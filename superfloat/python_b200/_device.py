@@ -227,6 +227,64 @@ class B200Device(Device):
         _lib.sum_codes(fmt.bits, X, outer, K, inner, o, fl, ws, cnt, stream=stream)
         return o, cnt, fl
 
+    # --- the chip's sign-magnitude memory format -------------------------------------------
+    def upload_bits(self, fmt, patterns):
+        """Sign-magnitude words (host) -> int16 device codes, converted on the
+        device; ValueError for a word that does not fit ``fmt``'s width
+        (src/sf/_vectorized.py:84-89)."""
+        torch = self._ready()
+        p = np.asarray(patterns)
+        if p.size and (p.min() < 0 or p.max() >= (1 << 16)):
+            raise ValueError(f"bit pattern does not fit in {fmt.bits} bits")
+        host = torch.from_numpy(np.ascontiguousarray(p, dtype=np.uint16).view(np.int16))
+        words = host.pin_memory().to(self.torch_device, non_blocking=True)
+        codes = torch.empty_like(words)
+        cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=self.torch_device)
+        _lib.from_bits(fmt.bits, words, codes, cnt)
+        _lib.check_patterns(cnt.cpu().numpy(), fmt.bits)
+        return codes
+
+    def download_bits(self, fmt, codes) -> np.ndarray:
+        """int16 device codes -> sign-magnitude words (host uint16)."""
+        torch = self._ready()
+        words = torch.empty_like(codes)
+        _lib.to_bits(fmt.bits, codes.contiguous(), words)
+        return words.cpu().numpy().view(np.uint16)
+
+    def run_bits(self, op, fmt, *patterns, **kw):
+        """``run`` in the chip's format: sign-magnitude words in and out.
+        Elementwise ops read and write the words directly in the kernel;
+        reductions convert on the device around the code kernels.  Returns
+        (uint16 words, event masks)."""
+        torch = self._ready()
+        with self._lock:
+            self.launches += 1
+        if op in ("matmul", "matmul_wide", "sum"):
+            xs = [self.upload_bits(fmt, p) for p in patterns[:ARITY[op]]]
+            codes, cnt, fl = self.run_device(op, fmt, *xs, flags=True, **kw)
+            _lib.check_counts(cnt.cpu().numpy())
+            words = self.download_bits(fmt, codes)
+        else:
+            ps = [np.asarray(p) for p in patterns[:ARITY[op]]]
+            for p in ps:
+                if p.size and (p.min() < 0 or p.max() >= (1 << 16)):
+                    raise ValueError(f"bit pattern does not fit in {fmt.bits} bits")
+            shape = np.broadcast_shapes(*(p.shape for p in ps))
+            xs = [torch.from_numpy(np.array(np.broadcast_to(p, shape), dtype=np.uint16).view(np.int16))
+                  .to(self.torch_device) for p in ps]
+            out = torch.empty(shape, dtype=torch.int16, device=self.torch_device)
+            fl = torch.empty(shape, dtype=torch.uint8, device=self.torch_device)
+            cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=self.torch_device)
+            if out.numel():
+                _lib.elementwise_signmag(op, fmt.bits, xs[0], xs[1] if len(xs) > 1 else None,
+                                         xs[2] if len(xs) > 2 else None, out, fl, cnt, pow_n=int(kw.get("n", 0)))
+            c = cnt.cpu().numpy()
+            _lib.check_counts(c)
+            _lib.check_patterns(c, fmt.bits)
+            words = out.cpu().numpy().view(np.uint16)
+        fl = fl.cpu().numpy()
+        return words, {e: (fl & _EVENT_BIT[e]) != 0 for e in OP_EVENTS[op]}
+
     # --- the reference's plug-in contract --------------------------------------------------
     def run(self, op, fmt, *operands, **kw):
         """Execute ``op`` on int64 code arrays (src/sf/_device.py:96-106).

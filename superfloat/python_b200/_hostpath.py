@@ -30,10 +30,15 @@ class HostPipeline:
         self.flags = [torch.empty(chunk, dtype=torch.uint8, device=d) for _ in range(slots)]
         self.counts = [torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=d) for _ in range(slots)]
 
-    def run(self, op, fmt, *xs, out, flags_out=None, pow_n: int = 0):
+    def run(self, op, fmt, *xs, out, flags_out=None, pow_n: int = 0, layout: str = "codes"):
         """``out[i] = op(xs...)[i]`` over host int16 tensors of equal length
         (pinned for the copies to overlap).  Returns the event counts (numpy
-        int64[8]); per-output event bytes go to ``flags_out`` when given."""
+        int64[8]); per-output event bytes go to ``flags_out`` when given.
+        ``layout="signmag"``: operands and result are the chip's
+        sign-magnitude words (carried in int16 tensors), converted inside the
+        kernel; ValueError when a word does not fit the width."""
+        if layout not in ("codes", "signmag"):
+            raise ValueError(f"layout must be 'codes' or 'signmag', got {layout!r}")
         import torch
         n = out.numel()
         for c in self.counts:
@@ -55,7 +60,11 @@ class HostPipeline:
                 fl = self.flags[slot][:m] if flags_out is not None else None
                 b = ins[1] if len(ins) > 1 else None
                 c = ins[2] if len(ins) > 2 else None
-                _lib.elementwise(op, fmt.bits, ins[0], b, c, o, fl, self.counts[slot], pow_n=pow_n, stream=st)
+                if layout == "signmag":
+                    _lib.elementwise_signmag(op, fmt.bits, ins[0], b, c, o, fl, self.counts[slot], pow_n=pow_n,
+                                             stream=st)
+                else:
+                    _lib.elementwise(op, fmt.bits, ins[0], b, c, o, fl, self.counts[slot], pow_n=pow_n, stream=st)
                 out[lo:hi].copy_(o, non_blocking=True)
                 if flags_out is not None:
                     flags_out[lo:hi].copy_(fl, non_blocking=True)
@@ -67,6 +76,8 @@ class HostPipeline:
             total += c
         res = total.cpu().numpy()
         _lib.check_counts(res)
+        if layout == "signmag":
+            _lib.check_patterns(res, fmt.bits)
         return res
 
 

@@ -44,6 +44,9 @@ SIGNATURES = {
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
+    "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
+    "sfb_from_bits": (_i32, [_i32, _p, _p, _i64, _p, _p]),
+    "sfb_elementwise_signmag": (_i32, [_i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _p, _p]),
     "sfb_sum": (_i32, [_i32, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p]),
     "sfb_dot": (_i32, [_i32, _p, _p, _i64, _p, _p, _p, _i64, _p, _p]),
     "sfb_matmul_wide_acc": (_i32, [_i32, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
@@ -176,6 +179,28 @@ def wide_workspace(bits, mx, batch, M, N, K) -> int:
     if n < 0:
         check(int(n), "sf matmul (wide) workspace")
     return int(n)
+
+
+def to_bits(bits, codes, out, stream=None):
+    rc = load().sfb_to_bits(bits, _ptr(codes), _ptr(out), codes.numel(), _stream(stream))
+    check(rc, "sf to_bits")
+
+
+def from_bits(bits, patterns, codes, counts, stream=None):
+    rc = load().sfb_from_bits(bits, _ptr(patterns), _ptr(codes), patterns.numel(), _ptr(counts), _stream(stream))
+    check(rc, "sf from_bits")
+
+
+def elementwise_signmag(op, bits, a, b, c, out, flags, counts, pow_n=0, stream=None):
+    rc = load().sfb_elementwise_signmag(OPS[op], bits, _ptr(a), _ptr(b), _ptr(c), _ptr(out), _ptr(flags),
+                                        out.numel(), int(pow_n), _ptr(counts), _stream(stream))
+    check(rc, "sf elementwise (sign-magnitude)")
+
+
+def check_patterns(counts, bits) -> None:
+    """ValueError when a sign-magnitude word had bits at or above N (counts host data)."""
+    if int(counts[7]) != 0:
+        raise ValueError(f"{int(counts[7])} bit pattern(s) do not fit in {bits} bits")
 
 
 def reduce_workspace(outputs, K) -> int:

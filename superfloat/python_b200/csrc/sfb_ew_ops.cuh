@@ -127,5 +127,19 @@ __device__ __forceinline__ unsigned flag_byte(const Ev &e) {
            (e.inval ? SFB_F_INVALID : 0u);
 }
 
+// The chip's memory format (src/sf/_vectorized.py:78-89): a 16-bit word
+// with the sign at bit N-1 and |k| in the low N-1 bits; the pattern with
+// only the sign set reads as 0.  A pattern with bits at or above N does not
+// fit the width (``bad``).
+__device__ __forceinline__ int sm_to_code(unsigned p, Width w, bool &bad) {
+    bad = (p >> w.bits) != 0;
+    const int mag = (int)(p & (unsigned)w.M);
+    return ((p >> w.sh) & 1u) ? -mag : mag;
+}
+
+__device__ __forceinline__ unsigned code_to_sm(int k, Width w) {
+    return k < 0 ? ((1u << w.sh) | (unsigned)(-k)) : (unsigned)k;
+}
+
 }  // namespace ewops
 }  // namespace sfb
