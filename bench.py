@@ -391,6 +391,7 @@ def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
     cnt = torch.zeros(8, dtype=torch.int64, device=dev.torch_device)
     for _ in range(2):
         dev.run_device("matmul_wide", fmt, tA, tB, out=out, counts=cnt, shift=0)
+    _shard.gather_rows(out, cuts, dist, world)               # the first collective of this size sets NCCL up
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     reps = 3
     torch.cuda.synchronize()
