@@ -184,6 +184,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--matmul-only", type=int, default=0, metavar="SIZE",
                     help="time only the wide and chain matmuls, wide at SIZE^3 (a small case for profiling)")
+    ap.add_argument("--wide", action="store_true", help="with --gpt2-only: the accumulate=\"wide\" conversion")
     ap.add_argument("--chain-only", action="store_true",
                     help="time only the proven chain kernel on the GPT-2-small projection shapes")
     ap.add_argument("--sweep-only", action="store_true", help="time only the exhaustive sf16 pair sweep")
@@ -207,6 +208,9 @@ def main():
         return 0
     if args.sweep_only:
         print(json.dumps(bench_sweep(torch, None, 0, 1)), flush=True)
+        return 0
+    if args.gpt2_only and args.wide:
+        print(json.dumps(bench_gpt2(torch, seq=args.gpt2_only, accumulate="wide")), flush=True)
         return 0
     if args.gpt2_only:
         print(json.dumps(bench_gpt2(torch, seq=args.gpt2_only)), flush=True)
@@ -363,6 +367,7 @@ def main():
         if rank == 0 and world == 1:
             mm["chain_gpt2_projections"] = bench_chain_shapes(torch)
             mm["gpt2_small_convert"] = bench_gpt2(torch)
+            mm["gpt2_small_convert_wide"] = bench_gpt2(torch, accumulate="wide")
         if rank == 0:
             line["matmul"] = mm
 
@@ -530,7 +535,7 @@ def bench_chain_shapes(torch, reps=10):
     return res
 
 
-def bench_gpt2(torch, batch=8, seq=512, reps=3):
+def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     """sft.convert(dtype=sf16) GPT-2-small (12 layers, d_model 768, 12 heads,
     FFN 3072, vocab 50257; random init, seed 0) forward on batch x seq token
     ids, on the GPU; 49 SF layers (chain accumulation, headroom "bound")."""
@@ -539,7 +544,8 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3):
     import superfloat.python_b200.torch as sft
     torch.manual_seed(0)
     cfg = GPT2Config(n_layer=12, n_embd=768, n_head=12, n_inner=3072, vocab_size=50257, n_positions=1024)
-    model = sft.convert(GPT2LMHeadModel(cfg).eval(), dtype="sf16").cuda()
+    kw = {"accumulate": "wide", "attention": False} if accumulate == "wide" else {}
+    model = sft.convert(GPT2LMHeadModel(cfg).eval(), dtype="sf16", **kw).cuda()
     ids = torch.randint(0, 50257, (batch, seq), generator=torch.Generator().manual_seed(0)).cuda()
     with torch.no_grad(), warnings.catch_warnings():
         warnings.simplefilter("ignore")
@@ -557,7 +563,8 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3):
     st = sft.last_status(model)
     return {"ms_per_forward": ms, "tokens_per_s": R / (ms / 1e3), "sf_layers": len(st),
             "sf16_TOPS": 2 * products / (ms / 1e3) / 1e12, "saturated": sum(v.saturated or 0 for v in st.values()),
-            "workload": f"GPT-2-small sft.convert(sf16) forward, {batch} x {seq} tokens, float parts on the GPU"}
+            "workload": f"GPT-2-small sft.convert(sf16, accumulate={accumulate!r}) forward, {batch} x {seq} tokens, "
+                        "float parts on the GPU"}
 
 
 if __name__ == "__main__":

@@ -156,6 +156,14 @@ SFB_API int sfb_quantize(const void *x, int dtype, int64_t rows, int64_t cols, i
                          const double *row_scale, int bits, int16_t *codes, int64_t ldc, sfb_qstats *stats,
                          sfb_stream stream);
 
+/* sfb_quantize with the scale a0 = absmax / m taken on the device from a
+ * finished sfb_scan's statistics (1 when absmax is 0): the first pass of the
+ * activation scale search (src/sf/torch/_core.py:306-331) without a host
+ * round trip between the scan and the quantize. */
+SFB_API int sfb_quantize_auto(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                              const sfb_qstats *scan, double m, int bits, int16_t *codes, int64_t ldc,
+                              sfb_qstats *stats, sfb_stream stream);
+
 /* Bytes of device workspace sfb_matmul_wide needs for this problem (0 when
  * it needs none); negative on a bad argument. */
 SFB_API int64_t sfb_matmul_wide_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K);

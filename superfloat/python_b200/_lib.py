@@ -45,6 +45,7 @@ SIGNATURES = {
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
+    "sfb_quantize_auto": (_i32, [_p, _i32, _i64, _i64, _i64, _p, ctypes.c_double, _i32, _p, _i64, _p, _p]),
     "sfb_from_bits": (_i32, [_i32, _p, _p, _i64, _p, _p]),
     "sfb_elementwise_signmag": (_i32, [_i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _p, _p]),
     "sfb_sum": (_i32, [_i32, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p]),
@@ -163,6 +164,12 @@ def quantize(x, rows, cols, ld, scale, row_scale, bits, codes, ldc, stats, strea
     rc = load().sfb_quantize(_ptr(x), _fdtype(x), rows, cols, ld, float(scale), _ptr(row_scale), bits, _ptr(codes),
                              ldc, _ptr(stats), _stream(stream))
     check(rc, "sf quantize")
+
+
+def quantize_auto(x, rows, cols, ld, scan_stats, m, bits, codes, ldc, stats, stream=None):
+    rc = load().sfb_quantize_auto(_ptr(x), _fdtype(x), rows, cols, ld, _ptr(scan_stats), float(m), bits, _ptr(codes),
+                                  ldc, _ptr(stats), _stream(stream))
+    check(rc, "sf quantize (scale from scan)")
 
 
 def qstats_view(t):

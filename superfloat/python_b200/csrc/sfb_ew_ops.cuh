@@ -21,18 +21,20 @@ namespace ewops {
 // floor(ua 2^sh / ub) for 0 <= ua <= ub < 2^15, ub >= 1, sh <= 15 (the
 // quotient is at most 2^sh, reached exactly when ua == ub).
 // Reciprocal estimate, then one exact integer correction:
-//   x = ua 2^sh / ub.  ua 2^sh and ub convert to float exactly with the
-//   exponent-bias trick (ua < 2^23 placed in the mantissa under exponent
-//   23 + sh); rcp.approx has relative error < 2^-22 and the product rounds
-//   once, so the estimate is within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding
-//   it to the nearest integer (the 1.5 * 2^23 bias) gives floor(x) or
-//   floor(x) + 1, and the sign of the remainder tells which.
+//   x = ua 2^sh / ub.  ua and ub convert to float exactly (integer-to-float
+//   conversions, on the XU pipe beside the reciprocal, which leaves the ALU
+//   pipe to the rest of the op); rcp.approx has relative error < 2^-22 and
+//   ua * (rcp(ub) 2^sh) rounds once (2^sh scales exactly), so the estimate is
+//   within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding it to the nearest
+//   integer (the 1.5 * 2^23 bias) gives floor(x) or floor(x) + 1, and the
+//   sign of the remainder tells which.
 __device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
-    const float fa = __int_as_float(((150 + sh) << 23) | ua) - __int_as_float((150 + sh) << 23);
-    const float fb = __int_as_float(0x4B000000 | ub) - 8388608.0f;
+    const float fa = __uint2float_rn(ua);
+    const float fb = __uint2float_rn(ub);
     float r;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fb));
-    const unsigned q0 = (unsigned)__float_as_int(fa * r + 12582912.0f) - 0x4B400000u;
+    const float r2 = r * __int_as_float((127 + sh) << 23);          // r 2^sh, exact
+    const unsigned q0 = (unsigned)__float_as_int(fmaf(fa, r2, 12582912.0f)) - 0x4B400000u;
     const unsigned rem = (ua << sh) - q0 * ub;
     return q0 + (unsigned)((int)rem >> 31);                            // q0 - 1 when rem < 0
 }

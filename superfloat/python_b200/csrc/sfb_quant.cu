@@ -51,8 +51,13 @@ __global__ void __launch_bounds__(QT) scan_kernel(const T *__restrict__ x, int64
 template <typename T>
 __global__ void __launch_bounds__(QT) quant_kernel(const T *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
                                                    double scale, const double *__restrict__ row_scale, Width w,
-                                                   int16_t *__restrict__ codes, int64_t ldc, sfb_qstats *st) {
+                                                   int16_t *__restrict__ codes, int64_t ldc, sfb_qstats *st,
+                                                   const sfb_qstats *__restrict__ scan, double m) {
     const int lane = threadIdx.x & 31;
+    if (scan) {                                  // the scale a0 = max|x| / m from a scan pass (1 when all 0)
+        const double amax = scan->absmax;
+        scale = amax > 0.0 ? amax / m : 1.0;
+    }
     const int64_t warp = ((int64_t)blockIdx.x * QT + threadIdx.x) >> 5;
     const int64_t nwarps = ((int64_t)gridDim.x * QT) >> 5;
     const double thr = 1.0 - ldexp(1.0, -w.bits);
@@ -138,11 +143,36 @@ extern "C" int sfb_quantize(const void *x, int dtype, int64_t rows, int64_t cols
     const Width w = width(bits);
     const int g = grid_for(rows * 32);
     if (dtype == SFB_F32)
-        quant_kernel<float><<<g, QT, 0, st>>>((const float *)x, rows, cols, ld, scale, row_scale, w, codes, ldc, stats);
+        quant_kernel<float><<<g, QT, 0, st>>>((const float *)x, rows, cols, ld, scale, row_scale, w, codes, ldc, stats,
+                                              nullptr, 0.0);
     else if (dtype == SFB_F64)
         quant_kernel<double><<<g, QT, 0, st>>>((const double *)x, rows, cols, ld, scale, row_scale, w, codes, ldc,
-                                               stats);
+                                               stats, nullptr, 0.0);
     else
         return set_error(SFB_EINVAL, "sfb_quantize: dtype %d is not SFB_F32 / SFB_F64", dtype);
     return check_launch("sfb_quantize");
+}
+
+extern "C" int sfb_quantize_auto(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                 const sfb_qstats *scan, double m, int bits, int16_t *codes, int64_t ldc,
+                                 sfb_qstats *stats, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_quantize_auto: width %d is not 4..16", bits);
+    if (rows < 0 || cols < 0 || stats == nullptr || scan == nullptr || !(m > 0.0))
+        return set_error(SFB_EINVAL, "sfb_quantize_auto: bad shape, null statistics or m <= 0");
+    if (rows == 0 || cols == 0) return SFB_OK;
+    if (ld < cols || ldc < cols) return set_error(SFB_EINVAL, "sfb_quantize_auto: ld or ldc below cols");
+    if (x == nullptr || codes == nullptr) return set_error(SFB_EINVAL, "sfb_quantize_auto: null buffer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const Width w = width(bits);
+    const int g = grid_for(rows * 32);
+    if (dtype == SFB_F32)
+        quant_kernel<float><<<g, QT, 0, st>>>((const float *)x, rows, cols, ld, 1.0, nullptr, w, codes, ldc, stats,
+                                              scan, m);
+    else if (dtype == SFB_F64)
+        quant_kernel<double><<<g, QT, 0, st>>>((const double *)x, rows, cols, ld, 1.0, nullptr, w, codes, ldc, stats,
+                                               scan, m);
+    else
+        return set_error(SFB_EINVAL, "sfb_quantize_auto: dtype %d is not SFB_F32 / SFB_F64", dtype);
+    return check_launch("sfb_quantize_auto");
 }

@@ -216,14 +216,18 @@ weight_cache = WeightCache()
 
 class _Quantized:
     """Codes of x / a from one sfb_quantize pass, with the cast's underflow
-    count and the L1 statistics (the events dict of ``cast``)."""
+    count and the L1 statistics (the events dict of ``cast``).  ``done``:
+    codes and host statistics of a pass already run (the fused first pass)."""
 
-    def __init__(self, fmt, x2d: torch.Tensor, a: float):
-        R, K = x2d.shape
-        self.codes = torch.empty(R, K, dtype=torch.int16, device=x2d.device)
-        st = _stats_buf(x2d.device)
-        _lib.quantize(x2d, R, K, x2d.stride(0), a, None, fmt.bits, self.codes, K, st[0])
-        q = _lib.qstats_view(st[0].cpu())
+    def __init__(self, fmt, x2d: torch.Tensor, a: float, done=None):
+        if done is not None:
+            self.codes, q = done
+        else:
+            R, K = x2d.shape
+            self.codes = torch.empty(R, K, dtype=torch.int16, device=x2d.device)
+            st = _stats_buf(x2d.device)
+            _lib.quantize(x2d, R, K, x2d.stride(0), a, None, fmt.bits, self.codes, K, st[0])
+            q = _lib.qstats_view(st[0].cpu())
         self.events = {"overflow": q["overflow"], "underflow": q["underflow"], "invalid": q["invalid"]}
         self.row_l1, self.max_abs = q["max_row_l1"], q["max_abs"]
 
@@ -234,15 +238,16 @@ class _Quantized:
 
 
 def activation_fused(fmt, x2d: torch.Tensor, amax: float, b_max_abs: int, b_max_col_l1: int, bias_over_scale,
-                     headroom: str):
+                     headroom: str, first=None):
     """The activation scale search (src/sf/torch/_core.py:306-331) on a
-    float32 / float64 (R, K) device tensor, each cast one sfb_quantize pass.
+    float32 / float64 (R, K) device tensor, each cast one sfb_quantize pass
+    (``first``: the pass at a0 already run, as (codes, host statistics)).
     Returns (codes, events, a, a0, proven): ``proven`` when the L1 bound shows
     that no chain step can saturate."""
     m = fmt.max_code / fmt.scale
     a0 = amax / m if amax > 0 else 1.0
     a = a0
-    q = _Quantized(fmt, x2d, a)
+    q = _Quantized(fmt, x2d, a, done=first)
     if headroom == "none":
         return q.codes, q.events, a, a0, q.bound(fmt, b_max_abs, b_max_col_l1) <= fmt.max_code
     a_bias = bias_over_scale(None)
@@ -278,6 +283,46 @@ def _scanned(x: torch.Tensor, cuda, fmt, what: str):
     return x, sc["absmax"]
 
 
+class BiasCache:
+    """A layer's bias as the scale search reads it, per bias version and
+    prepared weight: the sanitized float64 bias on the device, and on the
+    host |b| / s_w and the scale that fits the largest finite ratio.  Biases
+    holding NaN / inf are not cached (their events fire on every call)."""
+
+    def __init__(self, max_entries: int = 512):
+        self.items = OrderedDict()
+        self.max_entries = max_entries
+
+    def get(self, fmt, b: torch.Tensor, pw: PreparedWeight, cuda):
+        key = (b.untyped_storage().data_ptr(), b.storage_offset(), tuple(b.shape), tuple(b.stride()), b._version,
+               b.dtype, str(b.device), id(pw), fmt.bits, str(cuda))
+        hit = self.items.get(key)
+        if hit is not None and hit[0]() is not None and hit[1]() is pw:
+            self.items.move_to_end(key)
+            return hit[2]
+        bd = b.detach().to(device=cuda, dtype=torch.float64)
+        finite = bool(torch.isfinite(bd).all())
+        bd = sanitize(bd, fmt, "linear bias")
+        need = (bd.abs() / pw.s_w).cpu().numpy()            # may hold inf; host float64, as the reference
+        fin = np.isfinite(need)
+        a_bias = float(need[fin].max()) / (fmt.max_code / fmt.scale) if fin.any() else 0.0
+        val = (bd, need, a_bias)
+        if finite:
+            owner = b
+            while owner._base is not None:
+                owner = owner._base
+            self.items[key] = (weakref.ref(owner), weakref.ref(pw), val)
+            while len(self.items) > self.max_entries:
+                self.items.popitem(last=False)
+        return val
+
+    def clear(self):
+        self.items.clear()
+
+
+bias_cache = BiasCache()
+
+
 # --- linear ----------------------------------------------------------------------------------
 
 def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_tensor",
@@ -289,15 +334,31 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
     dev = dev or target()
     cuda = dev.torch_device
     S, M = fmt.scale, fmt.max_code
-    x, amax = _scanned(x, cuda, fmt, "linear input")
+    x = x.detach().to(device=cuda)
+    if x.dtype not in (torch.float32, torch.float64):
+        x = x.to(torch.float32)                            # float16 / bfloat16 widen exactly
+    x = x.contiguous()
+    R, K = x.shape
+    m = M / S
+    # the scan and the first quantize (scale max|x| / m, taken on the device): one statistics read
+    st = _stats_buf(cuda, 2)
+    kx0 = torch.empty(R, K, dtype=torch.int16, device=cuda)
+    _lib.scan(x, st[0])
+    _lib.quantize_auto(x, R, K, K, st[0], m, fmt.bits, kx0, K, st[1])
+    host = st.cpu()
+    sc, q0 = _lib.qstats_view(host[0]), _lib.qstats_view(host[1])
+    first = None
+    if sc["nan"] or sc["inf"]:                              # the policy decides; then the finite values
+        x = sanitize(x.to(torch.float64), fmt, "linear input")
+        amax = finite_absmax(x)
+    else:
+        amax = sc["absmax"]
+        first = (kx0, q0)
     pw = weight_cache.get(fmt, w, wscale, cuda)
+    bd = need = None
     if b is not None:
-        b = sanitize(b.detach().to(device=cuda, dtype=torch.float64), fmt, "linear bias")
-    if b is not None and b.numel():
-        need = (b.abs() / pw.s_w).cpu().numpy()            # may hold inf; host float64, as the reference
-        fin = np.isfinite(need)
-        a_bias = float(need[fin].max()) / (M / S) if fin.any() else 0.0
-
+        bd, need, a_bias = bias_cache.get(fmt, b, pw, cuda)
+    if b is not None and bd.numel():
         def bias_over_scale(a):
             if a is None:
                 return a_bias
@@ -307,24 +368,23 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
         def bias_over_scale(a):
             return None if a is None else 0.0
 
-    R, K = x.shape
-    kx, ev_x, a, a0, proven = activation_fused(fmt, x, amax, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom)
-    bias_sat = 0
+    kx, ev_x, a, a0, proven = activation_fused(fmt, x, amax, pw.max_abs, pw.max_col_l1, bias_over_scale, headroom,
+                                               first=first)
     kb = None
+    cnt = torch.zeros(_lib.N_COUNTS + 1, dtype=torch.int64, device=cuda)   # + the bias codes' saturations
     if b is not None:
-        kb, ev_b = cast(fmt, b / (a * pw.s_w))
-        bias_sat = int(ev_b["overflow"])
+        kb, ev_b = cast(fmt, bd / (a * pw.s_w))
+        cnt[_lib.N_COUNTS] = ev_b["overflow"]
     N = pw.kwT.shape[1]
     y = torch.empty(R, N, dtype=torch.float64 if out_dtype == torch.float64 else torch.float32, device=cuda)
-    cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=cuda)
     _lib.linear_chain(fmt.bits, kx, pw.kwT, kb, a, pw.s_w, proven,
                       y if y.dtype == torch.float32 else None, y if y.dtype == torch.float64 else None,
                       None, None, cnt, R, N, K, K, N)
     c = cnt.cpu().numpy()
-    _lib.check_counts(c)
+    _lib.check_counts(c[:_lib.N_COUNTS])
     return CoreResult(y=y, saturated=int(c[0]), exact=True, underflow=int(c[1]),
                       input_underflow=int(ev_x["underflow"]), weight_underflow=pw.w_under,
-                      bias_saturated=bias_sat, headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
+                      bias_saturated=int(c[_lib.N_COUNTS]), headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
                       outputs=R * N, act_scale=a)
 
 
