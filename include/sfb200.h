@@ -156,6 +156,40 @@ SFB_API int sfb_quantize(const void *x, int dtype, int64_t rows, int64_t cols, i
                          const double *row_scale, int bits, int16_t *codes, int64_t ldc, sfb_qstats *stats,
                          sfb_stream stream);
 
+/* The converted layer's activation scale search with headroom="bound" on the
+ * device, one cooperative launch (src/sf/torch/_core.py:200-236, :306-331):
+ * scan, a0 = max finite |x| / m, casts of x / a (NaN read as 0, +-inf as +-max
+ * finite |x|, the reference's sanitize), the bias step and the L1-bound loop,
+ * leaving the final codes (R x K, row stride K) and the result struct on the
+ * device.  w_max_abs / w_max_col_l1: max |W code| and max sum_k |W code| of the
+ * prepared weight; has_bias, need_max = max |b| / s_w (inf allowed) and a_bias
+ * the scale its largest finite ratio needs.  scratch: device bytes of
+ * sfb_linear_scale_scratch().  err = 1: the search did not converge in 32
+ * steps (the reference raises).  No counterpart entry in the reference, which
+ * runs the search on the host. */
+typedef struct {
+    double a, a0;
+    int64_t proven, iterations, nan_count, inf_count, underflow, err;
+} sfb_scale_result;
+SFB_API int64_t sfb_linear_scale_scratch(void);
+SFB_API int sfb_linear_scale(const void *x, int dtype, int64_t R, int64_t K, int64_t ld, int bits,
+                             int64_t w_max_abs, int64_t w_max_col_l1, int has_bias, double need_max, double a_bias,
+                             int16_t *codes, sfb_scale_result *result, void *scratch, sfb_stream stream);
+
+/* sfb_linear_chain in proven mode with the activation scale read from
+ * device memory (a_dev: the a of a finished sfb_linear_scale), so the
+ * layer's kernels queue without a host round trip. */
+SFB_API int sfb_linear_chain_dev(int bits, const int16_t *X, const int16_t *WT, const int16_t *bias,
+                                 const double *a_dev, const double *s_col, float *y32, double *y64, int16_t *codes,
+                                 uint8_t *flags, int64_t R, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                                 sfb_counts *counts, sfb_stream stream);
+
+/* The bias codes of a converted layer at its scale: cast(b[n] / (a_dev[0] *
+ * s_col[n])) with the cast rule of src/sf/_vectorized.py:59-71
+ * (src/sf/torch/_core.py:376-378); *n_over += the codes that saturated. */
+SFB_API int sfb_bias_codes(int bits, const double *b, const double *a_dev, const double *s_col, int64_t n,
+                           int16_t *codes, int64_t *n_over, sfb_stream stream);
+
 /* sfb_quantize with the scale a0 = absmax / m taken on the device from a
  * finished sfb_scan's statistics (1 when absmax is 0): the first pass of the
  * activation scale search (src/sf/torch/_core.py:306-331) without a host

@@ -45,6 +45,12 @@ SIGNATURES = {
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
+    "sfb_linear_scale_scratch": (_i64, []),
+    "sfb_linear_scale": (_i32, [_p, _i32, _i64, _i64, _i64, _i32, _i64, _i64, _i32, ctypes.c_double, ctypes.c_double,
+                                _p, _p, _p, _p]),
+    "sfb_linear_chain_dev": (_i32, [_i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p,
+                                    _p]),
+    "sfb_bias_codes": (_i32, [_i32, _p, _p, _p, _i64, _p, _p, _p]),
     "sfb_quantize_auto": (_i32, [_p, _i32, _i64, _i64, _i64, _p, ctypes.c_double, _i32, _p, _i64, _p, _p]),
     "sfb_from_bits": (_i32, [_i32, _p, _p, _i64, _p, _p]),
     "sfb_elementwise_signmag": (_i32, [_i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _p, _p]),
@@ -170,6 +176,33 @@ def quantize_auto(x, rows, cols, ld, scan_stats, m, bits, codes, ldc, stats, str
     rc = load().sfb_quantize_auto(_ptr(x), _fdtype(x), rows, cols, ld, _ptr(scan_stats), float(m), bits, _ptr(codes),
                                   ldc, _ptr(stats), _stream(stream))
     check(rc, "sf quantize (scale from scan)")
+
+
+SCALE_RESULT_WORDS = 8              # sfb_scale_result: a, a0 (float64), 6 x int64
+
+
+def linear_scale_scratch() -> int:
+    return int(load().sfb_linear_scale_scratch())
+
+
+def linear_scale(x, R, K, ld, bits, w_max_abs, w_max_col_l1, has_bias, need_max, a_bias, codes, result, scratch,
+                 stream=None):
+    rc = load().sfb_linear_scale(_ptr(x), _fdtype(x), R, K, ld, bits, int(w_max_abs), int(w_max_col_l1),
+                                 int(bool(has_bias)), float(need_max), float(a_bias), _ptr(codes), _ptr(result),
+                                 _ptr(scratch), _stream(stream))
+    check(rc, "sf linear scale search")
+
+
+def linear_chain_dev(bits, X, WT, bias, a_dev, s_col, y32, y64, counts, R, N, K, ldx, ldw, stream=None):
+    rc = load().sfb_linear_chain_dev(bits, _ptr(X), _ptr(WT), _ptr(bias), _ptr(a_dev), _ptr(s_col), _ptr(y32),
+                                     _ptr(y64), None, None, R, N, K, ldx, ldw, _ptr(counts), _stream(stream))
+    check(rc, "sf linear (chain, device scale)")
+
+
+def bias_codes(bits, b, a_dev, s_col, n, codes, n_over, stream=None):
+    rc = load().sfb_bias_codes(bits, _ptr(b), _ptr(a_dev), _ptr(s_col), n, _ptr(codes), _ptr(n_over),
+                               _stream(stream))
+    check(rc, "sf bias codes")
 
 
 def qstats_view(t):

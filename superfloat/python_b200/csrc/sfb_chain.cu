@@ -73,6 +73,7 @@ union Pack8 {
 struct Epi {
     const int16_t *bias;      // nullable, N codes
     double a;                 // activation scale (dequant), used when y32 / y64 set
+    const double *a_dev;      // nullable: the scale read from device memory instead
     const double *s_col;      // per-column scale (dequant)
     float *y32;               // nullable
     double *y64;              // nullable
@@ -92,7 +93,7 @@ __device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, 
     if (e.codes) e.codes[idx] = (int16_t)v;
     if (e.flags) e.flags[idx] = (uint8_t)((o ? SFB_F_OVERFLOW : 0u) | (un ? SFB_F_UNDERFLOW : 0u));
     if (e.y32 || e.y64) {
-        const double y = (double)v / (double)(1 << w.sh) * e.a * e.s_col[gn];
+        const double y = (double)v / (double)(1 << w.sh) * (e.a_dev ? __ldg(e.a_dev) : e.a) * e.s_col[gn];
         if (e.y32) e.y32[idx] = (float)y;
         if (e.y64) e.y64[idx] = y;
     }
@@ -533,7 +534,7 @@ extern "C" int sfb_matmul_chain(int bits, const int16_t *A, const int16_t *B, co
     if (rc) return rc;
     if (batch == 0 || M == 0 || N == 0) return SFB_OK;
     if (out == nullptr) return set_error(SFB_EINVAL, "sfb_matmul_chain: null output");
-    Epi e{bias, 0.0, nullptr, nullptr, nullptr, out, flags};
+    Epi e{bias, 0.0, nullptr, nullptr, nullptr, nullptr, out, flags};
     return launch_chain(bits, A, B, e, batch, M, N, K, lda, ldb, stride_a, stride_b, stride_out, false, counts,
                         (cudaStream_t)stream, "sfb_matmul_chain");
 }
@@ -548,7 +549,23 @@ extern "C" int sfb_linear_chain(int bits, const int16_t *X, const int16_t *WT, c
     if (R == 0 || N == 0) return SFB_OK;
     if ((y32 || y64) && s_col == nullptr) return set_error(SFB_EINVAL, "sfb_linear_chain: y needs s_col");
     if (!y32 && !y64 && !codes) return set_error(SFB_EINVAL, "sfb_linear_chain: no output requested");
-    Epi e{bias, a, s_col, y32, y64, codes, flags};
+    Epi e{bias, a, nullptr, s_col, y32, y64, codes, flags};
     return launch_chain(bits, X, WT, e, 1, R, N, K, ldx, ldw, 0, 0, R * N, proven_no_saturation != 0, counts,
                         (cudaStream_t)stream, "sfb_linear_chain");
+}
+
+extern "C" int sfb_linear_chain_dev(int bits, const int16_t *X, const int16_t *WT, const int16_t *bias,
+                                    const double *a_dev, const double *s_col, float *y32, double *y64,
+                                    int16_t *codes, uint8_t *flags, int64_t R, int64_t N, int64_t K, int64_t ldx,
+                                    int64_t ldw, sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    int rc = chain_args("sfb_linear_chain_dev", bits, X, WT, 1, R, N, K, ldx, ldw, R * N);
+    if (rc) return rc;
+    if (R == 0 || N == 0) return SFB_OK;
+    if (a_dev == nullptr) return set_error(SFB_EINVAL, "sfb_linear_chain_dev: null scale");
+    if ((y32 || y64) && s_col == nullptr) return set_error(SFB_EINVAL, "sfb_linear_chain_dev: y needs s_col");
+    if (!y32 && !y64 && !codes) return set_error(SFB_EINVAL, "sfb_linear_chain_dev: no output requested");
+    Epi e{bias, 0.0, a_dev, s_col, y32, y64, codes, flags};
+    return launch_chain(bits, X, WT, e, 1, R, N, K, ldx, ldw, 0, 0, R * N, true, counts, (cudaStream_t)stream,
+                        "sfb_linear_chain_dev");
 }

@@ -105,6 +105,32 @@ __global__ void __launch_bounds__(QT) quant_kernel(const T *__restrict__ x, int6
     }
 }
 
+// bias codes at the layer's scale: cast(b[n] / (a s[n])), a from device memory
+__global__ void __launch_bounds__(QT) bias_codes_kernel(const double *__restrict__ b, const double *__restrict__ a_dev,
+                                                        const double *__restrict__ s_col, int64_t n, Width w,
+                                                        int16_t *__restrict__ codes, long long *n_over) {
+    const double a = *a_dev;
+    const double thr = 1.0 - ldexp(1.0, -w.bits);
+    const double S = (double)(1 << w.sh);
+    unsigned long long over = 0;
+    for (int64_t i = (int64_t)blockIdx.x * QT + threadIdx.x; i < n; i += (int64_t)gridDim.x * QT) {
+        const double v = b[i] / (a * s_col[i]);
+        int k;
+        if (isnan(v)) {
+            k = 0;
+        } else if (fabs(v) >= thr) {
+            k = v > 0 ? w.M : -w.M;
+            over++;
+        } else {
+            k = (int)rint(v * S);
+        }
+        codes[i] = (int16_t)k;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) over += __shfl_xor_sync(0xffffffffu, over, o);
+    if ((threadIdx.x & 31) == 0 && over) atomicAdd(reinterpret_cast<unsigned long long *>(n_over), over);
+}
+
 int grid_for(int64_t work) {
     const int64_t cap = (int64_t)sm_count() * (2048 / QT);
     int64_t g = (work + QT - 1) / QT;
@@ -175,4 +201,17 @@ extern "C" int sfb_quantize_auto(const void *x, int dtype, int64_t rows, int64_t
     else
         return set_error(SFB_EINVAL, "sfb_quantize_auto: dtype %d is not SFB_F32 / SFB_F64", dtype);
     return check_launch("sfb_quantize_auto");
+}
+
+extern "C" int sfb_bias_codes(int bits, const double *b, const double *a_dev, const double *s_col, int64_t n,
+                              int16_t *codes, int64_t *n_over, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_bias_codes: width %d is not 4..16", bits);
+    if (n < 0) return set_error(SFB_EINVAL, "sfb_bias_codes: negative length");
+    if (n == 0) return SFB_OK;
+    if (b == nullptr || a_dev == nullptr || s_col == nullptr || codes == nullptr || n_over == nullptr)
+        return set_error(SFB_EINVAL, "sfb_bias_codes: null argument");
+    bias_codes_kernel<<<grid_for(n), QT, 0, (cudaStream_t)stream>>>(b, a_dev, s_col, n, width(bits), codes,
+                                                                     reinterpret_cast<long long *>(n_over));
+    return check_launch("sfb_bias_codes");
 }

@@ -186,9 +186,21 @@ class WeightCache:
             w = w._base
         return w
 
+    @staticmethod
+    def _key(fmt, w, wscale, dev):
+        return (w.untyped_storage().data_ptr(), w.storage_offset(), tuple(w.shape), tuple(w.stride()),
+                w._version, w.dtype, str(w.device), fmt.bits, wscale, str(dev))
+
+    def peek(self, fmt, w: torch.Tensor, wscale: str, dev):
+        """The prepared weight when it is cached (so finite), else None."""
+        hit = self.items.get(self._key(fmt, w, wscale, dev))
+        if hit is not None and hit[0]() is not None:
+            self.hits += 1
+            return hit[1]
+        return None
+
     def get(self, fmt, w: torch.Tensor, wscale: str, dev) -> PreparedWeight:
-        key = (w.untyped_storage().data_ptr(), w.storage_offset(), tuple(w.shape), tuple(w.stride()),
-               w._version, w.dtype, str(w.device), fmt.bits, wscale, str(dev))
+        key = self._key(fmt, w, wscale, dev)
         hit = self.items.get(key)
         if hit is not None and hit[0]() is not None:
             self.items.move_to_end(key)
@@ -293,9 +305,20 @@ class BiasCache:
         self.items = OrderedDict()
         self.max_entries = max_entries
 
+    @staticmethod
+    def _key(fmt, b, pw, cuda):
+        return (b.untyped_storage().data_ptr(), b.storage_offset(), tuple(b.shape), tuple(b.stride()), b._version,
+                b.dtype, str(b.device), id(pw), fmt.bits, str(cuda))
+
+    def peek(self, fmt, b: torch.Tensor, pw: PreparedWeight, cuda):
+        """(bias float64, need, a_bias, max need) when cached (so finite), else None."""
+        hit = self.items.get(self._key(fmt, b, pw, cuda))
+        if hit is not None and hit[0]() is not None and hit[1]() is pw:
+            return hit[2]
+        return None
+
     def get(self, fmt, b: torch.Tensor, pw: PreparedWeight, cuda):
-        key = (b.untyped_storage().data_ptr(), b.storage_offset(), tuple(b.shape), tuple(b.stride()), b._version,
-               b.dtype, str(b.device), id(pw), fmt.bits, str(cuda))
+        key = self._key(fmt, b, pw, cuda)
         hit = self.items.get(key)
         if hit is not None and hit[0]() is not None and hit[1]() is pw:
             self.items.move_to_end(key)
@@ -306,7 +329,7 @@ class BiasCache:
         need = (bd.abs() / pw.s_w).cpu().numpy()            # may hold inf; host float64, as the reference
         fin = np.isfinite(need)
         a_bias = float(need[fin].max()) / (fmt.max_code / fmt.scale) if fin.any() else 0.0
-        val = (bd, need, a_bias)
+        val = (bd, need, a_bias, float(need.max()) if need.size else 0.0)
         if finite:
             owner = b
             while owner._base is not None:
@@ -340,6 +363,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
     x = x.contiguous()
     R, K = x.shape
     m = M / S
+    if headroom == "bound":
+        r = _linear_on_device(fmt, x, w, b, wscale, cuda, out_dtype)
+        if r is not None:
+            return r
     # the scan and the first quantize (scale max|x| / m, taken on the device): one statistics read
     st = _stats_buf(cuda, 2)
     kx0 = torch.empty(R, K, dtype=torch.int16, device=cuda)
@@ -357,7 +384,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
     pw = weight_cache.get(fmt, w, wscale, cuda)
     bd = need = None
     if b is not None:
-        bd, need, a_bias = bias_cache.get(fmt, b, pw, cuda)
+        bd, need, a_bias, _ = bias_cache.get(fmt, b, pw, cuda)
     if b is not None and bd.numel():
         def bias_over_scale(a):
             if a is None:
@@ -386,6 +413,57 @@ def linear(x: torch.Tensor, w: torch.Tensor, b, bits: int, wscale: str = "per_te
                       input_underflow=int(ev_x["underflow"]), weight_underflow=pw.w_under,
                       bias_saturated=int(c[_lib.N_COUNTS]), headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0,
                       outputs=R * N, act_scale=a)
+
+
+device_path_calls = 0          # layers completed by _linear_on_device (the tests read it)
+
+
+def _linear_on_device(fmt, x, w, b, wscale, cuda, out_dtype):
+    """The whole layer queued on the device with one host read at the end:
+    the scale search (sfb_linear_scale), the bias codes and the chain read the
+    scale from device memory.  Runs when the weight (and bias) are prepared
+    and so finite; returns None otherwise, and when the input held NaN / inf,
+    so that the host path applies the error policy in the reference's order."""
+    pw = weight_cache.peek(fmt, w, wscale, cuda)
+    if pw is None:
+        return None
+    bias = None
+    if b is not None:
+        bias = bias_cache.peek(fmt, b, pw, cuda)
+        if bias is None:
+            return None
+    R, K = x.shape
+    N = pw.kwT.shape[1]
+    kx = torch.empty(R, K, dtype=torch.int16, device=cuda)
+    words = torch.zeros(_lib.N_COUNTS + 1 + _lib.SCALE_RESULT_WORDS, dtype=torch.int64, device=cuda)
+    cnt, n_over, res = words[:_lib.N_COUNTS], words[_lib.N_COUNTS:_lib.N_COUNTS + 1], words[_lib.N_COUNTS + 1:]
+    scratch = torch.empty(_lib.linear_scale_scratch(), dtype=torch.uint8, device=cuda)
+    has_bias = bias is not None and bias[0].numel() > 0
+    need_max, a_bias = (bias[3], bias[2]) if has_bias else (0.0, 0.0)
+    _lib.linear_scale(x, R, K, K, fmt.bits, pw.max_abs, pw.max_col_l1, has_bias, need_max, a_bias, kx, res, scratch)
+    a_dev = res[0:1].view(torch.float64)
+    kb = None
+    if bias is not None:
+        kb = torch.empty(N, dtype=torch.int16, device=cuda)
+        _lib.bias_codes(fmt.bits, bias[0], a_dev, pw.s_w, N, kb, n_over)
+    y = torch.empty(R, N, dtype=torch.float64 if out_dtype == torch.float64 else torch.float32, device=cuda)
+    _lib.linear_chain_dev(fmt.bits, kx, pw.kwT, kb, a_dev, pw.s_w, y if y.dtype == torch.float32 else None,
+                          y if y.dtype == torch.float64 else None, cnt, R, N, K, K, N)
+    host = words.cpu()
+    c = host.numpy()
+    r = c[_lib.N_COUNTS + 1:]
+    nan_count, inf_count, err = int(r[4]), int(r[5]), int(r[7])
+    if nan_count or inf_count:
+        return None
+    if err:
+        raise RuntimeError("sf: headroom search did not converge")
+    _lib.check_counts(c[:_lib.N_COUNTS])
+    a, a0 = (float(v) for v in host[_lib.N_COUNTS + 1:_lib.N_COUNTS + 3].view(torch.float64))
+    global device_path_calls
+    device_path_calls += 1
+    return CoreResult(y=y, saturated=int(c[0]), exact=True, underflow=int(c[1]), input_underflow=int(r[6]),
+                      weight_underflow=pw.w_under, bias_saturated=int(c[_lib.N_COUNTS]),
+                      headroom_bits=math.log2(a / a0) if a0 > 0 else 0.0, outputs=R * N, act_scale=a)
 
 
 def matmul(a_val: torch.Tensor, b_val: torch.Tensor, bits: int, headroom: str = "bound", dev=None) -> CoreResult:

@@ -193,3 +193,63 @@ def test_gpt2_on_the_gpu_compiled(gpu):
     st = sft.last_status(model)
     assert len(st) == 49 and all(s.saturated == 0 and s.exact and s.placement == "b200" for s in st.values())
     torch._dynamo.reset()
+
+
+@pytest.mark.parametrize("case", [c["tag"] for c in META["cases"] if c["headroom"] == "bound"])
+def test_prepared_layers_search_the_scale_on_the_device(gpu, case):
+    """A layer's second call (weight and bias prepared) runs the scale search,
+    bias codes and chain on the device with one host read: the same output
+    and status as the reference."""
+    from superfloat.python_b200.torch import _core
+    c = next(x for x in META["cases"] if x["tag"] == case)
+    torch.manual_seed(0)
+    model = sft.convert(MAKE[c["arch"]](), headroom=c["headroom"], scale=c["scale"])
+    mods = _layers_by_name(model)
+    with torch.no_grad():
+        for lay in c["layers"]:
+            xin = torch.from_numpy(ARR[lay["key"] + "__in"])
+            mods[lay["name"]](xin)                              # prepares the weight and bias
+            before = _core.device_path_calls
+            with sft.capture_status() as st:
+                y = mods[lay["name"]](xin)
+            assert _core.device_path_calls == before + 1, lay["name"]
+            np.testing.assert_array_equal(y.numpy(), ARR[lay["key"] + "__out"], err_msg=lay["name"])
+            _check_status(st[lay["name"]], lay["status"], lay["name"])
+
+
+def test_gpt2_second_forward_on_the_device_path(gpu):
+    """GPT-2-small twice: the second forward's 49 layers all take the device
+    path and match the reference's layer outputs, statuses and logits."""
+    from superfloat.python_b200.torch import _core
+    g = META["gpt2"]
+    model = sft.convert(_gpt2(), dtype="sf16")
+    ids = torch.from_numpy(ARR[g["ids"]])
+    with torch.no_grad():
+        model(ids)
+        before = _core.device_path_calls
+        seen = []
+        hooks = [m.register_forward_hook(lambda mod, i, o: seen.append((mod.sf_name, sha(o))))
+                 for m in model.modules() if hasattr(m, "sf_name")]
+        sft.reset_status()
+        y = model(ids)
+        for h in hooks:
+            h.remove()
+    assert _core.device_path_calls == before + 49
+    st = sft.last_status(model)
+    for (name, out_sha), lay in zip(seen, g["layers"]):
+        assert out_sha == lay["out_sha"], name
+        _check_status(st[name], lay["status"], name)
+    assert sha(y.logits) == g["logits_sha"]
+
+
+def test_nan_input_on_a_prepared_layer_takes_the_policy(gpu):
+    lin = sft.convert(nn.Sequential(nn.Linear(8, 4)))[0]
+    x = torch.randn(3, 8)
+    with torch.no_grad():
+        lin(x)
+        x[1, 2] = float("nan")
+        with pytest.raises(sf.SFInvalidError):
+            lin(x)
+        with sf.errstate(invalid="ignore"):
+            y = lin(x)
+    assert torch.isfinite(y).all()
