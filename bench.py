@@ -228,19 +228,29 @@ def main():
     targs = {"add": (tx, ty), "sub": (tx, ty), "mul": (tx, ty), "fma": (tx, ty, tz), "div": (tx, td)}
     stream = torch.cuda.current_stream()
 
-    def step(evs=None):
-        counts.zero_()
+    # one count buffer per step: a step's status all-reduce runs on NCCL's stream
+    # while the next step's kernels run; the timed region waits for every one
+    bufs = [torch.zeros_like(counts) for _ in range(max(args.steps, args.warmup))]
+    pending = []
+
+    def step(evs=None, buf=None):
+        buf.zero_()
         for i, op in enumerate(OPS):
             if evs is not None:
                 evs[op][0].record(stream)
-            dev.run_device(op, fmt, *targs[op], out=outs[op], counts=counts[i])
+            dev.run_device(op, fmt, *targs[op], out=outs[op], counts=buf[i])
             if evs is not None:
                 evs[op][1].record(stream)
         if world > 1:
-            dist.all_reduce(counts)
+            pending.append(dist.all_reduce(buf, async_op=True))
 
-    for _ in range(args.warmup):
-        step()
+    def drain():
+        while pending:
+            pending.pop(0).wait()
+
+    for i in range(args.warmup):
+        step(buf=bufs[i])
+    drain()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -255,11 +265,13 @@ def main():
         dist.barrier()
     t_start.record(stream)
     evs_all = []
-    for _ in range(args.steps):
+    for i in range(args.steps):
         evs = {op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
-        step(evs)
+        step(evs, bufs[i])
         evs_all.append(evs)
+    drain()                                  # the last reductions are part of the timed work
     t_end.record(stream)
+    counts = bufs[args.steps - 1]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
