@@ -176,6 +176,17 @@ SFB_API int sfb_linear_scale(const void *x, int dtype, int64_t R, int64_t K, int
                              int64_t w_max_abs, int64_t w_max_col_l1, int has_bias, double need_max, double a_bias,
                              int16_t *codes, sfb_scale_result *result, void *scratch, sfb_stream stream);
 
+/* sfb_matmul_chain with a workspace: when the output has few tiles
+ * (batch 1), each output's K is split into pieces summarised in parallel and
+ * composed in order (the clamp-add maps of the chain compose exactly), the
+ * same bits as the sequential chain.  workspace: sfb_matmul_chain_workspace()
+ * bytes (0: no split); a smaller or null workspace runs the unsplit kernel. */
+SFB_API int64_t sfb_matmul_chain_workspace(int64_t batch, int64_t M, int64_t N, int64_t K);
+SFB_API int sfb_matmul_chain_ws(int bits, const int16_t *A, const int16_t *B, const int16_t *bias, int16_t *out,
+                                uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_out, void *workspace,
+                                int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
+
 /* sfb_linear_chain in proven mode with the activation scale read from
  * device memory (a_dev: the a of a finished sfb_linear_scale), so the
  * layer's kernels queue without a host round trip. */

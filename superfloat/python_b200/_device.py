@@ -192,8 +192,9 @@ class B200Device(Device):
             ws = self.workspace(_lib.reduce_workspace(1, K))
             _lib.dot(fmt.bits, a1, b1, K, o, fl, ws, cnt, stream=stream)
         elif op == "matmul":
-            _lib.matmul_chain(fmt.bits, A3, B3, bias, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
-                              sa, sb, M * N, stream=stream)
+            ws = self.workspace(_lib.chain_workspace(nb, M, N, K))
+            _lib.matmul_chain_ws(fmt.bits, A3, B3, bias, o, fl, cnt, nb, M, N, K, _ld(A3), _ld(B3),
+                                 sa, sb, M * N, ws, stream=stream)
         else:
             mxv = mx or self.mx
             sh_t = None

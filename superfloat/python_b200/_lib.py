@@ -46,6 +46,9 @@ SIGNATURES = {
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
     "sfb_linear_scale_scratch": (_i64, []),
+    "sfb_matmul_chain_workspace": (_i64, [_i64, _i64, _i64, _i64]),
+    "sfb_matmul_chain_ws": (_i32, [_i32, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                   _p, _i64, _p, _p]),
     "sfb_linear_scale": (_i32, [_p, _i32, _i64, _i64, _i64, _i32, _i64, _i64, _i32, ctypes.c_double, ctypes.c_double,
                                 _p, _p, _p, _p]),
     "sfb_linear_chain_dev": (_i32, [_i32, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p,
@@ -176,6 +179,21 @@ def quantize_auto(x, rows, cols, ld, scan_stats, m, bits, codes, ldc, stats, str
     rc = load().sfb_quantize_auto(_ptr(x), _fdtype(x), rows, cols, ld, _ptr(scan_stats), float(m), bits, _ptr(codes),
                                   ldc, _ptr(stats), _stream(stream))
     check(rc, "sf quantize (scale from scan)")
+
+
+def chain_workspace(batch, M, N, K) -> int:
+    n = load().sfb_matmul_chain_workspace(batch, M, N, K)
+    if n < 0:
+        check(int(n), "sf matmul (chain) workspace")
+    return int(n)
+
+
+def matmul_chain_ws(bits, A, B, bias, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so, workspace,
+                    stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_matmul_chain_ws(bits, _ptr(A), _ptr(B), _ptr(bias), _ptr(out), _ptr(flags), batch, M, N, K,
+                                    lda, ldb, sa, sb, so, _ptr(workspace), ws_bytes, _ptr(counts), _stream(stream))
+    check(rc, "sf matmul (chain)")
 
 
 SCALE_RESULT_WORDS = 8              # sfb_scale_result: a, a0 (float64), 6 x int64

@@ -48,6 +48,8 @@
 // half), hi = (word - lo) >> 16.  Underflow of lane L: bit 15 + 16 L of the
 // underflow word is clear.  A 384-thread CTA owns a 192 x 128 tile, 8 rows x
 // 4 lane pairs per thread, one CTA per SM.
+#include <algorithm>
+
 #include "sfb_common.cuh"
 
 namespace sfb {
@@ -472,6 +474,178 @@ __global__ void __launch_bounds__(NT, 1) chain_pk_kernel(const int16_t *__restri
     flush_counts(cnt, counts, sc);
 }
 
+// --- general mode with K split across CTAs ---------------------------------------------------
+//
+// For few output tiles the general chain leaves SMs idle.  Each step
+// v -> clip(v + t, -M, M) is a clamp-add map; a run of steps composes to
+// v -> clip(v + s, lo, hi), and the run is clip-free for an entry v exactly
+// when v + P stays in [-M, M] for every prefix sum P, i.e. v in
+// [-M - pmin, M - pmax]; these compose in order (s adds, lo / hi clamp
+// through the later run, pmax = max(pmaxA, sA + pmaxB), likewise pmin).  So
+// each CTA summarises one piece of K for its 64 x 64 tile, and a second
+// kernel composes the pieces in order from v = 0: the value is clip(s, lo,
+// hi), overflow is pmax > M or pmin < -M, underflow (a nonzero product
+// truncating to 0) is an OR.  The same bits as the sequential chain.
+
+struct Piece {
+    int s, lo, hi, pmax, pmin, under;
+};
+
+template <bool BITS16>
+__global__ void __launch_bounds__(THREADS, 1) chain_piece_kernel(const int16_t *__restrict__ A,
+                                                                 const int16_t *__restrict__ B, int M, int N, int K,
+                                                                 int64_t lda, int64_t ldb, int kspan, Width w0,
+                                                                 int vec, Piece *__restrict__ ws) {
+    constexpr int TM = 4, BM = 64;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    Stage<BM> *st = reinterpret_cast<Stage<BM> *>(smem_raw);
+    const Width w = BITS16 ? Width{16, 15, 32767} : w0;
+    const int tid = threadIdx.x;
+    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int piece = blockIdx.z;
+    const int kbeg = piece * kspan, kend = min(K, kbeg + kspan);
+    int sum[TM][TN], lo[TM][TN], hi[TM][TN], pmax[TM][TN], pmin[TM][TN];
+    uint32_t um[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++)
+            sum[i][j] = 0, lo[i][j] = -(1 << 30), hi[i][j] = 1 << 30, pmax[i][j] = -(1 << 30),
+            pmin[i][j] = 1 << 30, um[i][j] = 0xFFFFFFFFu;
+
+    constexpr int TPR = THREADS / BM, PER = BK / TPR;
+    const int ar = tid / TPR, ah = tid % TPR;
+    const int bk = tid >> 3, bc = (tid & 7) * 8;
+    Pack8 ra[PER / 8], rb;
+    auto load_regs = [&](int k0) {
+        const int gm = m0 + ar;
+        const int ka = k0 + ah * PER;
+#pragma unroll
+        for (int q = 0; q < PER / 8; q++) {
+            const int kq = ka + q * 8;
+            if (vec && gm < M && kq + 8 <= kend) {
+                ra[q].u = __ldg(reinterpret_cast<const uint4 *>(A + (int64_t)gm * lda + kq));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    ra[q].h[j] = (gm < M && kq + j < kend) ? A[(int64_t)gm * lda + kq + j] : (int16_t)0;
+            }
+        }
+        const int gk = k0 + bk, gn0 = n0 + bc;
+        if (vec && gk < kend && gn0 + 8 <= N) {
+            rb.u = __ldg(reinterpret_cast<const uint4 *>(B + (int64_t)gk * ldb + gn0));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                rb.h[j] = (gk < kend && gn0 + j < N) ? B[(int64_t)gk * ldb + gn0 + j] : (int16_t)0;
+        }
+    };
+    auto store_regs = [&](Stage<BM> &sg) {
+#pragma unroll
+        for (int q = 0; q < PER / 8; q++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int v = ra[q].h[j];
+                const int kk = ah * PER + q * 8 + j;
+                sg.a_abs[kk][ar] = (uint32_t)abs(v);
+                sg.a_sgn[kk][ar] = v >> 31;
+            }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int v = rb.h[j];
+            sg.b_abs[bk][bc + j] = (uint32_t)abs(v);
+            sg.b_sgn[bk][bc + j] = v >> 31;
+        }
+    };
+
+    const int nk = (kend - kbeg + BK - 1) / BK;
+    if (nk > 0) {
+        load_regs(kbeg);
+        store_regs(st[0]);
+    }
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        Stage<BM> &cur = st[kt & 1];
+        if (kt + 1 < nk) load_regs(kbeg + (kt + 1) * BK);
+        const int kn = min(BK, kend - (kbeg + kt * BK));     // padded steps are skipped: they are not in the chain
+        for (int k = 0; k < kn; k++) {
+            uint32_t aa[TM], ba[TN];
+            int32_t as_[TM], bs_[TN];
+#pragma unroll
+            for (int i = 0; i < TM; i++) aa[i] = cur.a_abs[k][ty * TM + i], as_[i] = cur.a_sgn[k][ty * TM + i];
+#pragma unroll
+            for (int j = 0; j < TN; j++) ba[j] = cur.b_abs[k][tx * TN + j], bs_[j] = cur.b_sgn[k][tx * TN + j];
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) {
+                    const uint32_t p = aa[i] * ba[j];
+                    const int32_t sg = as_[i] ^ bs_[j];
+                    const int32_t t = (((int32_t)(p >> w.sh)) ^ sg) - sg;
+                    um[i][j] = min(um[i][j], p - 1u);
+                    sum[i][j] += t;
+                    pmax[i][j] = max(pmax[i][j], sum[i][j]);
+                    pmin[i][j] = min(pmin[i][j], sum[i][j]);
+                    lo[i][j] = clampi(lo[i][j] + t, -w.M, w.M);
+                    hi[i][j] = clampi(hi[i][j] + t, -w.M, w.M);
+                }
+        }
+        if (kt + 1 < nk) store_regs(st[(kt + 1) & 1]);
+        __syncthreads();
+    }
+    const uint32_t unit_m1 = (1u << w.sh) - 1u;
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int gm = m0 + ty * TM + i;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int gn = n0 + tx * TN + j;
+            if (gm < M && gn < N)
+                ws[((int64_t)piece * M + gm) * N + gn] =
+                    Piece{sum[i][j], lo[i][j], hi[i][j], pmax[i][j], pmin[i][j], um[i][j] < unit_m1 ? 1 : 0};
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) chain_combine_kernel(const Piece *__restrict__ ws, int pieces, int M, int N,
+                                                            Width w, Epi e, sfb_counts *counts) {
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    Counts cnt;
+    const int64_t total = (int64_t)M * N;
+    for (int64_t o = (int64_t)blockIdx.x * 256 + threadIdx.x; o < total; o += (int64_t)gridDim.x * 256) {
+        long long s = 0, lo = -(1ll << 62), hi = 1ll << 62, pmax = -(1ll << 62), pmin = 1ll << 62;
+        int under = 0;
+        for (int p = 0; p < pieces; p++) {
+            const Piece b = ws[(int64_t)p * total + o];
+            if (b.pmax == -(1 << 30)) continue;                 // an empty piece (the identity)
+            lo = lo + b.s < b.lo ? b.lo : (lo + b.s > b.hi ? b.hi : lo + b.s);
+            hi = hi + b.s < b.lo ? b.lo : (hi + b.s > b.hi ? b.hi : hi + b.s);
+            pmax = max(pmax, s + b.pmax);
+            pmin = min(pmin, s + b.pmin);
+            s += b.s;
+            under |= b.under;
+        }
+        const int v = (int)(s < lo ? lo : (s > hi ? hi : s));
+        const bool over = pmax > w.M || pmin < -w.M;
+        const int gn = (int)(o % N);
+        emit(e, w, o, gn, v, over, under != 0, cnt);
+    }
+    flush_counts(cnt, counts, sc);
+}
+
+// pieces for a general chain of few tiles (1: no split)
+int chain_pieces(int64_t batch, int64_t M, int64_t N, int64_t K) {
+    if (batch != 1 || K < 4 * BK) return 1;
+    const int64_t tiles = ((M + 63) / 64) * ((N + BN - 1) / BN);
+    const int64_t want = (2 * (int64_t)sm_count() + tiles - 1) / tiles;            // one wave at 2 CTAs per SM
+    const int64_t most = std::max<int64_t>(1, K / (2 * BK));
+    const int64_t p = std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(want, most), 16));
+    // a piece sums at most 2^15 products in int32 (|sum| < 2^30, below the empty-piece marker)
+    return (K + p - 1) / p <= 32768 - BK ? (int)p : 1;
+}
+
 int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int64_t batch, int64_t M, int64_t N,
                  int64_t K, int64_t lda, int64_t ldb, int64_t sa, int64_t sb, int64_t so, bool safe,
                  sfb_counts *counts, cudaStream_t st, const char *what) {
@@ -568,4 +742,52 @@ extern "C" int sfb_linear_chain_dev(int bits, const int16_t *X, const int16_t *W
     Epi e{bias, 0.0, a_dev, s_col, y32, y64, codes, flags};
     return launch_chain(bits, X, WT, e, 1, R, N, K, ldx, ldw, 0, 0, R * N, true, counts, (cudaStream_t)stream,
                         "sfb_linear_chain_dev");
+}
+
+extern "C" int64_t sfb_matmul_chain_workspace(int64_t batch, int64_t M, int64_t N, int64_t K) {
+    using namespace sfb;
+    if (batch < 0 || M < 0 || N < 0 || K < 0) return set_error(SFB_EINVAL, "sfb_matmul_chain_workspace: bad size");
+    const int p = chain_pieces(batch, M, N, K);
+    return p > 1 ? (int64_t)p * M * N * (int64_t)sizeof(Piece) : 0;
+}
+
+extern "C" int sfb_matmul_chain_ws(int bits, const int16_t *A, const int16_t *B, const int16_t *bias, int16_t *out,
+                                   uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                   int64_t ldb, int64_t stride_a, int64_t stride_b, int64_t stride_out,
+                                   void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    int rc = chain_args("sfb_matmul_chain_ws", bits, A, B, batch, M, N, K, lda, ldb, stride_out);
+    if (rc) return rc;
+    if (batch == 0 || M == 0 || N == 0) return SFB_OK;
+    if (out == nullptr) return set_error(SFB_EINVAL, "sfb_matmul_chain_ws: null output");
+    Epi e{bias, 0.0, nullptr, nullptr, nullptr, nullptr, out, flags};
+    cudaStream_t st = (cudaStream_t)stream;
+    const int pieces = chain_pieces(batch, M, N, K);
+    const int64_t need = pieces > 1 ? (int64_t)pieces * M * N * (int64_t)sizeof(Piece) : 0;
+    if (pieces <= 1 || workspace == nullptr || workspace_bytes < need || M > 0x7fffffff || N > 0x7fffffff)
+        return launch_chain(bits, A, B, e, batch, M, N, K, lda, ldb, stride_a, stride_b, stride_out, false, counts,
+                            st, "sfb_matmul_chain_ws");
+    const int kspan = (int)(((K + pieces - 1) / pieces + BK - 1) / BK * BK);
+    const int np = (int)((K + kspan - 1) / kspan);
+    const Width w = width(bits);
+    const int vec = (lda % 8 == 0) && (ldb % 8 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0);
+    const int smem = 2 * (int)sizeof(Stage<64>);
+    auto kern = bits == 16 ? chain_piece_kernel<true> : chain_piece_kernel<false>;
+    static bool attr[64][2] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr[dev][bits == 16]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return check_launch("sfb_matmul_chain_ws");
+        attr[dev][bits == 16] = true;
+    }
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 63) / 64), (unsigned)np);
+    Piece *ws = reinterpret_cast<Piece *>(workspace);
+    kern<<<grid, THREADS, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, kspan, w, vec, ws);
+    rc = check_launch("sfb_matmul_chain_ws (pieces)");
+    if (rc) return rc;
+    const int64_t g = std::min<int64_t>((M * N + 255) / 256, (int64_t)sm_count() * 8);
+    chain_combine_kernel<<<(unsigned)std::max<int64_t>(g, 1), 256, 0, st>>>(ws, np, (int)M, (int)N, w, e, counts);
+    return check_launch("sfb_matmul_chain_ws (combine)");
 }

@@ -20,7 +20,7 @@ def sha_mask(m):
 
 
 SHAPES = [(1, 1, 1), (1, 7, 1), (5, 3, 9), (64, 64, 32), (65, 63, 33), (130, 70, 257), (3, 200, 64),
-          (100, 1, 100), (7, 7, 0)]
+          (100, 1, 100), (7, 7, 0), (5, 9, 4099), (64, 64, 1000)]
 
 
 def _codes(rng, bits, shape, frac=1.0):
