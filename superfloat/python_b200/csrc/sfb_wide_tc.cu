@@ -4,21 +4,29 @@
 // is t = (a w + 80 - C) >> 8 with C = C(a mod 64, w mod 64) the dropped
 // partial-product columns, C(x, y) = sum_{i<6} x_i ((y << i) mod 64).  Writing
 // X = (a w - C) / 64 (an integer), t = (X + 1) >> 2, so with s = +-1 the
-// product's sign and r = (X + 1) mod 4:
+// product's sign, r = (X + 1) mod 4 and u = r for a positive product, 3 - r for
+// a negative one (s t = (s X + 1 + [s < 0] - u) / 4 either way):
 //
-//     4 sum_k s t = sum_k s (a w - C) / 64  +  sum_k s (1 - r).
+//     4 sum_k s t = sum_k s X - (sum_k s) / 2 + 3 K / 2 - sum_k u
 //
-// * sum s (a w - C) is exact integer linear algebra on int8 operands:
+// over the K padded to a multiple of 128 (padded products are 0 with s = +1).
+// * sum s X - (sum s) / 2 is exact integer linear algebra on int8 operands:
 //   the left-aligned signed codes k = s a split into limbs k = 256 h + l
-//   (h signed, l unsigned) give 4 GEMMs, and sum s C = sum_i (s_a bit_i(a))
-//   (s_w ((w << i) mod 64)) 6 more.  They run as tcgen05 kind::i8 MMAs into
-//   three s32 TMEM accumulators by scale: D0 = h.h (x 2^16), D1 = h.l + l.h
-//   (x 2^8), D2 = l.l - sum_i bit_i . C_i (x 1; the C planes are stored
-//   negated).  |D| < 2^31 for K <= 16384.
-// * sum s (1 - r) needs r per product: X mod 4 = (P + 2Q) mod 4 with
-//   P = sum_{i<=6} a_i w_{6-i}, Q = sum_{i<=7} a_i w_{7-i} over the low bits,
-//   computed bit-sliced on the INT pipe, 32 products per 32-bit word
-//   (kernel wide_rem_kernel), about one logic op per product.
+//   (h signed, l unsigned) give 4 GEMMs, sum s C = sum_i (s_a bit_i(a))
+//   (s_w ((w << i) mod 64)) 6 more, and (+-1) (-+32) sign planes the 11th.
+//   They run as tcgen05 kind::i8 MMAs into three s32 TMEM accumulators by
+//   scale: D0 = h.h (x 2^16), D1 = h.l + l.h (x 2^8), D2 = l.l - sum_i bit_i .
+//   C_i - 32 sum s (x 1; the C planes are stored negated).  |D| < 2^31 for
+//   K <= 16384.
+// * sum u needs r per product: X mod 4 = (P + 2Q) mod 4 over the low bytes x
+//   of a and y of w (P = sum_{i<=6} x_i y_{6-i}, Q = sum_{i<=7} x_i y_{7-i}),
+//   which splits by the nibbles of x into F(x mod 16) + G(x >> 4), each a sum
+//   of x's bits times two-bit words of y's bits.  Bit-sliced over 32 columns,
+//   F and G are 16-entry tables of two-bit words per (k, column word), built
+//   once per CTA and read by every row; w's sign and the +1 are folded into
+//   the tables and a's sign selects a complemented copy, so u for 32 products
+//   is two shared-memory reads and a two-bit add (kernel wide_rem_kernel),
+//   summed over k in carry-save bit-plane counters.
 //
 // The sum is the MX accumulator when no chunk of 8 can clip; each output is
 // checked against the bound sum_k |t_k| <= min(rowL1 colmax, rowmax colL1)/256
@@ -30,7 +38,7 @@
 // swizzle) into a ring of stages; thread 32 issues the MMAs (one thread, as
 // tcgen05 requires) and commits each stage back to the producer; all four
 // warps then read the TMEM accumulators (tcgen05.ld, one 32-lane quarter per
-// warp) and write sum s (a w - C) / 64 as int64.  Every wait is bounded: on
+// warp) and write sum s X - (sum s) / 2 as int64.  Every wait is bounded: on
 // timeout the kernel records an error in the caller's counters and returns
 // after freeing its TMEM.
 #include <cuda.h>
@@ -50,8 +58,8 @@ namespace {
 
 constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
 constexpr int STAGES = 6;
-constexpr int NPASS = 10;
-constexpr int NPLANES = 8;         // int8 operand planes per matrix
+constexpr int NPASS = 11;
+constexpr int NPLANES = 9;         // int8 operand planes per matrix
 constexpr int STAGE_BYTES = 2 * TILE * TILE;
 constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int KMAX = 16384;        // |D| < 2^31 up to this K
@@ -60,7 +68,7 @@ constexpr unsigned kSpinLimit = 1u << 26;
 // pass -> (A plane, B plane, accumulator, A signed, B signed)
 __constant__ int c_pass[NPASS][5] = {
     {0, 0, 0, 1, 1}, {0, 1, 1, 1, 0}, {1, 0, 1, 0, 1}, {1, 1, 2, 0, 0}, {2, 2, 2, 1, 1},
-    {3, 3, 2, 1, 1}, {4, 4, 2, 1, 1}, {5, 5, 2, 1, 1}, {6, 6, 2, 1, 1}, {7, 7, 2, 1, 1}};
+    {3, 3, 2, 1, 1}, {4, 4, 2, 1, 1}, {5, 5, 2, 1, 1}, {6, 6, 2, 1, 1}, {7, 7, 2, 1, 1}, {8, 8, 2, 1, 1}};
 
 // --- PTX wrappers --------------------------------------------------------------------------
 
@@ -154,20 +162,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 
 // --- operand preparation ------------------------------------------------------------------
 //
-// One thread per (row, 32-k word).  Writes the eight int8 planes (h, l,
-// bit_0..bit_5 of A; h, l, -C_0..-C_5 of B), the nine bit planes of the
-// remainder (bits 0..7 of the magnitude and the sign, 32 k per word), and the
-// row / column L1 norm and maximum of the magnitudes.
+// One thread per (row, 32-k word).  Writes the nine int8 planes (h, l,
+// bit_0..bit_5, sign +-1 of A; h, l, -C_0..-C_5, sign -+32 of B), the row /
+// column L1 norm and maximum of the magnitudes, and for A the remainder's
+// per-product record: byte 0 = (x mod 16) + 16 s, byte 1 = (x >> 4) + 16 s
+// (x the magnitude's low byte, s its sign), two k per 32-bit word, laid out
+// [k / 2][row].
 
 template <bool IS_A>
 __global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X, int64_t ld, int rows, int K,
                                                    int rows_pad, int Kp, int bits, uint8_t *__restrict__ planes,
-                                                   uint32_t *__restrict__ bitp, long long *__restrict__ l1,
+                                                   uint16_t *__restrict__ rec, long long *__restrict__ l1,
                                                    int *__restrict__ mx) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     const int kw = blockIdx.y;
     if (r >= rows_pad) return;
-    uint32_t bw[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
     long long sum = 0;
     int mval = 0;
     const int sh = 16 - bits;
@@ -177,6 +186,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X
         for (int p = 0; p < NPLANES; p++)
 #pragma unroll
             for (int q = 0; q < 4; q++) pw[p][q] = 0;
+        uint32_t rw[8];
 #pragma unroll
         for (int jj = 0; jj < 16; jj++) {
             const int j = half * 16 + jj;
@@ -195,9 +205,14 @@ __global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X
                 if (s) v = -v;
                 pw[2 + i][jj >> 2] |= ((uint32_t)v & 0xFFu) << sh8;
             }
-#pragma unroll
-            for (int i = 0; i < 8; i++) bw[i] |= (uint32_t)((a >> i) & 1) << j;
-            bw[8] |= (uint32_t)s << j;
+            const int sg = IS_A ? (s ? -1 : 1) : (s ? 32 : -32);        // product -32 s
+            pw[8][jj >> 2] |= ((uint32_t)sg & 0xFFu) << sh8;
+            if (IS_A) {
+                const uint32_t e = (uint32_t)(s << 4);
+                const uint32_t v = ((a & 15) + e) | ((((a >> 4) & 15) + e) << 8);
+                if (jj & 1) rw[jj >> 1] |= v << 16;
+                else rw[jj >> 1] = v;
+            }
             sum += a;
             mval = max(mval, a);
         }
@@ -206,14 +221,49 @@ __global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X
             uint4 *dst = reinterpret_cast<uint4 *>(planes + ((int64_t)p * rows_pad + r) * Kp + kw * 32 + half * 16);
             *dst = make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
         }
-    }
+        if (IS_A) {
+            uint32_t *rp = reinterpret_cast<uint32_t *>(rec);
 #pragma unroll
-    for (int i = 0; i < 9; i++) bitp[((int64_t)kw * 9 + i) * rows_pad + r] = bw[i];
+            for (int q = 0; q < 8; q++) rp[(int64_t)(kw * 16 + half * 8 + q) * rows_pad + r] = rw[q];
+        }
+    }
     if (sum) atomicAdd(reinterpret_cast<unsigned long long *>(l1 + r), (unsigned long long)sum);
     if (mval) atomicMax(mx + r, mval);
 }
 
-// --- the tcgen05 GEMM: sum_k s (a w - C) / 64 per output -----------------------------------
+// B's bits sliced over columns: for each k and 32-column word, the low byte
+// y of the magnitudes as eight bit planes and the signs, laid out
+// [k][plane 0..8][column word].  A block is four warps (128 columns) over 8 k.
+constexpr int BN_KB = 8;
+
+__global__ void __launch_bounds__(128) bits_n_kernel(const int16_t *__restrict__ B, int64_t ldb, int N, int K, int NWt,
+                                                     int bits, uint32_t *__restrict__ bn) {
+    __shared__ uint32_t st[9][4];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int n = blockIdx.x * 128 + threadIdx.x;
+    const int sh = 16 - bits;
+    for (int kk = 0; kk < BN_KB; kk++) {
+        const int k = blockIdx.y * BN_KB + kk;
+        const int code = (n < N && k < K) ? (int)B[(int64_t)k * ldb + n] : 0;
+        const int y = (abs(code) << sh) & 255;
+        uint32_t mine = 0;
+#pragma unroll
+        for (int p = 0; p < 8; p++) {
+            const uint32_t word = __ballot_sync(0xffffffffu, (y >> p) & 1);
+            if (lane == p) mine = word;
+        }
+        const uint32_t sw = __ballot_sync(0xffffffffu, code < 0);
+        if (lane == 8) mine = sw;
+        if (lane < 9) st[lane][w] = mine;
+        __syncthreads();
+        if (threadIdx.x < 9)
+            *reinterpret_cast<uint4 *>(bn + ((int64_t)k * 9 + threadIdx.x) * NWt + blockIdx.x * 4) =
+                make_uint4(st[threadIdx.x][0], st[threadIdx.x][1], st[threadIdx.x][2], st[threadIdx.x][3]);
+        __syncthreads();
+    }
+}
+
+// --- the tcgen05 GEMM: sum_k s X - (sum_k s) / 2 per output ---------------------------------
 
 __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB, int nkb,
@@ -309,7 +359,7 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
 #pragma unroll
             for (int j = 0; j < 32; j++) {
                 const long long t = ((long long)d0[j] << 16) + ((long long)d1[j] << 8) + (long long)d2[j];
-                dst[c * 32 + j] = t >> 6;            // exact: the total is 64 sum s X
+                dst[c * 32 + j] = t >> 6;            // exact: the total is 64 sum s X - 32 sum s, sum s even
             }
         }
     } else if (threadIdx.x == 0) {
@@ -323,18 +373,68 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
-// --- the bit-sliced remainder, the combination and POP ---------------------------------------
+// --- the remainder sum_k u, the combination and POP -----------------------------------------
+//
+// One CTA per 256 rows x 128 columns: a lane owns one row, and for each of
+// its four 32-column words keeps sum_k u as carry-save bit planes (bit b of
+// a plane belongs to column 32 word + b).  K runs in chunks of 16, double
+// buffered in shared memory: the rows' records and B's column-sliced bits
+// arrive by cp.async, then every thread builds half of one (k, word) table,
+// and the rows read them.
+//
+// A table entry is a two-bit word (two 32-bit planes) per (k, word, index).
+// The F half, indexed by (x mod 16) + 16 s_a, holds F* = s_w ? ~F : F + 1 for
+// s_a = 0 and -F* for s_a = 1; the G half, indexed by (x >> 4) + 16 s_a,
+// holds G* = s_w ? ~G : G and ~G*.  Then u = F-entry + G-entry (mod 4):
+// u' = F* + G* is r for a positive w and 3 - r for a negative one, and
+// ~u' = (-F*) + ~G* flips it for a negative a.  Built as sums of the nibble
+// bits' terms d_i = (y_{6-i}, y_{7-i}), negated where s_w (the start values
+// (1, s_w) and (s_w, s_w) are F* and G* of 0).
+//
+// Entry (e, table t) sits at (e * 65 + t) * 8 bytes of its half: the 16
+// entries one row-lane can read of one table fall in distinct bank pairs,
+// and the builders (consecutive t) store to consecutive words.
 
-constexpr int RT = 64;     // output tile of the remainder kernel
-constexpr int KC = 8;      // 32-k words per shared-memory chunk
+constexpr int RM = 256;                    // rows per CTA: 8 warps, one row per lane
+constexpr int RNW = 4;                     // 32-column words per CTA
+constexpr int RKC = 16;                    // k per chunk: two blocks of 8
+constexpr int RNTAB = RKC * RNW;           // tables per chunk
+constexpr int RTSTR = RNTAB + 1;           // entry stride in tables (odd)
+constexpr int RENT = 32;                   // entries per half: 16 nibbles x 2 signs of a
+constexpr int TAB_HALF = RENT * RTSTR * 8;
+constexpr int TAB_BYTES = 2 * TAB_HALF;
+constexpr int REC_BYTES = (RKC / 2) * RM * 4;
+constexpr int BST_BYTES = RKC * 9 * RNW * 4;
+constexpr int BUF_BYTES = TAB_BYTES + REC_BYTES + BST_BYTES;
+constexpr int NPL = 17;                    // counter planes per column word
+constexpr int EPI_BYTES = RNW * NPL * RM * 4;
+constexpr int REM_SMEM = (2 * BUF_BYTES > EPI_BYTES) ? 2 * BUF_BYTES : EPI_BYTES;
+static_assert(BUF_BYTES % 16 == 0 && TAB_BYTES % 16 == 0 && REC_BYTES % 16 == 0, "cp.async alignment");
 
-__device__ __forceinline__ uint32_t maj3(uint32_t x, uint32_t y, uint32_t z) { return (x & y) | (z & (x ^ y)); }
+__device__ __forceinline__ void cp16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+struct W2 {
+    uint32_t lo, hi;
+};
+
+__device__ __forceinline__ W2 add2(W2 a, W2 b) { return W2{a.lo ^ b.lo, a.hi ^ b.hi ^ (a.lo & b.lo)}; }
+
+// s + a + b = (s ^ a ^ b) + 2 maj(s, a, b), bit by bit: s keeps the sum, the carry is returned
+__device__ __forceinline__ uint32_t csa(uint32_t &s, uint32_t a, uint32_t b) {
+    const uint32_t c = (s & a) | (s & b) | (a & b);
+    s ^= a ^ b;
+    return c;
+}
 
 struct RemIn {
-    const uint32_t *bitsA, *bitsB;
+    const uint32_t *rec, *bn;
     const long long *SX, *rowL1, *colL1;
     const int *rowMax, *colMax;
-    int Mp, Np, KW;
+    int Mp, Np, Kp, NWt;
     const int16_t *A, *B;
     int64_t lda, ldb;
     int M, N, K;
@@ -370,101 +470,224 @@ __device__ long long exact_output(const RemIn &in, int m, int n, bool &clip) {
 }
 
 __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
-    extern __shared__ __align__(16) uint32_t rs[];
-    uint32_t *sA = rs;                      // [KC][9][RT]
-    uint32_t *sB = rs + KC * 9 * RT;        // [KC][9][RT]
+    extern __shared__ __align__(16) uint8_t rsm[];
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * RT, n0 = blockIdx.x * RT;
-    int acc1[4][4], acc2[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) acc1[i][j] = 0, acc2[i][j] = 0;
+    const int tid = threadIdx.x;
+    const int ml = tid;                          // this lane's row within the tile
+    const int m0 = blockIdx.y * RM, nw0 = blockIdx.x * RNW, n0 = nw0 * 32;
 
-    for (int kw0 = 0; kw0 < in.KW; kw0 += KC) {
-        const int nkw = min(KC, in.KW - kw0);
-        __syncthreads();
-        for (int e = tid; e < nkw * 9 * (RT / 4); e += 256) {
-            const int q = e % (RT / 4), p = (e / (RT / 4)) % 9, kk = e / (9 * (RT / 4));
-            const int64_t ga = ((int64_t)(kw0 + kk) * 9 + p) * in.Mp + m0 + q * 4;
-            const int64_t gb = ((int64_t)(kw0 + kk) * 9 + p) * in.Np + n0 + q * 4;
-            reinterpret_cast<uint4 *>(sA)[(kk * 9 + p) * (RT / 4) + q] = *reinterpret_cast<const uint4 *>(in.bitsA + ga);
-            reinterpret_cast<uint4 *>(sB)[(kk * 9 + p) * (RT / 4) + q] = *reinterpret_cast<const uint4 *>(in.bitsB + gb);
-        }
-        __syncthreads();
-        for (int kk = 0; kk < nkw; kk++) {
-            uint4 pa[9], pb[9];
+    // carry-save counters per column word: weights 1..16 (block level), 32, 64 (+ a
+    // pending 64), then a binary counter 128 .. 32768 (sum u <= 3 K < 2^16)
+    uint32_t p1[RNW], p2[RNW], p4[RNW], p8[RNW], p16[RNW], h32[RNW], pend32[RNW], h64[RNW], pend64[RNW];
+    uint32_t hh[RNW][9];
 #pragma unroll
-            for (int p = 0; p < 9; p++) {
-                pa[p] = reinterpret_cast<const uint4 *>(sA)[(kk * 9 + p) * (RT / 4) + ty];
-                pb[p] = reinterpret_cast<const uint4 *>(sB)[(kk * 9 + p) * (RT / 4) + tx];
+    for (int v = 0; v < RNW; v++) {
+        p1[v] = p2[v] = p4[v] = p8[v] = p16[v] = h32[v] = pend32[v] = h64[v] = pend64[v] = 0;
+#pragma unroll
+        for (int l = 0; l < 9; l++) hh[v][l] = 0;
+    }
+
+    auto load_chunk = [&](int c, int q) {
+        uint8_t *buf = rsm + q * BUF_BYTES;
+        const uint32_t *src = in.rec + (int64_t)c * (RKC / 2) * in.Mp + m0;
+        for (int i = tid; i < (RKC / 2) * RM / 4; i += 256) {
+            const int row = i / (RM / 4), col = i % (RM / 4);
+            cp16(smem_u32(buf + TAB_BYTES + (row * RM + col * 4) * 4), src + (int64_t)row * in.Mp + col * 4);
+        }
+        if (tid < RKC * 9) {
+            const int kk = tid / 9, p = tid % 9;
+            cp16(smem_u32(buf + TAB_BYTES + REC_BYTES + (kk * 9 + p) * RNW * 4),
+                 in.bn + ((int64_t)(c * RKC + kk) * 9 + p) * in.NWt + nw0);
+        }
+        cp_commit();
+    };
+
+    auto build = [&](int q) {
+        uint8_t *buf = rsm + q * BUF_BYTES;
+        const uint32_t *bs = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES + REC_BYTES);
+        const int t = tid & (RNTAB - 1), half = (tid >> 6) & 1, hi = tid >> 7;
+        const int kk = t / RNW, v = t % RNW;
+        uint32_t y[9];
+#pragma unroll
+        for (int p = 0; p < 9; p++) y[p] = bs[(kk * 9 + p) * RNW + v];
+        const uint32_t sw = y[8];
+        W2 d[4], start;
+        if (half == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) d[i] = W2{y[6 - i], y[7 - i]};
+            start = W2{0xFFFFFFFFu, sw};
+        } else {
+            d[0] = W2{y[2], y[3]};
+            d[1] = W2{y[1], y[2]};
+            d[2] = W2{y[0], y[1]};
+            d[3] = W2{0u, y[0]};
+            start = W2{sw, sw};
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) d[i].hi ^= d[i].lo & sw;         // -d where w is negative
+        W2 e[8];
+        e[0] = hi ? add2(start, d[3]) : start;
+        e[1] = add2(e[0], d[0]);
+        e[2] = add2(e[0], d[1]);
+        e[3] = add2(e[1], d[1]);
+        e[4] = add2(e[0], d[2]);
+        e[5] = add2(e[4], d[0]);
+        e[6] = add2(e[4], d[1]);
+        e[7] = add2(e[5], d[1]);
+        uint2 *tab = reinterpret_cast<uint2 *>(buf + half * TAB_HALF);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int idx = hi * 8 + j;
+            tab[idx * RTSTR + t] = make_uint2(e[j].lo, e[j].hi);
+            const W2 c = half == 0 ? W2{e[j].lo, e[j].hi ^ e[j].lo} : W2{~e[j].lo, ~e[j].hi};
+            tab[(idx + 16) * RTSTR + t] = make_uint2(c.lo, c.hi);
+        }
+    };
+
+    auto hot = [&](int c, int q) {
+        const uint8_t *buf = rsm + q * BUF_BYTES;
+        const uint32_t *recs = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES);
+        uint32_t c64[RNW];
+#pragma unroll
+        for (int b = 0; b < 2; b++) {
+            const uint8_t *aF[8], *aG[8];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t r = recs[(b * 4 + j) * RM + ml];
+                aF[2 * j] = buf + __byte_perm(r, 0, 0x4440) * (RTSTR * 8) + (b * 8 + 2 * j) * RNW * 8;
+                aG[2 * j] = buf + TAB_HALF + __byte_perm(r, 0, 0x4441) * (RTSTR * 8) + (b * 8 + 2 * j) * RNW * 8;
+                aF[2 * j + 1] = buf + __byte_perm(r, 0, 0x4442) * (RTSTR * 8) + (b * 8 + 2 * j + 1) * RNW * 8;
+                aG[2 * j + 1] =
+                    buf + TAB_HALF + __byte_perm(r, 0, 0x4443) * (RTSTR * 8) + (b * 8 + 2 * j + 1) * RNW * 8;
             }
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                uint32_t a[9];
+            for (int v = 0; v < RNW; v++) {
+                uint32_t u0[8], u1[8];
 #pragma unroll
-                for (int p = 0; p < 9; p++) a[p] = (&pa[p].x)[i];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    uint32_t w[9];
-#pragma unroll
-                    for (int p = 0; p < 9; p++) w[p] = (&pb[p].x)[j];
-                    // P = sum_{i<=6} a_i w_{6-i} mod 4 by a carry-save tree
-                    const uint32_t t0 = a[0] & w[6], t1 = a[1] & w[5], t2 = a[2] & w[4], t3 = a[3] & w[3];
-                    const uint32_t t4 = a[4] & w[2], t5 = a[5] & w[1], t6 = a[6] & w[0];
-                    const uint32_t s1 = t0 ^ t1 ^ t2, c1 = maj3(t0, t1, t2);
-                    const uint32_t s2 = t3 ^ t4 ^ t5, c2 = maj3(t3, t4, t5);
-                    const uint32_t x0 = s1 ^ s2 ^ t6, c3 = maj3(s1, s2, t6);
-                    // r1 = X1 ^ X0 = P1 ^ Q0 ^ X0, Q0 the parity of sum_{i<=7} a_i w_{7-i}
-                    uint32_t r1 = c1 ^ c2 ^ c3 ^ x0;
-                    r1 ^= (a[0] & w[7]) ^ (a[1] & w[6]) ^ (a[2] & w[5]) ^ (a[3] & w[4]);
-                    r1 ^= (a[4] & w[3]) ^ (a[5] & w[2]) ^ (a[6] & w[1]) ^ (a[7] & w[0]);
-                    const uint32_t neg = a[8] ^ w[8];
-                    acc1[i][j] += __popc(x0) + 4 * __popc(r1 & neg);
-                    acc2[i][j] += __popc(x0 & neg) + __popc(r1);
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint2 f = *reinterpret_cast<const uint2 *>(aF[kk] + v * 8);
+                    const uint2 g = *reinterpret_cast<const uint2 *>(aG[kk] + v * 8);
+                    u0[kk] = f.x ^ g.x;
+                    u1[kk] = f.y ^ g.y ^ (f.x & g.x);
+                }
+                // 8 words of weight 1 and 8 of weight 2 into the planes: one carry of weight 32 out
+                const uint32_t c2a = csa(p1[v], u0[0], u0[1]);
+                const uint32_t c4a = csa(p2[v], u1[0], u1[1]);
+                const uint32_t c2b = csa(p1[v], u0[2], u0[3]);
+                const uint32_t c4b = csa(p2[v], c2a, c2b);
+                const uint32_t c4c = csa(p2[v], u1[2], u1[3]);
+                const uint32_t c8a = csa(p4[v], c4a, c4b);
+                const uint32_t c2c = csa(p1[v], u0[4], u0[5]);
+                const uint32_t c4d = csa(p2[v], u1[4], u1[5]);
+                const uint32_t c8b = csa(p4[v], c4c, c4d);
+                const uint32_t c2d = csa(p1[v], u0[6], u0[7]);
+                const uint32_t c4e = csa(p2[v], c2c, c2d);
+                const uint32_t c4f = csa(p2[v], u1[6], u1[7]);
+                const uint32_t c8c = csa(p4[v], c4e, c4f);
+                const uint32_t c16a = csa(p8[v], c8a, c8b);
+                const uint32_t c16b = p8[v] & c8c;
+                p8[v] ^= c8c;
+                const uint32_t c32 = csa(p16[v], c16a, c16b);
+                if (b == 0) {
+                    pend32[v] = c32;
+                } else {
+                    c64[v] = csa(h32[v], pend32[v], c32);
+                    pend32[v] = 0;
                 }
             }
         }
+        if ((c & 1) == 0) {
+#pragma unroll
+            for (int v = 0; v < RNW; v++) pend64[v] = c64[v];
+        } else {
+#pragma unroll
+            for (int v = 0; v < RNW; v++) {
+                uint32_t cc = csa(h64[v], pend64[v], c64[v]);
+                pend64[v] = 0;
+#pragma unroll
+                for (int l = 0; l < 9; l++) {
+                    const uint32_t t = hh[v][l] & cc;
+                    hh[v][l] ^= cc;
+                    cc = t;
+                }
+            }
+        }
+    };
+
+    const int nch = in.Kp / RKC;
+    load_chunk(0, 0);
+    cp_wait_all();
+    __syncthreads();
+    build(0);
+    __syncthreads();
+    for (int c = 0; c < nch; c++) {
+        const int q = c & 1;
+        if (c + 1 < nch) load_chunk(c + 1, q ^ 1);
+        hot(c, q);
+        cp_wait_all();
+        __syncthreads();
+        if (c + 1 < nch) build(q ^ 1);
+        __syncthreads();
     }
+
+    // the planes to shared memory, [word][plane][row]; then one thread per output
+    uint32_t *pl = reinterpret_cast<uint32_t *>(rsm);
+#pragma unroll
+    for (int v = 0; v < RNW; v++) {
+        uint32_t *d = pl + (v * NPL) * RM + ml;
+        d[0 * RM] = p1[v];
+        d[1 * RM] = p2[v];
+        d[2 * RM] = p4[v];
+        d[3 * RM] = p8[v];
+        d[4 * RM] = p16[v];
+        d[5 * RM] = h32[v];
+        d[6 * RM] = h64[v];
+        d[7 * RM] = pend64[v];
+#pragma unroll
+        for (int l = 0; l < 9; l++) d[(8 + l) * RM] = hh[v][l];
+    }
+    __syncthreads();
 
     Counts cnt;
     const long long lim = (1ll << 31) - 1;
+    const long long half_k3 = 3ll * in.Kp / 2;
+    const int nl = tid & 127, vw = nl >> 5, bit = nl & 31;
+    const int n = n0 + nl;
+    for (int i = 0; i < RM / 2; i++) {
+        const int mloc = 2 * i + (tid >> 7);
+        const int m = m0 + mloc;
+        if (m >= in.M || n >= in.N) continue;
+        const uint32_t *src = pl + (vw * NPL) * RM + mloc;
+        long long U = 0;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int m = m0 + ty * 4 + i;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int n = n0 + tx * 4 + j;
-            if (m < in.M && n < in.N) {
-                const long long R = (long long)acc1[i][j] - 2ll * acc2[i][j];
-                long long S = (in.SX[(int64_t)m * in.Np + n] + R) >> 2;     // exact: 4 | (SX + R)
-                const long long b1 = in.rowL1[m] * (long long)in.colMax[n];
-                const long long b2 = (long long)in.rowMax[m] * in.colL1[n];
-                const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
-                bool cl = false;
-                if (!safe) S = exact_output(in, m, n, cl);
-                if (in.acc_out) {
-                    in.acc_out[(int64_t)m * in.N + n] = (int32_t)S;
-                    if (in.flags) in.flags[(int64_t)m * in.N + n] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
-                    cnt.clip += cl;
-                    continue;
-                }
-                const int sft = in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
-                bool over, under;
-                const int q = mx_pop(S, sft, in.u.F, in.w, over, under);
-                over |= cl;
-                in.out[(int64_t)m * in.N + n] = (int16_t)q;
-                if (in.flags)
-                    in.flags[(int64_t)m * in.N + n] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) |
-                                                                (under ? SFB_F_UNDERFLOW : 0u) |
-                                                                (cl ? SFB_F_ACC_CLIPPED : 0u));
-                cnt.over += over;
-                cnt.under += under;
-                cnt.clip += cl;
-            }
+        for (int l = 0; l < NPL; l++) {
+            const int wt = l < 7 ? l : l - 1;                    // planes 6 and 7 both weigh 64
+            U += (long long)((src[l * RM] >> bit) & 1u) << wt;
         }
+        long long S = (in.SX[(int64_t)m * in.Np + n] + half_k3 - U) >> 2;     // exact: a multiple of 4
+        const long long b1 = in.rowL1[m] * (long long)in.colMax[n];
+        const long long b2 = (long long)in.rowMax[m] * in.colL1[n];
+        const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
+        bool cl = false;
+        if (!safe) S = exact_output(in, m, n, cl);
+        if (in.acc_out) {
+            in.acc_out[(int64_t)m * in.N + n] = (int32_t)S;
+            if (in.flags) in.flags[(int64_t)m * in.N + n] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
+            cnt.clip += cl;
+            continue;
+        }
+        const int sft = in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
+        bool over, under;
+        const int qv = mx_pop(S, sft, in.u.F, in.w, over, under);
+        over |= cl;
+        in.out[(int64_t)m * in.N + n] = (int16_t)qv;
+        if (in.flags)
+            in.flags[(int64_t)m * in.N + n] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) | (under ? SFB_F_UNDERFLOW : 0u) |
+                                                        (cl ? SFB_F_ACC_CLIPPED : 0u));
+        cnt.over += over;
+        cnt.under += under;
+        cnt.clip += cl;
     }
     flush_counts(cnt, in.counts, sc);
 }
@@ -473,14 +696,14 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
 
 struct Layout {
     int64_t Mp, Np, Kp, KW;
-    int64_t off_pa, off_pb, off_ba, off_bb, off_l1a, off_l1b, off_mxa, off_mxb, off_sx, total;
+    int64_t off_pa, off_pb, off_ra, off_bn, off_l1a, off_l1b, off_mxa, off_mxb, off_sx, total;
 };
 
 int64_t up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 Layout layout_for(int64_t M, int64_t N, int64_t K) {
     Layout L;
-    L.Mp = up(M, TILE);
+    L.Mp = up(M, RM);               // the remainder kernel's row tile (a multiple of TILE)
     L.Np = up(N, TILE);
     L.Kp = up(K, TILE);
     L.KW = L.Kp / 32;
@@ -492,8 +715,8 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
     };
     L.off_pa = take(NPLANES * L.Mp * L.Kp);
     L.off_pb = take(NPLANES * L.Np * L.Kp);
-    L.off_ba = take(4 * 9 * L.KW * L.Mp);
-    L.off_bb = take(4 * 9 * L.KW * L.Np);
+    L.off_ra = take(2 * L.Kp * L.Mp);
+    L.off_bn = take(4 * 9 * L.Kp * (L.Np / 32));
     L.off_l1a = take(8 * L.Mp);
     L.off_l1b = take(8 * L.Np);
     L.off_mxa = take(4 * L.Mp);
@@ -568,13 +791,14 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(wide_rem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * KC * 9 * RT * 4) != cudaSuccess)
+                                 REM_SMEM) != cudaSuccess)
             return check_launch("sfb_matmul_wide (attributes)");
         smem_set[dev] = true;
     }
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);
     uint8_t *pa = base + L.off_pa, *pb = base + L.off_pb;
-    uint32_t *ba = reinterpret_cast<uint32_t *>(base + L.off_ba), *bb = reinterpret_cast<uint32_t *>(base + L.off_bb);
+    uint16_t *ra = reinterpret_cast<uint16_t *>(base + L.off_ra);
+    uint32_t *bn = reinterpret_cast<uint32_t *>(base + L.off_bn);
     long long *l1a = reinterpret_cast<long long *>(base + L.off_l1a);
     long long *l1b = reinterpret_cast<long long *>(base + L.off_l1b);
     int *mxa = reinterpret_cast<int *>(base + L.off_mxa), *mxb = reinterpret_cast<int *>(base + L.off_mxb);
@@ -589,14 +813,16 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         if (cudaMemsetAsync(base + L.off_l1a, 0, L.off_sx - L.off_l1a, st) != cudaSuccess)
             return check_launch("sfb_matmul_wide (stats reset)");
         prep_kernel<true><<<dim3((unsigned)(L.Mp / 128), (unsigned)L.KW), 128, 0, st>>>(
-            A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ba, l1a, mxa);
+            A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ra, l1a, mxa);
         prep_kernel<false><<<dim3((unsigned)(L.Np / 128), (unsigned)L.KW), 128, 0, st>>>(
-            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, bb, l1b, mxb);
+            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb);
+        bits_n_kernel<<<dim3((unsigned)(L.Np / 128), (unsigned)(L.Kp / BN_KB)), 128, 0, st>>>(
+            B + z * sb, ldb, (int)N, (int)K, (int)(L.Np / 32), bits, bn);
         tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
             tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
         RemIn in;
-        in.bitsA = ba;
-        in.bitsB = bb;
+        in.rec = reinterpret_cast<const uint32_t *>(ra);
+        in.bn = bn;
         in.SX = SX;
         in.rowL1 = l1a;
         in.colL1 = l1b;
@@ -604,7 +830,8 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.colMax = mxb;
         in.Mp = (int)L.Mp;
         in.Np = (int)L.Np;
-        in.KW = (int)L.KW;
+        in.Kp = (int)L.Kp;
+        in.NWt = (int)(L.Np / 32);
         in.A = A + z * sa;
         in.B = B + z * sb;
         in.lda = lda;
@@ -622,8 +849,7 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.w = w;
         in.u = mx_unit(mx, true);
         in.counts = counts;
-        wide_rem_kernel<<<dim3((unsigned)((N + RT - 1) / RT), (unsigned)((M + RT - 1) / RT)), 256,
-                          2 * KC * 9 * RT * 4, st>>>(in);
+        wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
         rc = check_launch("sfb_matmul_wide (tensor-core path)");
         if (rc) return rc;
     }
