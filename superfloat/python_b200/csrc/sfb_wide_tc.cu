@@ -391,9 +391,11 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
 // bits' terms d_i = (y_{6-i}, y_{7-i}), negated where s_w (the start values
 // (1, s_w) and (s_w, s_w) are F* and G* of 0).
 //
-// Entry (e, table t) sits at (e * 65 + t) * 8 bytes of its half: the 16
-// entries one row-lane can read of one table fall in distinct bank pairs,
-// and the builders (consecutive t) store to consecutive words.
+// Each half is two arrays of 32-bit words, the low and the high plane, with
+// entry (e, table t) at word e * 65 + t: the 32 entries of one table fall in
+// distinct banks, so a warp's read of one plane is one wavefront whatever
+// the rows' indexes, and the builders (consecutive t) store to consecutive
+// words.
 
 constexpr int RM = 256;                    // rows per CTA: 8 warps, one row per lane
 constexpr int RNW = 4;                     // 32-column words per CTA
@@ -401,7 +403,8 @@ constexpr int RKC = 16;                    // k per chunk: two blocks of 8
 constexpr int RNTAB = RKC * RNW;           // tables per chunk
 constexpr int RTSTR = RNTAB + 1;           // entry stride in tables (odd)
 constexpr int RENT = 32;                   // entries per half: 16 nibbles x 2 signs of a
-constexpr int TAB_HALF = RENT * RTSTR * 8;
+constexpr int TAB_PLANE = RENT * RTSTR * 4;   // one plane of one half
+constexpr int TAB_HALF = 2 * TAB_PLANE;
 constexpr int TAB_BYTES = 2 * TAB_HALF;
 constexpr int REC_BYTES = (RKC / 2) * RM * 4;
 constexpr int BST_BYTES = RKC * 9 * RNW * 4;
@@ -535,13 +538,16 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         e[5] = add2(e[4], d[0]);
         e[6] = add2(e[4], d[1]);
         e[7] = add2(e[5], d[1]);
-        uint2 *tab = reinterpret_cast<uint2 *>(buf + half * TAB_HALF);
+        uint32_t *tlo = reinterpret_cast<uint32_t *>(buf + half * TAB_HALF);
+        uint32_t *thi = reinterpret_cast<uint32_t *>(buf + half * TAB_HALF + TAB_PLANE);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             const int idx = hi * 8 + j;
-            tab[idx * RTSTR + t] = make_uint2(e[j].lo, e[j].hi);
+            tlo[idx * RTSTR + t] = e[j].lo;
+            thi[idx * RTSTR + t] = e[j].hi;
             const W2 c = half == 0 ? W2{e[j].lo, e[j].hi ^ e[j].lo} : W2{~e[j].lo, ~e[j].hi};
-            tab[(idx + 16) * RTSTR + t] = make_uint2(c.lo, c.hi);
+            tlo[(idx + 16) * RTSTR + t] = c.lo;
+            thi[(idx + 16) * RTSTR + t] = c.hi;
         }
     };
 
@@ -555,21 +561,23 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const uint32_t r = recs[(b * 4 + j) * RM + ml];
-                aF[2 * j] = buf + __byte_perm(r, 0, 0x4440) * (RTSTR * 8) + (b * 8 + 2 * j) * RNW * 8;
-                aG[2 * j] = buf + TAB_HALF + __byte_perm(r, 0, 0x4441) * (RTSTR * 8) + (b * 8 + 2 * j) * RNW * 8;
-                aF[2 * j + 1] = buf + __byte_perm(r, 0, 0x4442) * (RTSTR * 8) + (b * 8 + 2 * j + 1) * RNW * 8;
+                aF[2 * j] = buf + __byte_perm(r, 0, 0x4440) * (RTSTR * 4) + (b * 8 + 2 * j) * RNW * 4;
+                aG[2 * j] = buf + TAB_HALF + __byte_perm(r, 0, 0x4441) * (RTSTR * 4) + (b * 8 + 2 * j) * RNW * 4;
+                aF[2 * j + 1] = buf + __byte_perm(r, 0, 0x4442) * (RTSTR * 4) + (b * 8 + 2 * j + 1) * RNW * 4;
                 aG[2 * j + 1] =
-                    buf + TAB_HALF + __byte_perm(r, 0, 0x4443) * (RTSTR * 8) + (b * 8 + 2 * j + 1) * RNW * 8;
+                    buf + TAB_HALF + __byte_perm(r, 0, 0x4443) * (RTSTR * 4) + (b * 8 + 2 * j + 1) * RNW * 4;
             }
 #pragma unroll
             for (int v = 0; v < RNW; v++) {
                 uint32_t u0[8], u1[8];
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
-                    const uint2 f = *reinterpret_cast<const uint2 *>(aF[kk] + v * 8);
-                    const uint2 g = *reinterpret_cast<const uint2 *>(aG[kk] + v * 8);
-                    u0[kk] = f.x ^ g.x;
-                    u1[kk] = f.y ^ g.y ^ (f.x & g.x);
+                    const uint32_t flo = *reinterpret_cast<const uint32_t *>(aF[kk] + v * 4);
+                    const uint32_t fhi = *reinterpret_cast<const uint32_t *>(aF[kk] + TAB_PLANE + v * 4);
+                    const uint32_t glo = *reinterpret_cast<const uint32_t *>(aG[kk] + v * 4);
+                    const uint32_t ghi = *reinterpret_cast<const uint32_t *>(aG[kk] + TAB_PLANE + v * 4);
+                    u0[kk] = flo ^ glo;
+                    u1[kk] = fhi ^ ghi ^ (flo & glo);
                 }
                 // 8 words of weight 1 and 8 of weight 2 into the planes: one carry of weight 32 out
                 const uint32_t c2a = csa(p1[v], u0[0], u0[1]);
