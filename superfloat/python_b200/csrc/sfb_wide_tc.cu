@@ -162,73 +162,118 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 
 // --- operand preparation ------------------------------------------------------------------
 //
-// One thread per (row, 32-k word).  Writes the nine int8 planes (h, l,
-// bit_0..bit_5, sign +-1 of A; h, l, -C_0..-C_5, sign -+32 of B), the row /
-// column L1 norm and maximum of the magnitudes, and for A the remainder's
-// per-product record: byte 0 = (x mod 16) + 16 s, byte 1 = (x >> 4) + 16 s
-// (x the magnitude's low byte, s its sign), two k per 32-bit word, laid out
-// [k / 2][row].
+// One CTA (256 threads) per 32 rows x 128 k, staged through shared memory so
+// that the codes are read with 16-byte loads and every plane row segment
+// (128 k = 128 bytes) is written as one full line.  Writes the nine int8
+// planes (h, l, bit_0..bit_5, sign +-1 of A; h, l, -C_0..-C_5, sign -+32 of
+// B), the row / column L1 norm and maximum of the magnitudes, and for A the
+// remainder's per-product record: byte 0 = (x mod 16) + 16 s, byte 1 =
+// (x >> 4) + 16 s (x the magnitude's low byte, s its sign), two k per 32-bit
+// word, laid out [k / 2][row].  For B the rows of the tile are B's columns.
+
+constexpr int PR = 32, PK = 128;
 
 template <bool IS_A>
-__global__ void __launch_bounds__(128) prep_kernel(const int16_t *__restrict__ X, int64_t ld, int rows, int K,
+__global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X, int64_t ld, int rows, int K,
                                                    int rows_pad, int Kp, int bits, uint8_t *__restrict__ planes,
-                                                   uint16_t *__restrict__ rec, long long *__restrict__ l1,
+                                                   uint32_t *__restrict__ rec, long long *__restrict__ l1,
                                                    int *__restrict__ mx) {
-    const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    const int kw = blockIdx.y;
-    if (r >= rows_pad) return;
+    __shared__ __align__(16) int16_t tile[PR][PK + 8];
+    const int tid = threadIdx.x;
+    const int r0 = blockIdx.x * PR, k0 = blockIdx.y * PK;
+    const bool vec = ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (ld % 8 == 0);
+    if (IS_A) {
+        const int rr = tid >> 3, kk = (tid & 7) * 16, r = r0 + rr;
+        const int16_t *src = X + (int64_t)r * ld + k0 + kk;
+        int16_t v[16];
+        if (vec && r < rows && k0 + kk + 16 <= K) {
+            *reinterpret_cast<uint4 *>(v) = __ldg(reinterpret_cast<const uint4 *>(src));
+            *reinterpret_cast<uint4 *>(v + 8) = __ldg(reinterpret_cast<const uint4 *>(src + 8));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = (r < rows && k0 + kk + j < K) ? src[j] : (int16_t)0;
+        }
+        *reinterpret_cast<uint4 *>(&tile[rr][kk]) = *reinterpret_cast<const uint4 *>(v);
+        *reinterpret_cast<uint4 *>(&tile[rr][kk + 8]) = *reinterpret_cast<const uint4 *>(v + 8);
+    } else {
+        const int kl = tid >> 1, nl = (tid & 1) * 16, k = k0 + kl;
+        const int16_t *src = X + (int64_t)k * ld + r0 + nl;
+        int16_t v[16];
+        if (vec && k < K && r0 + nl + 16 <= rows) {
+            *reinterpret_cast<uint4 *>(v) = __ldg(reinterpret_cast<const uint4 *>(src));
+            *reinterpret_cast<uint4 *>(v + 8) = __ldg(reinterpret_cast<const uint4 *>(src + 8));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) v[j] = (k < K && r0 + nl + j < rows) ? src[j] : (int16_t)0;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) tile[nl + j][kl] = v[j];
+    }
+    __syncthreads();
+
+    const int rr = tid >> 3, seg = tid & 7, r = r0 + rr;
+    const int sh = 16 - bits;
+    uint32_t pw[NPLANES][4];
+#pragma unroll
+    for (int p = 0; p < NPLANES; p++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) pw[p][q] = 0;
     long long sum = 0;
     int mval = 0;
-    const int sh = 16 - bits;
-    for (int half = 0; half < 2; half++) {
-        uint32_t pw[NPLANES][4];
+    int16_t c16[16];
+    *reinterpret_cast<uint4 *>(c16) = *reinterpret_cast<const uint4 *>(&tile[rr][seg * 16]);
+    *reinterpret_cast<uint4 *>(c16 + 8) = *reinterpret_cast<const uint4 *>(&tile[rr][seg * 16 + 8]);
 #pragma unroll
-        for (int p = 0; p < NPLANES; p++)
+    for (int j = 0; j < 16; j++) {
+        const int code = c16[j];
+        const int a = abs(code) << sh;               // 15-bit magnitude as the SF16 block reads it
+        const int s = code < 0;
+        const int kt = s ? -a : a;
+        const uint32_t sh8 = 8 * (j & 3);
+        pw[0][j >> 2] |= ((uint32_t)(kt >> 8) & 0xFFu) << sh8;      // h (signed)
+        pw[1][j >> 2] |= ((uint32_t)kt & 0xFFu) << sh8;             // l (unsigned)
 #pragma unroll
-            for (int q = 0; q < 4; q++) pw[p][q] = 0;
-        uint32_t rw[8];
-#pragma unroll
-        for (int jj = 0; jj < 16; jj++) {
-            const int j = half * 16 + jj;
-            const int k = kw * 32 + j;
-            int code = 0;
-            if (r < rows && k < K) code = IS_A ? (int)X[(int64_t)r * ld + k] : (int)X[(int64_t)k * ld + r];
-            const int a = abs(code) << sh;               // 15-bit magnitude as the SF16 block reads it
-            const int s = code < 0;
-            const int kt = s ? -a : a;
-            const uint32_t sh8 = 8 * (jj & 3);
-            pw[0][jj >> 2] |= ((uint32_t)(kt >> 8) & 0xFFu) << sh8;      // h (signed)
-            pw[1][jj >> 2] |= ((uint32_t)kt & 0xFFu) << sh8;             // l (unsigned)
-#pragma unroll
-            for (int i = 0; i < 6; i++) {
-                int v = IS_A ? ((a >> i) & 1) : -(((a << i) & 63));     // A: bit_i(a); B: -((w << i) mod 64)
-                if (s) v = -v;
-                pw[2 + i][jj >> 2] |= ((uint32_t)v & 0xFFu) << sh8;
-            }
-            const int sg = IS_A ? (s ? -1 : 1) : (s ? 32 : -32);        // product -32 s
-            pw[8][jj >> 2] |= ((uint32_t)sg & 0xFFu) << sh8;
-            if (IS_A) {
-                const uint32_t e = (uint32_t)(s << 4);
-                const uint32_t v = ((a & 15) + e) | ((((a >> 4) & 15) + e) << 8);
-                if (jj & 1) rw[jj >> 1] |= v << 16;
-                else rw[jj >> 1] = v;
-            }
-            sum += a;
-            mval = max(mval, a);
+        for (int i = 0; i < 6; i++) {
+            int v = IS_A ? ((a >> i) & 1) : -(((a << i) & 63));     // A: bit_i(a); B: -((w << i) mod 64)
+            if (s) v = -v;
+            pw[2 + i][j >> 2] |= ((uint32_t)v & 0xFFu) << sh8;
         }
+        const int sg = IS_A ? (s ? -1 : 1) : (s ? 32 : -32);        // product -32 s
+        pw[8][j >> 2] |= ((uint32_t)sg & 0xFFu) << sh8;
+        sum += a;
+        mval = max(mval, a);
+    }
 #pragma unroll
-        for (int p = 0; p < NPLANES; p++) {
-            uint4 *dst = reinterpret_cast<uint4 *>(planes + ((int64_t)p * rows_pad + r) * Kp + kw * 32 + half * 16);
-            *dst = make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
-        }
-        if (IS_A) {
-            uint32_t *rp = reinterpret_cast<uint32_t *>(rec);
+    for (int p = 0; p < NPLANES; p++)
+        *reinterpret_cast<uint4 *>(planes + ((int64_t)p * rows_pad + r) * Kp + k0 + seg * 16) =
+            make_uint4(pw[p][0], pw[p][1], pw[p][2], pw[p][3]);
+    // the 8 threads of a row are 8 consecutive lanes
 #pragma unroll
-            for (int q = 0; q < 8; q++) rp[(int64_t)(kw * 16 + half * 8 + q) * rows_pad + r] = rw[q];
+    for (int o = 1; o < 8; o <<= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mval = max(mval, __shfl_xor_sync(0xffffffffu, mval, o));
+    }
+    if (seg == 0 && r < rows_pad) {
+        if (sum) atomicAdd(reinterpret_cast<unsigned long long *>(l1 + r), (unsigned long long)sum);
+        if (mval) atomicMax(mx + r, mval);
+    }
+    if (IS_A) {
+        // 32 rows x 64 k pairs: a warp writes one k pair for the 32 rows (128 bytes)
+        const int ml = tid & 31, g = tid >> 5;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+            const int kp = g * 8 + q;
+            uint32_t v = 0;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int code = tile[ml][2 * kp + h];
+                const int x = (abs(code) << sh) & 255;
+                const uint32_t e = code < 0 ? 16u : 0u;
+                v |= (((uint32_t)(x & 15) + e) | (((uint32_t)(x >> 4) + e) << 8)) << (16 * h);
+            }
+            rec[(int64_t)(k0 / 2 + kp) * rows_pad + r0 + ml] = v;
         }
     }
-    if (sum) atomicAdd(reinterpret_cast<unsigned long long *>(l1 + r), (unsigned long long)sum);
-    if (mval) atomicMax(mx + r, mval);
 }
 
 // B's bits sliced over columns: for each k and 32-column word, the low byte
@@ -805,7 +850,7 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     }
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);
     uint8_t *pa = base + L.off_pa, *pb = base + L.off_pb;
-    uint16_t *ra = reinterpret_cast<uint16_t *>(base + L.off_ra);
+    uint32_t *ra = reinterpret_cast<uint32_t *>(base + L.off_ra);
     uint32_t *bn = reinterpret_cast<uint32_t *>(base + L.off_bn);
     long long *l1a = reinterpret_cast<long long *>(base + L.off_l1a);
     long long *l1b = reinterpret_cast<long long *>(base + L.off_l1b);
@@ -820,16 +865,16 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     for (int64_t z = 0; z < batch; z++) {
         if (cudaMemsetAsync(base + L.off_l1a, 0, L.off_sx - L.off_l1a, st) != cudaSuccess)
             return check_launch("sfb_matmul_wide (stats reset)");
-        prep_kernel<true><<<dim3((unsigned)(L.Mp / 128), (unsigned)L.KW), 128, 0, st>>>(
+        prep_kernel<true><<<dim3((unsigned)(L.Mp / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
             A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ra, l1a, mxa);
-        prep_kernel<false><<<dim3((unsigned)(L.Np / 128), (unsigned)L.KW), 128, 0, st>>>(
+        prep_kernel<false><<<dim3((unsigned)(L.Np / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
             B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb);
         bits_n_kernel<<<dim3((unsigned)(L.Np / 128), (unsigned)(L.Kp / BN_KB)), 128, 0, st>>>(
             B + z * sb, ldb, (int)N, (int)K, (int)(L.Np / 32), bits, bn);
         tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
             tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
         RemIn in;
-        in.rec = reinterpret_cast<const uint32_t *>(ra);
+        in.rec = ra;
         in.bn = bn;
         in.SX = SX;
         in.rowL1 = l1a;
