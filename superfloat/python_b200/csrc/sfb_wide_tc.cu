@@ -43,6 +43,7 @@
 // after freeing its TMEM.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "sfb_wide_simt.cuh"
@@ -57,7 +58,7 @@ int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t
 namespace {
 
 constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
-constexpr int STAGES = 6;
+constexpr int STAGES = 4;          // 129 KB: a GEMM CTA and a remainder CTA share an SM
 constexpr int NPASS = 11;
 constexpr int NPLANES = 9;         // int8 operand planes per matrix
 constexpr int STAGE_BYTES = 2 * TILE * TILE;
@@ -480,6 +481,7 @@ __device__ __forceinline__ uint32_t csa(uint32_t &s, uint32_t a, uint32_t b) {
 
 struct RemIn {
     const uint32_t *rec, *bn;
+    uint16_t *U;          // sum u per output, [Mp][Np]
     const long long *SX, *rowL1, *colL1;
     const int *rowMax, *colMax;
     int Mp, Np, Kp, NWt;
@@ -519,8 +521,6 @@ __device__ long long exact_output(const RemIn &in, int m, int n, bool &clip) {
 
 __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     extern __shared__ __align__(16) uint8_t rsm[];
-    __shared__ unsigned sc[5];
-    zero_counts_smem(sc);
     const int tid = threadIdx.x;
     const int ml = tid;                          // this lane's row within the tile
     const int m0 = blockIdx.y * RM, nw0 = blockIdx.x * RNW, n0 = nw0 * 32;
@@ -702,31 +702,43 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     }
     __syncthreads();
 
-    Counts cnt;
-    const long long lim = (1ll << 31) - 1;
-    const long long half_k3 = 3ll * in.Kp / 2;
+    // sum u per output (< 3 Kp <= 49152) as 16 bits, [row][column]
     const int nl = tid & 127, vw = nl >> 5, bit = nl & 31;
-    const int n = n0 + nl;
     for (int i = 0; i < RM / 2; i++) {
         const int mloc = 2 * i + (tid >> 7);
-        const int m = m0 + mloc;
-        if (m >= in.M || n >= in.N) continue;
         const uint32_t *src = pl + (vw * NPL) * RM + mloc;
-        long long U = 0;
+        uint32_t U = 0;
 #pragma unroll
         for (int l = 0; l < NPL; l++) {
             const int wt = l < 7 ? l : l - 1;                    // planes 6 and 7 both weigh 64
-            U += (long long)((src[l * RM] >> bit) & 1u) << wt;
+            U += ((src[l * RM] >> bit) & 1u) << wt;
         }
-        long long S = (in.SX[(int64_t)m * in.Np + n] + half_k3 - U) >> 2;     // exact: a multiple of 4
+        in.U[(int64_t)(m0 + mloc) * in.Np + n0 + nl] = (uint16_t)U;
+    }
+}
+
+// The accumulator of each output from the GEMM's sum and the remainder's
+// (exact: a multiple of 4), the per-output clip bound (outputs it does not
+// prove are recomputed exactly on the CUDA cores) and POP.
+__global__ void __launch_bounds__(256) wide_tc_finish_kernel(RemIn in) {
+    __shared__ unsigned sc[5];
+    zero_counts_smem(sc);
+    Counts cnt;
+    const long long lim = (1ll << 31) - 1;
+    const long long half_k3 = 3ll * in.Kp / 2;
+    const int64_t total = (int64_t)in.M * in.N;
+    for (int64_t o = (int64_t)blockIdx.x * 256 + threadIdx.x; o < total; o += (int64_t)gridDim.x * 256) {
+        const int m = (int)(o / in.N), n = (int)(o - (int64_t)m * in.N);
+        const int64_t at = (int64_t)m * in.Np + n;
+        long long S = (in.SX[at] + half_k3 - (long long)in.U[at]) >> 2;
         const long long b1 = in.rowL1[m] * (long long)in.colMax[n];
         const long long b2 = (long long)in.rowMax[m] * in.colL1[n];
         const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
         bool cl = false;
         if (!safe) S = exact_output(in, m, n, cl);
         if (in.acc_out) {
-            in.acc_out[(int64_t)m * in.N + n] = (int32_t)S;
-            if (in.flags) in.flags[(int64_t)m * in.N + n] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
+            in.acc_out[o] = (int32_t)S;
+            if (in.flags) in.flags[o] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
             cnt.clip += cl;
             continue;
         }
@@ -734,10 +746,10 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         bool over, under;
         const int qv = mx_pop(S, sft, in.u.F, in.w, over, under);
         over |= cl;
-        in.out[(int64_t)m * in.N + n] = (int16_t)qv;
+        in.out[o] = (int16_t)qv;
         if (in.flags)
-            in.flags[(int64_t)m * in.N + n] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) | (under ? SFB_F_UNDERFLOW : 0u) |
-                                                        (cl ? SFB_F_ACC_CLIPPED : 0u));
+            in.flags[o] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) | (under ? SFB_F_UNDERFLOW : 0u) |
+                                    (cl ? SFB_F_ACC_CLIPPED : 0u));
         cnt.over += over;
         cnt.under += under;
         cnt.clip += cl;
@@ -749,10 +761,39 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
 
 struct Layout {
     int64_t Mp, Np, Kp, KW;
-    int64_t off_pa, off_pb, off_ra, off_bn, off_l1a, off_l1b, off_mxa, off_mxb, off_sx, total;
+    int64_t off_pa, off_pb, off_ra, off_bn, off_l1a, off_l1b, off_mxa, off_mxb, off_sx, off_u, total;
 };
 
 int64_t up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+// One side stream per device (the highest priority) with its fork / join
+// events; the lock keeps each call's record / wait / launch sequence whole
+// when several host threads use the path.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    std::mutex lock;
+    bool tried = false;
+};
+
+SideStream *side_stream(int dev) {
+    static SideStream g[64];
+    static std::mutex init;
+    std::lock_guard<std::mutex> l(init);
+    SideStream &x = g[dev];
+    if (!x.tried) {
+        x.tried = true;
+        int lo = 0, hi = 0;
+        if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+            cudaStreamCreateWithPriority(&x.s, cudaStreamNonBlocking, hi) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
+            (void)cudaGetLastError();
+            x.s = nullptr;
+        }
+    }
+    return x.s ? &x : nullptr;
+}
 
 Layout layout_for(int64_t M, int64_t N, int64_t K) {
     Layout L;
@@ -775,6 +816,7 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
     L.off_mxa = take(4 * L.Mp);
     L.off_mxb = take(4 * L.Np);
     L.off_sx = take(8 * L.Mp * L.Np);
+    L.off_u = take(2 * L.Mp * L.Np);
     L.total = o + 1024;            // slack for aligning the caller's base
     return L;
 }
@@ -871,8 +913,6 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
             B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb);
         bits_n_kernel<<<dim3((unsigned)(L.Np / 128), (unsigned)(L.Kp / BN_KB)), 128, 0, st>>>(
             B + z * sb, ldb, (int)N, (int)K, (int)(L.Np / 32), bits, bn);
-        tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
-            tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
         RemIn in;
         in.rec = ra;
         in.bn = bn;
@@ -902,7 +942,29 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.w = w;
         in.u = mx_unit(mx, true);
         in.counts = counts;
-        wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
+        in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
+        // the GEMM (tensor pipe, TMA) beside the remainder's main loop (ALU pipe): on a
+        // higher-priority side stream forked from and joined back to the caller's
+        const dim3 ggrid((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE));
+        const dim3 rgrid((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM));
+        SideStream *side = side_stream(dev);
+        if (side) {
+            std::lock_guard<std::mutex> g(side->lock);
+            if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
+                return check_launch("sfb_matmul_wide (fork)");
+            tc_gemm_kernel<<<ggrid, 128, GEMM_SMEM, side->s>>>(tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np,
+                                                               &counts->reserved[0]);
+            wide_rem_kernel<<<rgrid, 256, REM_SMEM, st>>>(in);
+            if (cudaEventRecord(side->join, side->s) != cudaSuccess || cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+                return check_launch("sfb_matmul_wide (join)");
+        } else {
+            tc_gemm_kernel<<<ggrid, 128, GEMM_SMEM, st>>>(tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np,
+                                                          &counts->reserved[0]);
+            wide_rem_kernel<<<rgrid, 256, REM_SMEM, st>>>(in);
+        }
+        const int64_t outs = M * N;
+        const int fg = (int)std::max<int64_t>(1, std::min<int64_t>((outs + 255) / 256, (int64_t)sm_count() * 8));
+        wide_tc_finish_kernel<<<fg, 256, 0, st>>>(in);
         rc = check_launch("sfb_matmul_wide (tensor-core path)");
         if (rc) return rc;
     }
