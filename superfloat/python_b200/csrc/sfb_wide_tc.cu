@@ -59,6 +59,7 @@ namespace {
 
 constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
 constexpr int STAGES = 4;          // 129 KB: a GEMM CTA and a remainder CTA share an SM
+constexpr int GROUP_M = 8;         // row tiles per group of the GEMM's CTA order
 constexpr int NPASS = 11;
 constexpr int NPLANES = 9;         // int8 operand planes per matrix
 constexpr int STAGE_BYTES = 2 * TILE * TILE;
@@ -323,7 +324,13 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     __shared__ int s_fail;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TILE, n0 = blockIdx.x * TILE;
+    // grouped order: GROUP_M row tiles at a time sweep the column tiles, so the
+    // CTAs running together share A and B tiles in L2
+    const int mt = gridDim.y, nt = gridDim.x;
+    const int t = blockIdx.y * nt + blockIdx.x;
+    const int gsize = GROUP_M * nt, g = t / gsize, gm0 = g * GROUP_M;
+    const int gm = min(GROUP_M, mt - gm0), r = t - g * gsize;
+    const int m0 = (gm0 + r % gm) * TILE, n0 = (r / gm) * TILE;
     if (threadIdx.x == 0) {
         s_fail = 0;
         for (int s = 0; s < STAGES; s++) {
