@@ -169,9 +169,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 // (128 k = 128 bytes) is written as one full line.  Writes the nine int8
 // planes (h, l, bit_0..bit_5, sign +-1 of A; h, l, -C_0..-C_5, sign -+32 of
 // B), the row / column L1 norm and maximum of the magnitudes, and for A the
-// remainder's per-product record: byte 0 = (x mod 16) + 16 s, byte 1 =
-// (x >> 4) + 16 s (x the magnitude's low byte, s its sign), two k per 32-bit
-// word, laid out [k / 2][row].  For B the rows of the tile are B's columns.
+// remainder's per-product record: byte 0 = (x mod 16) | 128 s, byte 1 =
+// x >> 4 (x the magnitude's low byte, s its sign), two k per 32-bit word,
+// laid out [k / 2][row].  For B the rows of the tile are B's columns.
 
 constexpr int PR = 32, PK = 128;
 
@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X
             for (int h = 0; h < 2; h++) {
                 const int code = tile[ml][2 * kp + h];
                 const int x = (abs(code) << sh) & 255;
-                const uint32_t e = code < 0 ? 16u : 0u;
-                v |= (((uint32_t)(x & 15) + e) | (((uint32_t)(x >> 4) + e) << 8)) << (16 * h);
+                const uint32_t sgn = code < 0 ? 0x80u : 0u;
+                v |= (((uint32_t)(x & 15) | sgn) | ((uint32_t)(x >> 4) << 8)) << (16 * h);
             }
             rec[(int64_t)(k0 / 2 + kp) * rows_pad + r0 + ml] = v;
         }
@@ -435,29 +435,27 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
 // arrive by cp.async, then every thread builds half of one (k, word) table,
 // and the rows read them.
 //
-// A table entry is a two-bit word (two 32-bit planes) per (k, word, index).
-// The F half, indexed by (x mod 16) + 16 s_a, holds F* = s_w ? ~F : F + 1 for
-// s_a = 0 and -F* for s_a = 1; the G half, indexed by (x >> 4) + 16 s_a,
-// holds G* = s_w ? ~G : G and ~G*.  Then u = F-entry + G-entry (mod 4):
-// u' = F* + G* is r for a positive w and 3 - r for a negative one, and
-// ~u' = (-F*) + ~G* flips it for a negative a.  Built as sums of the nibble
-// bits' terms d_i = (y_{6-i}, y_{7-i}), negated where s_w (the start values
-// (1, s_w) and (s_w, s_w) are F* and G* of 0).
+// A table entry is a two-bit word (two 32-bit planes, stored together) per
+// (k, word, index).  The F half, indexed by x mod 16, holds F* = s_w ? ~F :
+// F + 1; the G half, indexed by x >> 4, holds G* = s_w ? ~G : G.  Then
+// u' = F* + G* (mod 4) is r for a positive w and 3 - r for a negative one,
+// and u = u' ^ (3 if a < 0): a's sign is an all-ones mask folded into the
+// logic ops that form the two-bit sum.  Built as sums of the nibble bits'
+// terms d_i = (y_{6-i}, y_{7-i}), negated where s_w (the start values (1,
+// s_w) and (s_w, s_w) are F* and G* of 0).
 //
-// Each half is two arrays of 32-bit words, the low and the high plane, with
-// entry (e, table t) at word e * 65 + t: the 32 entries of one table fall in
-// distinct banks, so a warp's read of one plane is one wavefront whatever
-// the rows' indexes, and the builders (consecutive t) store to consecutive
-// words.
+// Entry (e, table t) sits at (e * 65 + t) * 8 bytes of its half: the 16
+// entries of one table fall in distinct bank pairs, so each half-warp's
+// 64-bit read is one wavefront whatever the rows' indexes, and the builders
+// (consecutive t) store to consecutive pairs.
 
 constexpr int RM = 256;                    // rows per CTA: 8 warps, one row per lane
 constexpr int RNW = 4;                     // 32-column words per CTA
 constexpr int RKC = 16;                    // k per chunk: two blocks of 8
 constexpr int RNTAB = RKC * RNW;           // tables per chunk
 constexpr int RTSTR = RNTAB + 1;           // entry stride in tables (odd)
-constexpr int RENT = 32;                   // entries per half: 16 nibbles x 2 signs of a
-constexpr int TAB_PLANE = RENT * RTSTR * 4;   // one plane of one half
-constexpr int TAB_HALF = 2 * TAB_PLANE;
+constexpr int RENT = 16;                   // entries per half: the 16 nibble values
+constexpr int TAB_HALF = RENT * RTSTR * 8;    // (low, high) plane pairs
 constexpr int TAB_BYTES = 2 * TAB_HALF;
 constexpr int REC_BYTES = (RKC / 2) * RM * 4;
 constexpr int BST_BYTES = RKC * 9 * RNW * 4;
@@ -476,6 +474,15 @@ __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_grou
 struct W2 {
     uint32_t lo, hi;
 };
+
+// prmt.b32 in its default mode: a selector nibble with bit 3 set replicates
+// the selected byte's top bit (the __byte_perm intrinsic keeps only the low
+// three bits of each nibble)
+__device__ __forceinline__ uint32_t sign_bytes(uint32_t x, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(x), "r"(sel));
+    return d;
+}
 
 __device__ __forceinline__ W2 add2(W2 a, W2 b) { return W2{a.lo ^ b.lo, a.hi ^ b.hi ^ (a.lo & b.lo)}; }
 
@@ -543,46 +550,50 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         for (int l = 0; l < 9; l++) hh[v][l] = 0;
     }
 
+    // chunk loads: each thread copies 32 contiguous bytes of the rows' records
+    // (2 x 16) and threads below 144 one 16-byte row of B's column bits
+    const int rrow = tid >> 5, rcol = (tid & 31) * 8;             // k pair row, u32 column
+    const uint32_t *rsrc = in.rec + (int64_t)rrow * in.Mp + m0 + rcol;
+    const uint32_t rdst = (uint32_t)(TAB_BYTES + (rrow * RM + rcol) * 4);
+    const int bkk = tid / 9, bp = tid - 9 * (tid / 9);
+    const uint32_t *bsrc = in.bn + ((int64_t)bkk * 9 + bp) * in.NWt + nw0;
+    const uint32_t bdst = (uint32_t)(TAB_BYTES + REC_BYTES + tid * RNW * 4);
+    const int64_t rstep = (int64_t)(RKC / 2) * in.Mp, bstep = (int64_t)RKC * 9 * in.NWt;
+    const uint32_t sbase = smem_u32(rsm);
     auto load_chunk = [&](int c, int q) {
-        uint8_t *buf = rsm + q * BUF_BYTES;
-        const uint32_t *src = in.rec + (int64_t)c * (RKC / 2) * in.Mp + m0;
-        for (int i = tid; i < (RKC / 2) * RM / 4; i += 256) {
-            const int row = i / (RM / 4), col = i % (RM / 4);
-            cp16(smem_u32(buf + TAB_BYTES + (row * RM + col * 4) * 4), src + (int64_t)row * in.Mp + col * 4);
-        }
-        if (tid < RKC * 9) {
-            const int kk = tid / 9, p = tid % 9;
-            cp16(smem_u32(buf + TAB_BYTES + REC_BYTES + (kk * 9 + p) * RNW * 4),
-                 in.bn + ((int64_t)(c * RKC + kk) * 9 + p) * in.NWt + nw0);
-        }
+        const uint32_t d = sbase + q * BUF_BYTES;
+        cp16(d + rdst, rsrc + c * rstep);
+        cp16(d + rdst + 16, rsrc + c * rstep + 4);
+        if (tid < RKC * 9) cp16(d + bdst, bsrc + c * bstep);
         cp_commit();
     };
 
+    // table build: thread -> (table t, half h, entries 8 hi .. 8 hi + 7); every
+    // step is the same for both halves but the y planes read and two masks
+    const int bt = tid & (RNTAB - 1), bh = (tid >> 6) & 1, bhi = tid >> 7;
+    const int bkl = bt / RNW, bv = bt % RNW;
+    const uint32_t hm = bh ? 0xFFFFFFFFu : 0u;                        // all ones for the G half
     auto build = [&](int q) {
         uint8_t *buf = rsm + q * BUF_BYTES;
-        const uint32_t *bs = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES + REC_BYTES);
-        const int t = tid & (RNTAB - 1), half = (tid >> 6) & 1, hi = tid >> 7;
-        const int kk = t / RNW, v = t % RNW;
-        uint32_t y[9];
+        const uint32_t *ys = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES + REC_BYTES) + bkl * 9 * RNW + bv;
+        // F: d_i = (y_{6-i}, y_{7-i}); G: d_i = (y_{2-i}, y_{3-i}), y_{-1} = 0
+        const int top = 7 - 4 * bh;
+        const uint32_t sw = ys[8 * RNW];
+        uint32_t yv[5];
 #pragma unroll
-        for (int p = 0; p < 9; p++) y[p] = bs[(kk * 9 + p) * RNW + v];
-        const uint32_t sw = y[8];
-        W2 d[4], start;
-        if (half == 0) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) d[i] = W2{y[6 - i], y[7 - i]};
-            start = W2{0xFFFFFFFFu, sw};
-        } else {
-            d[0] = W2{y[2], y[3]};
-            d[1] = W2{y[1], y[2]};
-            d[2] = W2{y[0], y[1]};
-            d[3] = W2{0u, y[0]};
-            start = W2{sw, sw};
+        for (int j = 0; j < 5; j++) {                                  // y_{top - j}, j = 0..4
+            const int p = top - j;
+            yv[j] = p >= 0 ? ys[p * RNW] : 0u;
         }
+        W2 d[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) d[i].hi ^= d[i].lo & sw;         // -d where w is negative
+        for (int i = 0; i < 4; i++) {
+            const uint32_t lo = yv[i + 1], hi = yv[i];
+            d[i] = W2{lo, hi ^ (lo & sw)};                             // -d where w is negative
+        }
+        const W2 start = W2{~hm | sw, sw};                             // F: (1, s_w); G: (s_w, s_w)
         W2 e[8];
-        e[0] = hi ? add2(start, d[3]) : start;
+        e[0] = bhi ? add2(start, d[3]) : start;
         e[1] = add2(e[0], d[0]);
         e[2] = add2(e[0], d[1]);
         e[3] = add2(e[1], d[1]);
@@ -590,17 +601,9 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         e[5] = add2(e[4], d[0]);
         e[6] = add2(e[4], d[1]);
         e[7] = add2(e[5], d[1]);
-        uint32_t *tlo = reinterpret_cast<uint32_t *>(buf + half * TAB_HALF);
-        uint32_t *thi = reinterpret_cast<uint32_t *>(buf + half * TAB_HALF + TAB_PLANE);
+        uint2 *tab = reinterpret_cast<uint2 *>(buf + bh * TAB_HALF);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int idx = hi * 8 + j;
-            tlo[idx * RTSTR + t] = e[j].lo;
-            thi[idx * RTSTR + t] = e[j].hi;
-            const W2 c = half == 0 ? W2{e[j].lo, e[j].hi ^ e[j].lo} : W2{~e[j].lo, ~e[j].hi};
-            tlo[(idx + 16) * RTSTR + t] = c.lo;
-            thi[(idx + 16) * RTSTR + t] = c.hi;
-        }
+        for (int j = 0; j < 8; j++) tab[(bhi * 8 + j) * RTSTR + bt] = make_uint2(e[j].lo, e[j].hi);
     };
 
     auto hot = [&](int c, int q) {
@@ -610,26 +613,27 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
 #pragma unroll
         for (int b = 0; b < 2; b++) {
             const uint8_t *aF[8], *aG[8];
+            uint32_t sm8[8];                                           // a's sign as a mask
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const uint32_t r = recs[(b * 4 + j) * RM + ml];
-                aF[2 * j] = buf + __byte_perm(r, 0, 0x4440) * (RTSTR * 4) + (b * 8 + 2 * j) * RNW * 4;
-                aG[2 * j] = buf + TAB_HALF + __byte_perm(r, 0, 0x4441) * (RTSTR * 4) + (b * 8 + 2 * j) * RNW * 4;
-                aF[2 * j + 1] = buf + __byte_perm(r, 0, 0x4442) * (RTSTR * 4) + (b * 8 + 2 * j + 1) * RNW * 4;
-                aG[2 * j + 1] =
-                    buf + TAB_HALF + __byte_perm(r, 0, 0x4443) * (RTSTR * 4) + (b * 8 + 2 * j + 1) * RNW * 4;
+                const uint8_t *fk = buf + (b * 8 + 2 * j) * RNW * 8, *gk = fk + TAB_HALF;
+                aF[2 * j] = fk + (r & 0xFu) * (RTSTR * 8);
+                aG[2 * j] = gk + __byte_perm(r, 0, 0x4441) * (RTSTR * 8);
+                sm8[2 * j] = sign_bytes(r, 0x8888);
+                aF[2 * j + 1] = fk + RNW * 8 + __umulhi(r & 0xF0000u, (uint32_t)(RTSTR * 8) << 16);
+                aG[2 * j + 1] = gk + RNW * 8 + __byte_perm(r, 0, 0x4443) * (RTSTR * 8);
+                sm8[2 * j + 1] = sign_bytes(r, 0xAAAA);
             }
 #pragma unroll
             for (int v = 0; v < RNW; v++) {
                 uint32_t u0[8], u1[8];
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
-                    const uint32_t flo = *reinterpret_cast<const uint32_t *>(aF[kk] + v * 4);
-                    const uint32_t fhi = *reinterpret_cast<const uint32_t *>(aF[kk] + TAB_PLANE + v * 4);
-                    const uint32_t glo = *reinterpret_cast<const uint32_t *>(aG[kk] + v * 4);
-                    const uint32_t ghi = *reinterpret_cast<const uint32_t *>(aG[kk] + TAB_PLANE + v * 4);
-                    u0[kk] = flo ^ glo;
-                    u1[kk] = fhi ^ ghi ^ (flo & glo);
+                    const uint2 f = *reinterpret_cast<const uint2 *>(aF[kk] + v * 8);
+                    const uint2 g = *reinterpret_cast<const uint2 *>(aG[kk] + v * 8);
+                    u0[kk] = f.x ^ g.x ^ sm8[kk];
+                    u1[kk] = f.y ^ (f.x & g.x) ^ g.y ^ sm8[kk];
                 }
                 // 8 words of weight 1 and 8 of weight 2 into the planes: one carry of weight 32 out
                 const uint32_t c2a = csa(p1[v], u0[0], u0[1]);
