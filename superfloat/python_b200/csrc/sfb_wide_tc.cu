@@ -58,7 +58,7 @@ int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t
 namespace {
 
 constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
-constexpr int STAGES = 4;          // 129 KB: a GEMM CTA and a remainder CTA share an SM
+constexpr int STAGES = 6;
 constexpr int GROUP_M = 8;         // row tiles per group of the GEMM's CTA order
 constexpr int NPASS = 11;
 constexpr int NPLANES = 9;         // int8 operand planes per matrix
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(128) bits_n_kernel(const int16_t *__restrict__
 
 __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmB, int nkb,
-                                                         long long *__restrict__ SX, int Np,
+                                                         int32_t *__restrict__ SX, int Np,
                                                          unsigned long long *__restrict__ err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     if (ok) {
         const int row = m0 + warp * 32 + lane;
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        long long *dst = SX + (int64_t)row * Np + n0;
+        int32_t *dst = SX + (int64_t)row * Np + n0;
         for (int c = 0; c < TILE / 32; c++) {
             int32_t d0[32], d1[32], d2[32];
             tmem_ld32(tmem + lane_base + 0 * TILE + c * 32, d0);
@@ -412,7 +412,9 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
 #pragma unroll
             for (int j = 0; j < 32; j++) {
                 const long long t = ((long long)d0[j] << 16) + ((long long)d1[j] << 8) + (long long)d2[j];
-                dst[c * 32 + j] = t >> 6;            // exact: the total is 64 sum s X - 32 sum s, sum s even
+                // t / 64 = sum s X - (sum s) / 2 exactly (sum s is even); kept as floor(t / 256)
+                // mod 2^32, the low two bits being recoverable from the remainder's sum
+                dst[c * 32 + j] = (int32_t)(uint32_t)(t >> 8);
             }
         }
     } else if (threadIdx.x == 0) {
@@ -496,7 +498,8 @@ __device__ __forceinline__ uint32_t csa(uint32_t &s, uint32_t a, uint32_t b) {
 struct RemIn {
     const uint32_t *rec, *bn;
     uint16_t *U;          // sum u per output, [Mp][Np]
-    const long long *SX, *rowL1, *colL1;
+    const int32_t *SX;    // floor((sum s X - (sum s) / 2) / 4) mod 2^32, [Mp][Np]
+    const long long *rowL1, *colL1;
     const int *rowMax, *colMax;
     int Mp, Np, Kp, NWt;
     const int16_t *A, *B;
@@ -728,42 +731,105 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     }
 }
 
-// The accumulator of each output from the GEMM's sum and the remainder's
-// (exact: a multiple of 4), the per-output clip bound (outputs it does not
-// prove are recomputed exactly on the CUDA cores) and POP.
+// The accumulator of each output from the GEMM's sum and the remainder's,
+// the per-output clip bound (outputs it does not prove are recomputed
+// exactly on the CUDA cores) and POP.  With T = sum s X - (sum s) / 2, the
+// accumulator is (T + 3 Kp / 2 - U) / 4, a multiple of 4 before the division,
+// so T mod 4 = (U - 3 Kp / 2) mod 4 and the accumulator is floor(T / 4) +
+// ((T mod 4) + 3 Kp / 2 - U) / 4: exact modulo 2^32 from the 32-bit
+// floor(T / 4), and so exact for every output the bound proves (|acc| < 2^31).
+// POP of a 32-bit accumulator (every output here: proven below 2^31, or the
+// clamped W = 32 accumulator), as mx_pop with 32-bit shifts.
+__device__ __forceinline__ int mx_pop32(int acc, int shift, int F, Width w, bool &over, bool &under) {
+    const int e = shift - F + w.bits - 1;
+    const uint32_t mag = acc < 0 ? 0u - (uint32_t)acc : (uint32_t)acc;
+    uint32_t q;
+    if (e >= 0) {
+        over = e >= 16 ? mag != 0 : mag > ((uint32_t)w.M >> e);
+        q = over ? (uint32_t)w.M : mag << e;
+    } else {
+        const int d = -e;
+        if (d >= 32) {
+            q = 0;
+        } else {
+            const uint32_t fl = mag >> d, rem = mag & ((1u << d) - 1u), half = 1u << (d - 1);
+            q = fl + ((rem > half) || (rem == half && (fl & 1u)));
+        }
+        over = q > (uint32_t)w.M;
+        if (over) q = (uint32_t)w.M;
+    }
+    under = acc != 0 && q == 0;
+    return acc < 0 ? -(int)q : (int)q;
+}
+
+// One block per 256 columns and a stride of rows.  A row whose L1 norm times
+// the block's largest column magnitude is within the clip bound needs no
+// per-output test (the bound is only ever used conservatively).
 __global__ void __launch_bounds__(256) wide_tc_finish_kernel(RemIn in) {
     __shared__ unsigned sc[5];
+    __shared__ int s_cmax[8];
     zero_counts_smem(sc);
     Counts cnt;
     const long long lim = (1ll << 31) - 1;
-    const long long half_k3 = 3ll * in.Kp / 2;
-    const int64_t total = (int64_t)in.M * in.N;
-    for (int64_t o = (int64_t)blockIdx.x * 256 + threadIdx.x; o < total; o += (int64_t)gridDim.x * 256) {
-        const int m = (int)(o / in.N), n = (int)(o - (int64_t)m * in.N);
-        const int64_t at = (int64_t)m * in.Np + n;
-        long long S = (in.SX[at] + half_k3 - (long long)in.U[at]) >> 2;
-        const long long b1 = in.rowL1[m] * (long long)in.colMax[n];
-        const long long b2 = (long long)in.rowMax[m] * in.colL1[n];
-        const bool safe = ((b1 < b2 ? b1 : b2) >> 8) + in.K <= lim;
-        bool cl = false;
-        if (!safe) S = exact_output(in, m, n, cl);
-        if (in.acc_out) {
-            in.acc_out[o] = (int32_t)S;
-            if (in.flags) in.flags[o] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
-            cnt.clip += cl;
-            continue;
+    const int h = 3 * in.Kp / 2;
+    const int n = blockIdx.x * 256 + threadIdx.x;
+    const bool nin = n < in.N;
+    const int cmx = nin ? in.colMax[n] : 0;
+    const long long cl1 = nin ? in.colL1[n] : 0;
+    int bm = cmx;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) bm = max(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+    if ((threadIdx.x & 31) == 0) s_cmax[threadIdx.x >> 5] = bm;
+    __syncthreads();
+    bm = s_cmax[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) bm = max(bm, s_cmax[i]);
+    // four rows per step, their loads issued together
+    for (int m0 = blockIdx.y; m0 < in.M; m0 += 4 * gridDim.y) {
+        if (!nin) continue;
+        int Uv[4];
+        uint32_t tv[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int m = m0 + j * gridDim.y;
+            const int64_t at = (int64_t)min(m, in.M - 1) * in.Np + n;
+            Uv[j] = in.U[at];
+            tv[j] = (uint32_t)in.SX[at];
         }
-        const int sft = in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
-        bool over, under;
-        const int qv = mx_pop(S, sft, in.u.F, in.w, over, under);
-        over |= cl;
-        in.out[o] = (int16_t)qv;
-        if (in.flags)
-            in.flags[o] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) | (under ? SFB_F_UNDERFLOW : 0u) |
-                                    (cl ? SFB_F_ACC_CLIPPED : 0u));
-        cnt.over += over;
-        cnt.under += under;
-        cnt.clip += cl;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int m = m0 + j * gridDim.y;
+            if (m >= in.M) break;
+            const long long rl1 = in.rowL1[m];
+            const bool row_safe = ((rl1 * (long long)bm) >> 8) + in.K <= lim;
+            const int64_t o = (int64_t)m * in.N + n;
+            const int U = Uv[j];
+            int S = (int32_t)(tv[j] + (uint32_t)((((U - h) & 3) + h - U) >> 2));
+            bool cl = false;
+            if (!row_safe) {
+                const long long b1 = rl1 * (long long)cmx;
+                const long long b2 = (long long)in.rowMax[m] * cl1;
+                if (((b1 < b2 ? b1 : b2) >> 8) + in.K > lim) S = (int)exact_output(in, m, n, cl);
+            }
+            if (in.acc_out) {
+                in.acc_out[o] = S;
+                if (in.flags) in.flags[o] = (uint8_t)(cl ? SFB_F_ACC_CLIPPED : 0u);
+                cnt.clip += cl;
+                continue;
+            }
+            const int sft =
+                in.shift_arr ? (int)in.shift_arr[(int64_t)m * in.ssm + (int64_t)n * in.ssn] : in.shift;
+            bool over, under;
+            const int qv = mx_pop32(S, sft, in.u.F, in.w, over, under);
+            over |= cl;
+            in.out[o] = (int16_t)qv;
+            if (in.flags)
+                in.flags[o] = (uint8_t)((over ? SFB_F_OVERFLOW : 0u) | (under ? SFB_F_UNDERFLOW : 0u) |
+                                        (cl ? SFB_F_ACC_CLIPPED : 0u));
+            cnt.over += over;
+            cnt.under += under;
+            cnt.clip += cl;
+        }
     }
     flush_counts(cnt, in.counts, sc);
 }
@@ -776,35 +842,6 @@ struct Layout {
 };
 
 int64_t up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
-
-// One side stream per device (the highest priority) with its fork / join
-// events; the lock keeps each call's record / wait / launch sequence whole
-// when several host threads use the path.
-struct SideStream {
-    cudaStream_t s = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-    std::mutex lock;
-    bool tried = false;
-};
-
-SideStream *side_stream(int dev) {
-    static SideStream g[64];
-    static std::mutex init;
-    std::lock_guard<std::mutex> l(init);
-    SideStream &x = g[dev];
-    if (!x.tried) {
-        x.tried = true;
-        int lo = 0, hi = 0;
-        if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
-            cudaStreamCreateWithPriority(&x.s, cudaStreamNonBlocking, hi) != cudaSuccess ||
-            cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess) {
-            (void)cudaGetLastError();
-            x.s = nullptr;
-        }
-    }
-    return x.s ? &x : nullptr;
-}
 
 Layout layout_for(int64_t M, int64_t N, int64_t K) {
     Layout L;
@@ -826,7 +863,7 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
     L.off_l1b = take(8 * L.Np);
     L.off_mxa = take(4 * L.Mp);
     L.off_mxb = take(4 * L.Np);
-    L.off_sx = take(8 * L.Mp * L.Np);
+    L.off_sx = take(4 * L.Mp * L.Np);
     L.off_u = take(2 * L.Mp * L.Np);
     L.total = o + 1024;            // slack for aligning the caller's base
     return L;
@@ -908,7 +945,7 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     long long *l1a = reinterpret_cast<long long *>(base + L.off_l1a);
     long long *l1b = reinterpret_cast<long long *>(base + L.off_l1b);
     int *mxa = reinterpret_cast<int *>(base + L.off_mxa), *mxb = reinterpret_cast<int *>(base + L.off_mxb);
-    long long *SX = reinterpret_cast<long long *>(base + L.off_sx);
+    int32_t *SX = reinterpret_cast<int32_t *>(base + L.off_sx);
     CUtensorMap tmA, tmB;
     int rc = make_map(&tmA, pa, L.Mp, L.Kp);
     if (rc) return rc;
@@ -954,28 +991,12 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.u = mx_unit(mx, true);
         in.counts = counts;
         in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
-        // the GEMM (tensor pipe, TMA) beside the remainder's main loop (ALU pipe): on a
-        // higher-priority side stream forked from and joined back to the caller's
-        const dim3 ggrid((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE));
-        const dim3 rgrid((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM));
-        SideStream *side = side_stream(dev);
-        if (side) {
-            std::lock_guard<std::mutex> g(side->lock);
-            if (cudaEventRecord(side->fork, st) != cudaSuccess || cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess)
-                return check_launch("sfb_matmul_wide (fork)");
-            tc_gemm_kernel<<<ggrid, 128, GEMM_SMEM, side->s>>>(tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np,
-                                                               &counts->reserved[0]);
-            wide_rem_kernel<<<rgrid, 256, REM_SMEM, st>>>(in);
-            if (cudaEventRecord(side->join, side->s) != cudaSuccess || cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
-                return check_launch("sfb_matmul_wide (join)");
-        } else {
-            tc_gemm_kernel<<<ggrid, 128, GEMM_SMEM, st>>>(tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np,
-                                                          &counts->reserved[0]);
-            wide_rem_kernel<<<rgrid, 256, REM_SMEM, st>>>(in);
-        }
-        const int64_t outs = M * N;
-        const int fg = (int)std::max<int64_t>(1, std::min<int64_t>((outs + 255) / 256, (int64_t)sm_count() * 8));
-        wide_tc_finish_kernel<<<fg, 256, 0, st>>>(in);
+        tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
+            tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
+        wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
+        const int64_t fx = (N + 255) / 256;
+        const dim3 fgrid((unsigned)fx, (unsigned)std::max<int64_t>(1, std::min<int64_t>(M, (int64_t)sm_count() * 8 / fx)));
+        wide_tc_finish_kernel<<<fgrid, 256, 0, st>>>(in);
         rc = check_launch("sfb_matmul_wide (tensor-core path)");
         if (rc) return rc;
     }
