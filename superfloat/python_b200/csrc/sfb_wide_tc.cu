@@ -57,12 +57,13 @@ int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t
 
 namespace {
 
-constexpr int TILE = 128;          // output tile (M and N) and K bytes per stage
+constexpr int TILE = 128;          // output rows per GEMM tile and K bytes per stage
+constexpr int GN = 160;            // output columns per GEMM tile (3 accumulators x 160 <= 512 TMEM columns)
 constexpr int STAGES = 6;
 constexpr int GROUP_M = 8;         // row tiles per group of the GEMM's CTA order
 constexpr int NPASS = 11;
 constexpr int NPLANES = 9;         // int8 operand planes per matrix
-constexpr int STAGE_BYTES = 2 * TILE * TILE;
+constexpr int STAGE_BYTES = TILE * TILE + GN * TILE;
 constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int KMAX = 16384;        // |D| < 2^31 up to this K
 constexpr unsigned kSpinLimit = 1u << 26;
@@ -129,7 +130,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 
 // kind::i8 instruction descriptor: s32 accumulate, K-major A and B, M = N = 128
 __device__ __forceinline__ uint32_t idesc_i8(int a_signed, int b_signed) {
-    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((uint32_t)(TILE >> 3) << 17) |
+    return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((uint32_t)(GN >> 3) << 17) |
            ((uint32_t)(TILE >> 4) << 24);
 }
 
@@ -330,7 +331,7 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     const int t = blockIdx.y * nt + blockIdx.x;
     const int gsize = GROUP_M * nt, g = t / gsize, gm0 = g * GROUP_M;
     const int gm = min(GROUP_M, mt - gm0), r = t - g * gsize;
-    const int m0 = (gm0 + r % gm) * TILE, n0 = (r / gm) * TILE;
+    const int m0 = (gm0 + r % gm) * TILE, n0 = (r / gm) * GN;
     if (threadIdx.x == 0) {
         s_fail = 0;
         for (int s = 0; s < STAGES; s++) {
@@ -386,7 +387,7 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
             const uint32_t b_addr = a_addr + TILE * TILE;
 #pragma unroll
             for (int kk = 0; kk < TILE / 32; kk++) {
-                mma_i8(tmem + acc * TILE, smem_desc(a_addr + kk * 32), smem_desc(b_addr + kk * 32), id,
+                mma_i8(tmem + acc * GN, smem_desc(a_addr + kk * 32), smem_desc(b_addr + kk * 32), id,
                        (started[acc] || kk > 0) ? 1u : 0u);
             }
             started[acc] = true;
@@ -404,11 +405,12 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
         const int row = m0 + warp * 32 + lane;
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
         int32_t *dst = SX + (int64_t)row * Np + n0;
-        for (int c = 0; c < TILE / 32; c++) {
+        for (int c = 0; c < GN / 32; c++) {
+            if (n0 + c * 32 >= Np) break;                 // the last column tile runs past the padded width
             int32_t d0[32], d1[32], d2[32];
-            tmem_ld32(tmem + lane_base + 0 * TILE + c * 32, d0);
-            tmem_ld32(tmem + lane_base + 1 * TILE + c * 32, d1);
-            tmem_ld32(tmem + lane_base + 2 * TILE + c * 32, d2);
+            tmem_ld32(tmem + lane_base + 0 * GN + c * 32, d0);
+            tmem_ld32(tmem + lane_base + 1 * GN + c * 32, d1);
+            tmem_ld32(tmem + lane_base + 2 * GN + c * 32, d2);
 #pragma unroll
             for (int j = 0; j < 32; j++) {
                 const long long t = ((long long)d0[j] << 16) + ((long long)d1[j] << 8) + (long long)d2[j];
@@ -893,12 +895,12 @@ EncodeTiled encoder() {
     return fn;
 }
 
-int make_map(CUtensorMap *map, void *base, int64_t rows_pad, int64_t Kp) {
+int make_map(CUtensorMap *map, void *base, int64_t rows_pad, int64_t Kp, int box_rows) {
     EncodeTiled enc = encoder();
     if (!enc) return set_error(SFB_ECUDA, "sfb_matmul_wide: cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)rows_pad, (cuuint64_t)NPLANES};
     const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)(Kp * rows_pad)};
-    const cuuint32_t box[3] = {TILE, TILE, 1};
+    const cuuint32_t box[3] = {TILE, (cuuint32_t)box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -947,9 +949,9 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     int *mxa = reinterpret_cast<int *>(base + L.off_mxa), *mxb = reinterpret_cast<int *>(base + L.off_mxb);
     int32_t *SX = reinterpret_cast<int32_t *>(base + L.off_sx);
     CUtensorMap tmA, tmB;
-    int rc = make_map(&tmA, pa, L.Mp, L.Kp);
+    int rc = make_map(&tmA, pa, L.Mp, L.Kp, TILE);
     if (rc) return rc;
-    rc = make_map(&tmB, pb, L.Np, L.Kp);
+    rc = make_map(&tmB, pb, L.Np, L.Kp, GN);
     if (rc) return rc;
     const Width w = width(bits);
     for (int64_t z = 0; z < batch; z++) {
@@ -991,7 +993,7 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.u = mx_unit(mx, true);
         in.counts = counts;
         in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
-        tc_gemm_kernel<<<dim3((unsigned)(L.Np / TILE), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
+        tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
             tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
         wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
         const int64_t fx = (N + 255) / 256;
