@@ -58,20 +58,16 @@ int wide_simt(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t
 namespace {
 
 constexpr int TILE = 128;          // output rows per GEMM tile and K bytes per stage
-constexpr int GN = 160;            // output columns per GEMM tile (3 accumulators x 160 <= 512 TMEM columns)
-constexpr int STAGES = 6;
+constexpr int GN = 256;            // output columns per GEMM tile
+constexpr int STAGES = 4;
 constexpr int GROUP_M = 8;         // row tiles per group of the GEMM's CTA order
-constexpr int NPASS = 11;
+constexpr int P1 = 3, P2 = 8;      // MMA passes per 128-k block in the two phases
+constexpr int GEMM_THREADS = 192;  // TMA warp, MMA warp, four fold / epilogue warps
 constexpr int NPLANES = 9;         // int8 operand planes per matrix
 constexpr int STAGE_BYTES = TILE * TILE + GN * TILE;
 constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int KMAX = 16384;        // |D| < 2^31 up to this K
 constexpr unsigned kSpinLimit = 1u << 26;
-
-// pass -> (A plane, B plane, accumulator, A signed, B signed)
-__constant__ int c_pass[NPASS][5] = {
-    {0, 0, 0, 1, 1}, {0, 1, 1, 1, 0}, {1, 0, 1, 0, 1}, {1, 1, 2, 0, 0}, {2, 2, 2, 1, 1},
-    {3, 3, 2, 1, 1}, {4, 4, 2, 1, 1}, {5, 5, 2, 1, 1}, {6, 6, 2, 1, 1}, {7, 7, 2, 1, 1}, {8, 8, 2, 1, 1}};
 
 // --- PTX wrappers --------------------------------------------------------------------------
 
@@ -311,18 +307,77 @@ __global__ void __launch_bounds__(128) bits_n_kernel(const int16_t *__restrict__
     }
 }
 
-// --- the tcgen05 GEMM: sum_k s X - (sum_k s) / 2 per output ---------------------------------
+// --- the tcgen05 GEMM: floor((sum_k s X - (sum_k s) / 2) / 4) per output ------------------------
+//
+// A 128 x 256 output tile needs three 256-column s32 accumulators by scale
+// (D0 = h.h x 2^16, D1 = h.l + l.h x 2^8, D2 = the rest x 1), more than the
+// 512 TMEM columns.  Only floor(T / 4) mod 2^32 is kept, and with 64 T =
+// 2^16 D0 + 2^8 D1 + D2 that is (2^8 D0 + D1 + floor(D2 / 256)) mod 2^32.
+// So the tile runs in two phases: the three h passes over all K into D0
+// (columns 0..255) and D1 (256..511); four warps fold E = 2^8 D0 + D1 (mod
+// 2^32) into D1's columns; the eight remaining passes accumulate D2 into
+// columns 0..255; the epilogue writes E + floor(D2 / 256).
+//
+// Warp 0 lane 0 issues the TMA loads (A and B tiles of each pass, both
+// phases, in one ring of stages); warp 1 lane 0 issues the MMAs (one thread,
+// as tcgen05 requires); warps 2..5 fold and write out (warp w reaches TMEM
+// lanes 32 (w mod 4) .. + 31).  Every wait is bounded: on timeout the kernel
+// records an error in the caller's counters and returns after freeing TMEM.
 
-__global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                         const __grid_constant__ CUtensorMap tmB, int nkb,
-                                                         int32_t *__restrict__ SX, int Np,
-                                                         unsigned long long *__restrict__ err) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+        "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// pass it of the tile's sequence -> A plane, B plane, accumulator column, signedness, first use
+struct Pass {
+    int pa, pb, col, sa, sb;
+    bool first;
+};
+
+__device__ __forceinline__ Pass pass_of(int it, int nkb) {
+    Pass p;
+    if (it < P1 * nkb) {
+        const int kb = it / P1, q = it % P1;
+        p.pa = q == 2 ? 1 : 0;
+        p.pb = q == 1 ? 1 : 0;
+        p.col = q == 0 ? 0 : GN;
+        p.sa = q == 2 ? 0 : 1;
+        p.sb = q == 1 ? 0 : 1;
+        p.first = kb == 0 && q != 2;
+    } else {
+        const int j = it - P1 * nkb, kb = j / P2, q = j % P2;
+        p.pa = p.pb = q == 0 ? 1 : q + 1;
+        p.col = 0;
+        p.sa = p.sb = q == 0 ? 0 : 1;
+        p.first = kb == 0 && q == 0;
+    }
+    return p;
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                                  const __grid_constant__ CUtensorMap tmB, int nkb,
+                                                                  int32_t *__restrict__ SX, int Np,
+                                                                  unsigned long long *__restrict__ err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-    // bars[0..S): full, bars[S..2S): empty, bars[2S]: done; then the TMEM address
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 1);
+    // bars[0..S): full, [S..2S): empty, [2S]: phase 1 done, [2S+1]: fold done, [2S+2]: all done
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 3);
     __shared__ int s_fail;
+    const uint32_t bar_p1 = smem_u32(&bars[2 * STAGES]), bar_fold = smem_u32(&bars[2 * STAGES + 1]),
+                   bar_done = smem_u32(&bars[2 * STAGES + 2]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // grouped order: GROUP_M row tiles at a time sweep the column tiles, so the
@@ -338,7 +393,9 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
             mbar_init(smem_u32(&bars[s]), 1);
             mbar_init(smem_u32(&bars[STAGES + s]), 1);
         }
-        mbar_init(smem_u32(&bars[2 * STAGES]), 1);
+        mbar_init(bar_p1, 1);
+        mbar_init(bar_fold, 4);
+        mbar_init(bar_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -350,9 +407,10 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int total = nkb * NPASS;
+    const int total = nkb * (P1 + P2);
 
     int issued = 0;
+    bool ok = true;
     if (threadIdx.x == 0) {
         // TMA producer
         for (int it = 0; it < total; it++) {
@@ -362,64 +420,91 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
                 break;
             }
             if (*(volatile int *)&s_fail) break;
-            const int kb = it / NPASS, p = it % NPASS;
+            const Pass p = pass_of(it, nkb);
+            const int kb = it < P1 * nkb ? it / P1 : (it - P1 * nkb) / P2;
             const uint32_t full = smem_u32(&bars[s]);
             uint8_t *sa = smem + s * STAGE_BYTES;
             mbar_expect_tx(full, STAGE_BYTES);
-            tma_load_3d(smem_u32(sa), &tmA, kb * TILE, m0, c_pass[p][0], full);
-            tma_load_3d(smem_u32(sa + TILE * TILE), &tmB, kb * TILE, n0, c_pass[p][1], full);
+            tma_load_3d(smem_u32(sa), &tmA, kb * TILE, m0, p.pa, full);
+            tma_load_3d(smem_u32(sa + TILE * TILE), &tmB, kb * TILE, n0, p.pb, full);
             issued = it + 1;
         }
     } else if (threadIdx.x == 32) {
         // MMA issuer
-        bool started[3] = {false, false, false};
-        for (int it = 0; it < total; it++) {
+        for (int it = 0; it < total && ok; it++) {
+            if (it == P1 * nkb) {
+                // phase 1 complete: let the fold run, then overwrite D0's columns
+                mma_commit(bar_p1);
+                if (!mbar_wait(bar_fold, 0)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
             const int s = it % STAGES, round = it / STAGES;
             if (!mbar_wait(smem_u32(&bars[s]), round & 1)) {
-                s_fail = 1;
+                ok = false;
                 break;
             }
             tc_fence_after();
-            const int p = it % NPASS;
-            const int acc = c_pass[p][2];
-            const uint32_t id = idesc_i8(c_pass[p][3], c_pass[p][4]);
+            const Pass p = pass_of(it, nkb);
+            const uint32_t id = idesc_i8(p.sa, p.sb);
             const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
             const uint32_t b_addr = a_addr + TILE * TILE;
 #pragma unroll
-            for (int kk = 0; kk < TILE / 32; kk++) {
-                mma_i8(tmem + acc * GN, smem_desc(a_addr + kk * 32), smem_desc(b_addr + kk * 32), id,
-                       (started[acc] || kk > 0) ? 1u : 0u);
-            }
-            started[acc] = true;
+            for (int kk = 0; kk < TILE / 32; kk++)
+                mma_i8(tmem + p.col, smem_desc(a_addr + kk * 32), smem_desc(b_addr + kk * 32), id,
+                       (p.first && kk == 0) ? 0u : 1u);
             mma_commit(smem_u32(&bars[STAGES + s]));
         }
-        mma_commit(smem_u32(&bars[2 * STAGES]));
-    }
-    __syncwarp();
-    // epilogue: all warps
-    bool ok = mbar_wait(smem_u32(&bars[2 * STAGES]), 0);
-    tc_fence_after();
-    __syncthreads();
-    if (s_fail) ok = false;
-    if (ok) {
-        const int row = m0 + warp * 32 + lane;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        int32_t *dst = SX + (int64_t)row * Np + n0;
-        for (int c = 0; c < GN / 32; c++) {
-            if (n0 + c * 32 >= Np) break;                 // the last column tile runs past the padded width
-            int32_t d0[32], d1[32], d2[32];
-            tmem_ld32(tmem + lane_base + 0 * GN + c * 32, d0);
-            tmem_ld32(tmem + lane_base + 1 * GN + c * 32, d1);
-            tmem_ld32(tmem + lane_base + 2 * GN + c * 32, d2);
+        if (!ok) {
+            s_fail = 1;
+            mma_commit(bar_p1);                 // release the fold warps (they see s_fail)
+        }
+        mma_commit(bar_done);
+    } else if (warp >= 2) {
+        const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+        // the fold: E = 2^8 D0 + D1 (mod 2^32) into D1's columns
+        // each decision is the whole warp's: the TMEM loads and stores are warp-collective
+        bool fine = __all_sync(0xffffffffu, mbar_wait(bar_p1, 0) && !*(volatile int *)&s_fail);
+        tc_fence_after();
+        if (fine) {
+            for (int c = 0; c < GN / 32; c++) {
+                int32_t d0[32], d1[32];
+                uint32_t e[32];
+                tmem_ld32(tmem + lane_base + c * 32, d0);
+                tmem_ld32(tmem + lane_base + GN + c * 32, d1);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const long long t = ((long long)d0[j] << 16) + ((long long)d1[j] << 8) + (long long)d2[j];
-                // t / 64 = sum s X - (sum s) / 2 exactly (sum s is even); kept as floor(t / 256)
-                // mod 2^32, the low two bits being recoverable from the remainder's sum
-                dst[c * 32 + j] = (int32_t)(uint32_t)(t >> 8);
+                for (int j = 0; j < 32; j++) e[j] = ((uint32_t)d0[j] << 8) + (uint32_t)d1[j];
+                tmem_st32(tmem + lane_base + GN + c * 32, e);
             }
         }
-    } else if (threadIdx.x == 0) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_fold);
+        // the epilogue: E + floor(D2 / 256)
+        const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_done, 0));
+        fine = __all_sync(0xffffffffu, landed && !*(volatile int *)&s_fail);
+        tc_fence_after();
+        if (fine) {
+            const int row = m0 + 32 * (warp & 3) + lane;
+            int32_t *dst = SX + (int64_t)row * Np + n0;
+            for (int c = 0; c < GN / 32; c++) {
+                if (n0 + c * 32 >= Np) break;             // the last column tile runs past the padded width
+                int32_t d2[32], ev[32];
+                tmem_ld32(tmem + lane_base + c * 32, d2);
+                tmem_ld32(tmem + lane_base + GN + c * 32, ev);
+#pragma unroll
+                for (int j = 0; j < 32; j++) dst[c * 32 + j] = (int32_t)((uint32_t)ev[j] + (uint32_t)(d2[j] >> 8));
+            }
+        } else if (!landed) {
+            s_fail = 1;
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (s_fail && threadIdx.x == 0) {
         atomicAdd(err, 1ull);
         // let this CTA's copies still in flight land before its shared memory is released
         for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; it++)
@@ -427,6 +512,7 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
     }
     tc_fence_before();
     __syncthreads();
+    tc_fence_after();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
@@ -848,7 +934,7 @@ int64_t up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 Layout layout_for(int64_t M, int64_t N, int64_t K) {
     Layout L;
     L.Mp = up(M, RM);               // the remainder kernel's row tile (a multiple of TILE)
-    L.Np = up(N, TILE);
+    L.Np = up(N, GN);               // whole GEMM column tiles (a multiple of the other kernels' 128)
     L.Kp = up(K, TILE);
     L.KW = L.Kp / 32;
     int64_t o = 0;
@@ -993,7 +1079,7 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.u = mx_unit(mx, true);
         in.counts = counts;
         in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
-        tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), 128, GEMM_SMEM, st>>>(
+        tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), GEMM_THREADS, GEMM_SMEM, st>>>(
             tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
         wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
         const int64_t fx = (N + 255) / 256;
