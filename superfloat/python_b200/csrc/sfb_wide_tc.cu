@@ -494,8 +494,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
                 int32_t d2[32], ev[32];
                 tmem_ld32(tmem + lane_base + c * 32, d2);
                 tmem_ld32(tmem + lane_base + GN + c * 32, ev);
+                uint32_t o[32];
 #pragma unroll
-                for (int j = 0; j < 32; j++) dst[c * 32 + j] = (int32_t)((uint32_t)ev[j] + (uint32_t)(d2[j] >> 8));
+                for (int j = 0; j < 32; j++) o[j] = (uint32_t)ev[j] + (uint32_t)(d2[j] >> 8);
+                uint4 *d4 = reinterpret_cast<uint4 *>(dst + c * 32);       // 128-byte aligned: Np, n0, c * 32 multiples of 32
+#pragma unroll
+                for (int j = 0; j < 8; j++) d4[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
             }
         } else if (!landed) {
             s_fail = 1;
