@@ -103,14 +103,16 @@ __device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, 
     cnt.under += un;
 }
 
-// TM rows per thread: 8 when the clip is proven unnecessary (BM = 128), 4 with
-// the per-step clip and overflow tracking (BM = 64), to stay within registers.
-template <bool SAFE, bool BITS16, int TM>
-__global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__restrict__ A, const int16_t *__restrict__ B,
+// TM rows per thread: 8 when the clip is proven unnecessary, 4 with the
+// per-step clip and overflow tracking, to stay within registers.  NT threads:
+// 256 (BM = 16 TM rows per CTA), or 128 (BM = 8 TM) so that small problems
+// still spread over the SMs.
+template <bool SAFE, bool BITS16, int TM, int NT = THREADS>
+__global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict__ A, const int16_t *__restrict__ B,
                                                            int M, int N, int K, int64_t lda, int64_t ldb, int64_t sa,
                                                            int64_t sb, int64_t so, Width w0, Epi e, int vec,
                                                            sfb_counts *counts) {
-    constexpr int BM = 16 * TM;
+    constexpr int BM = (NT / 16) * TM;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     Stage<BM> *st = reinterpret_cast<Stage<BM> *>(smem_raw);
     __shared__ unsigned sc[5];
@@ -130,13 +132,15 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
 #pragma unroll
         for (int j = 0; j < TN; j++) acc[i][j] = 0, um[i][j] = 0xFFFFFFFFu, ov[i][j] = 0;
 
-    // loader roles.  A: PER = 32 / (256 / BM) k of one row per thread; B: 8
-    // columns of one k row per thread.  16-byte loads when the rows are aligned.
-    constexpr int TPR = THREADS / BM;          // threads per A row: 2 or 4
+    // loader roles.  A: PER = 32 / (NT / BM) k of one row per thread; B: 8
+    // columns of BPASS k rows per thread.  16-byte loads when the rows are aligned.
+    constexpr int TPR = NT / BM;               // threads per A row: 2 or 4
     constexpr int PER = BK / TPR;              // k per thread: 16 or 8
+    constexpr int BROWS = NT / 8, BPASS = BK / BROWS;
+    static_assert(PER % 8 == 0 && BPASS * BROWS == BK, "chain2 loader shape");
     const int ar = tid / TPR, ah = tid % TPR;
     const int bk = tid >> 3, bc = (tid & 7) * 8;
-    Pack8 ra[PER / 8], rb;
+    Pack8 ra[PER / 8], rb[BPASS];
     auto load_regs = [&](int k0) {
         const int gm = m0 + ar;
         const int ka = k0 + ah * PER;
@@ -151,12 +155,16 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
                     ra[q].h[j] = (gm < M && kq + j < K) ? A[(int64_t)gm * lda + kq + j] : (int16_t)0;
             }
         }
-        const int gk = k0 + bk, gn0 = n0 + bc;
-        if (vec && gk < K && gn0 + 8 <= N) {
-            rb.u = __ldg(reinterpret_cast<const uint4 *>(B + (int64_t)gk * ldb + gn0));
-        } else {
 #pragma unroll
-            for (int j = 0; j < 8; j++) rb.h[j] = (gk < K && gn0 + j < N) ? B[(int64_t)gk * ldb + gn0 + j] : (int16_t)0;
+        for (int p = 0; p < BPASS; p++) {
+            const int gk = k0 + bk + p * BROWS, gn0 = n0 + bc;
+            if (vec && gk < K && gn0 + 8 <= N) {
+                rb[p].u = __ldg(reinterpret_cast<const uint4 *>(B + (int64_t)gk * ldb + gn0));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    rb[p].h[j] = (gk < K && gn0 + j < N) ? B[(int64_t)gk * ldb + gn0 + j] : (int16_t)0;
+            }
         }
     };
     auto store_regs = [&](Stage<BM> &s) {
@@ -175,11 +183,13 @@ __global__ void __launch_bounds__(THREADS, 2) chain2_kernel(const int16_t *__res
         for (int o = 1; o < TPR; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
         if (ah == 0) s.a_sw[ar] = bits;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int v = rb.h[j];
-            s.b_abs[bk][bc + j] = (uint32_t)abs(v);
-            s.b_sgn[bk][bc + j] = v >> 31;
-        }
+        for (int p = 0; p < BPASS; p++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int v = rb[p].h[j];
+                s.b_abs[bk + p * BROWS][bc + j] = (uint32_t)abs(v);
+                s.b_sgn[bk + p * BROWS][bc + j] = v >> 31;
+            }
     };
 
     const int nk = (K + BK - 1) / BK;
@@ -638,6 +648,8 @@ __global__ void __launch_bounds__(256) chain_combine_kernel(const Piece *__restr
 // pieces for a general chain of few tiles (1: no split)
 int chain_pieces(int64_t batch, int64_t M, int64_t N, int64_t K) {
     if (batch != 1 || K < 4 * BK) return 1;
+    // enough 32 x 64 tiles to occupy most SMs: the plain chain beats the pieces' summaries
+    if (((M + 31) / 32) * ((N + BN - 1) / BN) >= (int64_t)sm_count() / 2) return 1;
     const int64_t tiles = ((M + 63) / 64) * ((N + BN - 1) / BN);
     const int64_t want = (2 * (int64_t)sm_count() + tiles - 1) / tiles;            // one wave at 2 CTAs per SM
     const int64_t most = std::max<int64_t>(1, K / (2 * BK));
@@ -674,8 +686,22 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
                                                                           sb, so, w, e, vec, 1u, counts);
         return check_launch(what);
     }
-    const int smem = 2 * (int)sizeof(Stage<64>);
     const bool b16 = bits == 16;
+    if (batch * mt * nt < 2 * (int64_t)sm_count()) {
+        // few 64 x 64 tiles: 32 x 64 tiles on 128-thread CTAs, twice the CTAs
+        const dim3 g2((unsigned)nt, (unsigned)((M + 31) / 32), (unsigned)batch);
+        const int smem = 2 * (int)sizeof(Stage<32>);
+        auto kern = b16 ? chain2_kernel<false, true, 4, 128> : chain2_kernel<false, false, 4, 128>;
+        static bool attr_s[64][2] = {};
+        if (!attr_s[dev][b16]) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+                return check_launch(what);
+            attr_s[dev][b16] = true;
+        }
+        kern<<<g2, 128, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
+        return check_launch(what);
+    }
+    const int smem = 2 * (int)sizeof(Stage<64>);
     auto kern = b16 ? chain2_kernel<false, true, 4> : chain2_kernel<false, false, 4>;
     if (!attr[dev][b16]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
