@@ -14,33 +14,32 @@
 //   the left-aligned signed codes k = s a split into limbs k = 256 h + l
 //   (h signed, l unsigned) give 4 GEMMs, sum s C = sum_i (s_a bit_i(a))
 //   (s_w ((w << i) mod 64)) 6 more, and (+-1) (-+32) sign planes the 11th.
-//   They run as tcgen05 kind::i8 MMAs into three s32 TMEM accumulators by
-//   scale: D0 = h.h (x 2^16), D1 = h.l + l.h (x 2^8), D2 = l.l - sum_i bit_i .
-//   C_i - 32 sum s (x 1; the C planes are stored negated).  |D| < 2^31 for
-//   K <= 16384.
+//   They run as tcgen05 kind::i8 MMAs; by scale the sums are D0 = h.h
+//   (x 2^16), D1 = h.l + l.h (x 2^8) and D2 = l.l - sum_i bit_i . C_i - 32
+//   sum s (x 1; the C planes are stored negated), |D| < 2^31 for K <= 16384,
+//   and the output needs only floor(T / 4) mod 2^32 = 2^8 D0 + D1 +
+//   floor(D2 / 256) (mod 2^32), T = sum s X - (sum s) / 2.
 // * sum u needs r per product: X mod 4 = (P + 2Q) mod 4 over the low bytes x
 //   of a and y of w (P = sum_{i<=6} x_i y_{6-i}, Q = sum_{i<=7} x_i y_{7-i}),
 //   which splits by the nibbles of x into F(x mod 16) + G(x >> 4), each a sum
 //   of x's bits times two-bit words of y's bits.  Bit-sliced over 32 columns,
 //   F and G are 16-entry tables of two-bit words per (k, column word), built
 //   once per CTA and read by every row; w's sign and the +1 are folded into
-//   the tables and a's sign selects a complemented copy, so u for 32 products
-//   is two shared-memory reads and a two-bit add (kernel wide_rem_kernel),
-//   summed over k in carry-save bit-plane counters.
+//   the tables and a's sign is a mask applied in the same logic ops, so u for
+//   32 products is two 64-bit shared-memory reads and a two-bit add (kernel
+//   wide_rem_kernel), summed over k in carry-save bit-plane counters.
 //
 // The sum is the MX accumulator when no chunk of 8 can clip; each output is
 // checked against the bound sum_k |t_k| <= min(rowL1 colmax, rowmax colL1)/256
 // + K, and an output that fails it is recomputed exactly, chunk by chunk, on
-// the CUDA cores.  POP as in the CUDA-core kernel.
+// the CUDA cores (wide_tc_finish_kernel).  POP as in the CUDA-core kernel.
 //
-// Pipeline of the GEMM kernel (one CTA per 128 x 128 output tile, 128
-// threads): thread 0 issues TMA loads of 128 x 128-byte operand tiles (128-byte
-// swizzle) into a ring of stages; thread 32 issues the MMAs (one thread, as
-// tcgen05 requires) and commits each stage back to the producer; all four
-// warps then read the TMEM accumulators (tcgen05.ld, one 32-lane quarter per
-// warp) and write sum s X - (sum s) / 2 as int64.  Every wait is bounded: on
-// timeout the kernel records an error in the caller's counters and returns
-// after freeing its TMEM.
+// Kernels, in stream order: prep_kernel (A and B operand planes, A's nibble
+// records, L1 / max statistics), bits_n_kernel (B's column-sliced bits),
+// tc_gemm_kernel (128 x 256 output tiles in two phases, described at the
+// kernel), wide_rem_kernel (sum u per output), wide_tc_finish_kernel.  Every
+// wait on a barrier is bounded: on timeout a kernel records an error in the
+// caller's counters and returns after freeing its TMEM.
 #include <cuda.h>
 
 #include <algorithm>
@@ -520,14 +519,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
-// --- the remainder sum_k u, the combination and POP -----------------------------------------
+// --- the remainder sum_k u --------------------------------------------------------------------
 //
 // One CTA per 256 rows x 128 columns: a lane owns one row, and for each of
 // its four 32-column words keeps sum_k u as carry-save bit planes (bit b of
 // a plane belongs to column 32 word + b).  K runs in chunks of 16, double
 // buffered in shared memory: the rows' records and B's column-sliced bits
-// arrive by cp.async, then every thread builds half of one (k, word) table,
-// and the rows read them.
+// arrive by cp.async, then every thread builds 8 entries of one table half
+// for one (k, word), and the rows read them.  The kernel writes sum u per
+// output; wide_tc_finish_kernel combines it with the GEMM's sum.
 //
 // A table entry is a two-bit word (two 32-bit planes, stored together) per
 // (k, word, index).  The F half, indexed by x mod 16, holds F* = s_w ? ~F :
