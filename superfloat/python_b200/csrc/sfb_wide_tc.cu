@@ -523,10 +523,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
 //
 // One CTA per 256 rows x 128 columns: a lane owns one row, and for each of
 // its four 32-column words keeps sum_k u as carry-save bit planes (bit b of
-// a plane belongs to column 32 word + b).  K runs in chunks of 16, double
+// a plane belongs to column 32 word + b).  K runs in chunks of 32, double
 // buffered in shared memory: the rows' records and B's column-sliced bits
-// arrive by cp.async, then every thread builds 8 entries of one table half
-// for one (k, word), and the rows read them.  The kernel writes sum u per
+// arrive by cp.async, then every thread builds 8 entries of two table halves
+// (each for one (k, word)), and the rows read them.  The kernel writes sum u per
 // output; wide_tc_finish_kernel combines it with the GEMM's sum.
 //
 // A table entry is a two-bit word (two 32-bit planes, stored together) per
@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
 
 constexpr int RM = 256;                    // rows per CTA: 8 warps, one row per lane
 constexpr int RNW = 4;                     // 32-column words per CTA
-constexpr int RKC = 16;                    // k per chunk: two blocks of 8
+constexpr int RKC = 32;                    // k per chunk: four blocks of 8
 constexpr int RNTAB = RKC * RNW;           // tables per chunk
 constexpr int RTSTR = RNTAB + 1;           // entry stride in tables (odd)
 constexpr int RENT = 16;                   // entries per half: the 16 nibble values
@@ -646,29 +646,34 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     }
 
     // chunk loads: each thread copies 32 contiguous bytes of the rows' records
-    // (2 x 16) and threads below 144 one 16-byte row of B's column bits
+    // in each of RKC / 16 row groups, and 16-byte rows of B's column bits
     const int rrow = tid >> 5, rcol = (tid & 31) * 8;             // k pair row, u32 column
     const uint32_t *rsrc = in.rec + (int64_t)rrow * in.Mp + m0 + rcol;
     const uint32_t rdst = (uint32_t)(TAB_BYTES + (rrow * RM + rcol) * 4);
-    const int bkk = tid / 9, bp = tid - 9 * (tid / 9);
-    const uint32_t *bsrc = in.bn + ((int64_t)bkk * 9 + bp) * in.NWt + nw0;
-    const uint32_t bdst = (uint32_t)(TAB_BYTES + REC_BYTES + tid * RNW * 4);
     const int64_t rstep = (int64_t)(RKC / 2) * in.Mp, bstep = (int64_t)RKC * 9 * in.NWt;
     const uint32_t sbase = smem_u32(rsm);
     auto load_chunk = [&](int c, int q) {
         const uint32_t d = sbase + q * BUF_BYTES;
-        cp16(d + rdst, rsrc + c * rstep);
-        cp16(d + rdst + 16, rsrc + c * rstep + 4);
-        if (tid < RKC * 9) cp16(d + bdst, bsrc + c * bstep);
+#pragma unroll
+        for (int g = 0; g < RKC / 16; g++) {
+            const uint32_t *src = rsrc + c * rstep + (int64_t)g * 8 * in.Mp;
+            cp16(d + rdst + g * 8 * RM * 4, src);
+            cp16(d + rdst + g * 8 * RM * 4 + 16, src + 4);
+        }
+        for (int i = tid; i < RKC * 9; i += 256) {
+            const int kk = i / 9, p = i - 9 * kk;
+            cp16(d + TAB_BYTES + REC_BYTES + i * RNW * 4, in.bn + ((int64_t)kk * 9 + p) * in.NWt + nw0 + c * bstep);
+        }
         cp_commit();
     };
 
-    // table build: thread -> (table t, half h, entries 8 hi .. 8 hi + 7); every
-    // step is the same for both halves but the y planes read and two masks
-    const int bt = tid & (RNTAB - 1), bh = (tid >> 6) & 1, bhi = tid >> 7;
-    const int bkl = bt / RNW, bv = bt % RNW;
-    const uint32_t hm = bh ? 0xFFFFFFFFu : 0u;                        // all ones for the G half
-    auto build = [&](int q) {
+    // table build: item -> (table t, half h, entries 8 hi .. 8 hi + 7), two
+    // items per thread; every step is the same for both halves but the y
+    // planes read and two masks (h and hi are uniform over a warp)
+    auto build_item = [&](int q, int item) {
+        const int bt = item & (RNTAB - 1), bh = (item / RNTAB) & 1, bhi = item / (2 * RNTAB);
+        const int bkl = bt / RNW, bv = bt % RNW;
+        const uint32_t hm = bh ? 0xFFFFFFFFu : 0u;                    // all ones for the G half
         uint8_t *buf = rsm + q * BUF_BYTES;
         const uint32_t *ys = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES + REC_BYTES) + bkl * 9 * RNW + bv;
         // F: d_i = (y_{6-i}, y_{7-i}); G: d_i = (y_{2-i}, y_{3-i}), y_{-1} = 0
@@ -700,13 +705,17 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
 #pragma unroll
         for (int j = 0; j < 8; j++) tab[(bhi * 8 + j) * RTSTR + bt] = make_uint2(e[j].lo, e[j].hi);
     };
+    auto build = [&](int q) {
+        static_assert(4 * RNTAB == 2 * 256, "two build items per thread");
+        build_item(q, tid);
+        build_item(q, tid + 256);
+    };
 
-    auto hot = [&](int c, int q) {
+    auto hot = [&](int q) {
         const uint8_t *buf = rsm + q * BUF_BYTES;
         const uint32_t *recs = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES);
-        uint32_t c64[RNW];
 #pragma unroll
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < RKC / 8; b++) {
             const uint8_t *aF[8], *aG[8];
             uint32_t sm8[8];                                           // a's sign as a mask
 #pragma unroll
@@ -748,27 +757,26 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
                 const uint32_t c16b = p8[v] & c8c;
                 p8[v] ^= c8c;
                 const uint32_t c32 = csa(p16[v], c16a, c16b);
-                if (b == 0) {
+                // static per chunk: blocks 0 / 2 leave a weight-32 carry pending, 1 / 3 pair it
+                // into h32; the weight-64 carries of blocks 1 and 3 pair into h64, whose carry
+                // ripples up the binary counter once per chunk
+                if ((b & 1) == 0) {
                     pend32[v] = c32;
                 } else {
-                    c64[v] = csa(h32[v], pend32[v], c32);
+                    const uint32_t c64 = csa(h32[v], pend32[v], c32);
                     pend32[v] = 0;
-                }
-            }
-        }
-        if ((c & 1) == 0) {
+                    if (b == 1) {
+                        pend64[v] = c64;
+                    } else {
+                        uint32_t cc = csa(h64[v], pend64[v], c64);
+                        pend64[v] = 0;
 #pragma unroll
-            for (int v = 0; v < RNW; v++) pend64[v] = c64[v];
-        } else {
-#pragma unroll
-            for (int v = 0; v < RNW; v++) {
-                uint32_t cc = csa(h64[v], pend64[v], c64[v]);
-                pend64[v] = 0;
-#pragma unroll
-                for (int l = 0; l < 9; l++) {
-                    const uint32_t t = hh[v][l] & cc;
-                    hh[v][l] ^= cc;
-                    cc = t;
+                        for (int l = 0; l < 9; l++) {
+                            const uint32_t t = hh[v][l] & cc;
+                            hh[v][l] ^= cc;
+                            cc = t;
+                        }
+                    }
                 }
             }
         }
@@ -783,7 +791,7 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     for (int c = 0; c < nch; c++) {
         const int q = c & 1;
         if (c + 1 < nch) load_chunk(c + 1, q ^ 1);
-        hot(c, q);
+        hot(q);
         cp_wait_all();
         __syncthreads();
         if (c + 1 < nch) build(q ^ 1);
