@@ -35,7 +35,7 @@
 // the CUDA cores (wide_tc_finish_kernel).  POP as in the CUDA-core kernel.
 //
 // Kernels, in stream order: prep_kernel (A and B operand planes, A's nibble
-// records, L1 / max statistics), bits_n_kernel (B's column-sliced bits),
+// records, B's column-sliced bits, L1 / max statistics),
 // tc_gemm_kernel (128 x 256 output tiles in two phases, described at the
 // kernel), wide_rem_kernel (sum u per output), wide_tc_finish_kernel.  Every
 // wait on a barrier is bounded: on timeout a kernel records an error in the
@@ -167,7 +167,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 // B), the row / column L1 norm and maximum of the magnitudes, and for A the
 // remainder's per-product record: byte 0 = (x mod 16) | 128 s, byte 1 =
 // x >> 4 (x the magnitude's low byte, s its sign), two k per 32-bit word,
-// laid out [k / 2][row].  For B the rows of the tile are B's columns.
+// laid out [k / 2][row].  For B the rows of the tile are B's columns (32 of
+// them: one column word), and the kernel also writes B's low magnitude byte
+// and sign as bit planes sliced over those columns, [k][plane 0..8][word], one
+// warp ballot per plane and k.
 
 constexpr int PR = 32, PK = 128;
 
@@ -175,7 +178,7 @@ template <bool IS_A>
 __global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X, int64_t ld, int rows, int K,
                                                    int rows_pad, int Kp, int bits, uint8_t *__restrict__ planes,
                                                    uint32_t *__restrict__ rec, long long *__restrict__ l1,
-                                                   int *__restrict__ mx) {
+                                                   int *__restrict__ mx, uint32_t *__restrict__ bn, int NWt) {
     __shared__ __align__(16) int16_t tile[PR][PK + 8];
     const int tid = threadIdx.x;
     const int r0 = blockIdx.x * PR, k0 = blockIdx.y * PK;
@@ -255,6 +258,23 @@ __global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X
         if (sum) atomicAdd(reinterpret_cast<unsigned long long *>(l1 + r), (unsigned long long)sum);
         if (mval) atomicMax(mx + r, mval);
     }
+    if (!IS_A) {
+        // column-sliced bits: warp w takes k = 16 w .. 16 w + 15 of the tile
+        const int lane = tid & 31, w = tid >> 5, nw = r0 / 32;
+        for (int kk = 16 * w; kk < 16 * w + 16; kk++) {
+            const int code = tile[lane][kk];
+            const int y = (abs(code) << sh) & 255;
+            uint32_t mine = 0;
+#pragma unroll
+            for (int p = 0; p < 8; p++) {
+                const uint32_t word = __ballot_sync(0xffffffffu, (y >> p) & 1);
+                if (lane == p) mine = word;
+            }
+            const uint32_t sw = __ballot_sync(0xffffffffu, code < 0);
+            if (lane == 8) mine = sw;
+            if (lane < 9) bn[((int64_t)(k0 + kk) * 9 + lane) * NWt + nw] = mine;
+        }
+    }
     if (IS_A) {
         // 32 rows x 64 k pairs: a warp writes one k pair for the 32 rows (128 bytes)
         const int ml = tid & 31, g = tid >> 5;
@@ -271,38 +291,6 @@ __global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X
             }
             rec[(int64_t)(k0 / 2 + kp) * rows_pad + r0 + ml] = v;
         }
-    }
-}
-
-// B's bits sliced over columns: for each k and 32-column word, the low byte
-// y of the magnitudes as eight bit planes and the signs, laid out
-// [k][plane 0..8][column word].  A block is four warps (128 columns) over 8 k.
-constexpr int BN_KB = 8;
-
-__global__ void __launch_bounds__(128) bits_n_kernel(const int16_t *__restrict__ B, int64_t ldb, int N, int K, int NWt,
-                                                     int bits, uint32_t *__restrict__ bn) {
-    __shared__ uint32_t st[9][4];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int n = blockIdx.x * 128 + threadIdx.x;
-    const int sh = 16 - bits;
-    for (int kk = 0; kk < BN_KB; kk++) {
-        const int k = blockIdx.y * BN_KB + kk;
-        const int code = (n < N && k < K) ? (int)B[(int64_t)k * ldb + n] : 0;
-        const int y = (abs(code) << sh) & 255;
-        uint32_t mine = 0;
-#pragma unroll
-        for (int p = 0; p < 8; p++) {
-            const uint32_t word = __ballot_sync(0xffffffffu, (y >> p) & 1);
-            if (lane == p) mine = word;
-        }
-        const uint32_t sw = __ballot_sync(0xffffffffu, code < 0);
-        if (lane == 8) mine = sw;
-        if (lane < 9) st[lane][w] = mine;
-        __syncthreads();
-        if (threadIdx.x < 9)
-            *reinterpret_cast<uint4 *>(bn + ((int64_t)k * 9 + threadIdx.x) * NWt + blockIdx.x * 4) =
-                make_uint4(st[threadIdx.x][0], st[threadIdx.x][1], st[threadIdx.x][2], st[threadIdx.x][3]);
-        __syncthreads();
     }
 }
 
@@ -1056,11 +1044,10 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         if (cudaMemsetAsync(base + L.off_l1a, 0, L.off_sx - L.off_l1a, st) != cudaSuccess)
             return check_launch("sfb_matmul_wide (stats reset)");
         prep_kernel<true><<<dim3((unsigned)(L.Mp / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
-            A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ra, l1a, mxa);
+            A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ra, l1a, mxa, nullptr, 0);
         prep_kernel<false><<<dim3((unsigned)(L.Np / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
-            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb);
-        bits_n_kernel<<<dim3((unsigned)(L.Np / 128), (unsigned)(L.Kp / BN_KB)), 128, 0, st>>>(
-            B + z * sb, ldb, (int)N, (int)K, (int)(L.Np / 32), bits, bn);
+            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb, bn,
+            (int)(L.Np / 32));
         RemIn in;
         in.rec = ra;
         in.bn = bn;
