@@ -622,15 +622,17 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     const int ml = tid;                          // this lane's row within the tile
     const int m0 = blockIdx.y * RM, nw0 = blockIdx.x * RNW, n0 = nw0 * 32;
 
-    // carry-save counters per column word: weights 1..16 (block level), 32, 64 (+ a
-    // pending 64), then a binary counter 128 .. 32768 (sum u <= 3 K < 2^16)
+    // carry-save counters per column word: weights 1..16 (block level), 32, 64, 128
+    // (with pending words of weight 32, 64, 128), then a binary counter 256 .. 32768
+    // (sum u <= 3 K < 2^16)
     uint32_t p1[RNW], p2[RNW], p4[RNW], p8[RNW], p16[RNW], h32[RNW], pend32[RNW], h64[RNW], pend64[RNW];
-    uint32_t hh[RNW][9];
+    uint32_t h128[RNW], pend128[RNW], hh[RNW][8];
 #pragma unroll
     for (int v = 0; v < RNW; v++) {
         p1[v] = p2[v] = p4[v] = p8[v] = p16[v] = h32[v] = pend32[v] = h64[v] = pend64[v] = 0;
+        h128[v] = pend128[v] = 0;
 #pragma unroll
-        for (int l = 0; l < 9; l++) hh[v][l] = 0;
+        for (int l = 0; l < 8; l++) hh[v][l] = 0;
     }
 
     // chunk loads: each thread copies 32 contiguous bytes of the rows' records
@@ -699,7 +701,7 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         build_item(q, tid + 256);
     };
 
-    auto hot = [&](int q) {
+    auto hot = [&](int c, int q) {
         const uint8_t *buf = rsm + q * BUF_BYTES;
         const uint32_t *recs = reinterpret_cast<const uint32_t *>(buf + TAB_BYTES);
 #pragma unroll
@@ -746,8 +748,9 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
                 p8[v] ^= c8c;
                 const uint32_t c32 = csa(p16[v], c16a, c16b);
                 // static per chunk: blocks 0 / 2 leave a weight-32 carry pending, 1 / 3 pair it
-                // into h32; the weight-64 carries of blocks 1 and 3 pair into h64, whose carry
-                // ripples up the binary counter once per chunk
+                // into h32; the weight-64 carries of blocks 1 and 3 pair into h64; its carry is
+                // left pending in even chunks and paired into h128 in odd ones, whose carry
+                // ripples up the binary counter every second chunk
                 if ((b & 1) == 0) {
                     pend32[v] = c32;
                 } else {
@@ -756,13 +759,19 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
                     if (b == 1) {
                         pend64[v] = c64;
                     } else {
-                        uint32_t cc = csa(h64[v], pend64[v], c64);
+                        const uint32_t c128 = csa(h64[v], pend64[v], c64);
                         pend64[v] = 0;
+                        if ((c & 1) == 0) {
+                            pend128[v] = c128;
+                        } else {
+                            uint32_t cc = csa(h128[v], pend128[v], c128);
+                            pend128[v] = 0;
 #pragma unroll
-                        for (int l = 0; l < 9; l++) {
-                            const uint32_t t = hh[v][l] & cc;
-                            hh[v][l] ^= cc;
-                            cc = t;
+                            for (int l = 0; l < 8; l++) {
+                                const uint32_t t = hh[v][l] & cc;
+                                hh[v][l] ^= cc;
+                                cc = t;
+                            }
                         }
                     }
                 }
@@ -779,7 +788,7 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
     for (int c = 0; c < nch; c++) {
         const int q = c & 1;
         if (c + 1 < nch) load_chunk(c + 1, q ^ 1);
-        hot(q);
+        hot(c, q);
         cp_wait_all();
         __syncthreads();
         if (c + 1 < nch) build(q ^ 1);
@@ -798,9 +807,10 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         d[4 * RM] = p16[v];
         d[5 * RM] = h32[v];
         d[6 * RM] = h64[v];
-        d[7 * RM] = pend64[v];
+        d[7 * RM] = h128[v];
+        d[8 * RM] = pend128[v];
 #pragma unroll
-        for (int l = 0; l < 9; l++) d[(8 + l) * RM] = hh[v][l];
+        for (int l = 0; l < 8; l++) d[(9 + l) * RM] = hh[v][l];
     }
     __syncthreads();
 
@@ -812,7 +822,7 @@ __global__ void __launch_bounds__(256, 2) wide_rem_kernel(RemIn in) {
         uint32_t U = 0;
 #pragma unroll
         for (int l = 0; l < NPL; l++) {
-            const int wt = l < 7 ? l : l - 1;                    // planes 6 and 7 both weigh 64
+            const int wt = l < 8 ? l : l - 1;                    // planes 7 and 8 both weigh 128
             U += ((src[l * RM] >> bit) & 1u) << wt;
         }
         in.U[(int64_t)(m0 + mloc) * in.Np + n0 + nl] = (uint16_t)U;
