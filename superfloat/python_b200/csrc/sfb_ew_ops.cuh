@@ -18,27 +18,6 @@
 namespace sfb {
 namespace ewops {
 
-// floor(ua 2^sh / ub) for 0 <= ua <= ub < 2^15, ub >= 1, sh <= 15 (the
-// quotient is at most 2^sh, reached exactly when ua == ub).
-// Reciprocal estimate, then one exact integer correction:
-//   x = ua 2^sh / ub.  ua and ub convert to float exactly (integer-to-float
-//   conversions, on the XU pipe beside the reciprocal, which leaves the ALU
-//   pipe to the rest of the op); rcp.approx has relative error < 2^-22 and
-//   ua * (rcp(ub) 2^sh) rounds once (2^sh scales exactly), so the estimate is
-//   within 2^15 * 1.3 * 2^-22 < 0.01 of x.  Rounding it to the nearest
-//   integer (the 1.5 * 2^23 bias) gives floor(x) or floor(x) + 1, and the
-//   sign of the remainder tells which.
-__device__ __forceinline__ unsigned udiv_small(unsigned ua, unsigned ub, int sh) {
-    const float fa = __uint2float_rn(ua);
-    const float fb = __uint2float_rn(ub);
-    float r;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fb));
-    const float r2 = r * __int_as_float((127 + sh) << 23);          // r 2^sh, exact
-    const unsigned q0 = (unsigned)__float_as_int(fmaf(fa, r2, 12582912.0f)) - 0x4B400000u;
-    const unsigned rem = (ua << sh) - q0 * ub;
-    return q0 + (unsigned)((int)rem >> 31);                            // q0 - 1 when rem < 0
-}
-
 // Events one output raised; each op sets only the ones it can raise, so the
 // compiler drops the others from the tally.
 struct Ev {
@@ -80,16 +59,29 @@ __device__ __forceinline__ int ew_one(int a, int b, int c, Width w0, int pow_n, 
         ev.under = small_nonzero(p, sh);
         return r;
     } else if constexpr (OP == SFB_OP_DIV) {
-        // One quotient path for every case: with the dividend clamped to
-        // the divisor (and a zero divisor taken as 1) the quotient is at most
-        // 2^sh, reached exactly when |a| >= |b| > 0 (overflow) or b == 0 with
-        // a != 0 (divide); min(q, M) with the sign of a b then gives +-M
-        // there, 0 for 0 / 0, and trunc(a S / b) everywhere else.
-        const unsigned ua = (unsigned)abs(a), ub = (unsigned)abs(b);
-        const unsigned ub1 = max(ub, 1u);
-        const unsigned q = udiv_small(min(ua, ub1), ub1, sh);
+        // One quotient path for every case, mostly on the FMA and XU pipes.  The
+        // operands as float32 (exact), d = max(|b|, 1), x = min(|a|, d): the
+        // quotient q = floor(x 2^sh / d) is at most 2^sh, reached exactly when
+        // |a| >= |b| > 0 (overflow) or b == 0 with a != 0 (divide); min(q, M)
+        // with the sign of a b then gives +-M there, 0 for 0 / 0, and
+        // trunc(a S / b) everywhere else.
+        // q: x times rcp.approx(d) 2^sh (relative error < 2^-22, so within
+        // 2^15 2^-22 < 0.01 of x 2^sh / d) rounded to the nearest integer by the
+        // 1.5 2^23 bias gives floor or floor + 1, and the sign of the remainder
+        // x 2^sh - q0 d tells which; one fused multiply-add gives that
+        // remainder exactly (every term is an integer below 2^31 and the result
+        // is below 2^15 in magnitude).
+        const float fa = (float)a, fb = (float)b;
+        const float fd = fmaxf(fabsf(fb), 1.0f), fx = fminf(fabsf(fa), fd);
+        float r;
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fd));
+        const float scale = __int_as_float((127 + sh) << 23);              // 2^sh, exact
+        const float qb = fmaf(fx, r * scale, 12582912.0f);
+        const int q0 = __float_as_int(qb) - 0x4B400000;
+        const float rem = fmaf(-(qb - 12582912.0f), fd, fx * scale);
+        const int q = q0 + (__float_as_int(rem) >> 31);                    // q0 - 1 when rem < 0
         const int s = (a ^ b) >> 31;                 // -1 where the quotient is negative
-        const int m = (int)min(q, (unsigned)M);
+        const int m = min(q, M);
         ev.over = (q >> sh) != 0 && b != 0;
         ev.div0 = b == 0;
         return (m ^ s) - s;

@@ -1,11 +1,14 @@
 """The elementwise div's quotient step, emulated on the CPU with the
-kernel's float32 arithmetic (sfb_ew_ops.cuh, udiv_small): operands placed
-exactly by the exponent-bias trick, a reciprocal off by up to one ulp either
-way (the rcp.approx error), one fused multiply-add rounding to the nearest
-integer, one remainder correction.  It must give floor(ua 2^sh / ub) for every
-0 <= ua <= ub < 2^15, ub >= 1 (ua == ub included: the kernel clamps the
-dividend to the divisor so that every saturating case goes through the same
-quotient), and the full div rule built on it must equal the oracle."""
+kernel's float32 arithmetic (sfb_ew_ops.cuh, the div branch of ew_one):
+operands exact in float32, a reciprocal off by up to one ulp either way (the
+rcp.approx error), one fused multiply-add rounding to the nearest integer, and
+the remainder x 2^sh - q0 d from a second fused multiply-add (one float32
+rounding of the exact value), whose sign corrects q0.  It must give
+floor(ua 2^sh / ub) for every 0 <= ua <= ub < 2^15, ub >= 1 (ua == ub
+included: the kernel clamps the dividend to the divisor so that every
+saturating case goes through the same quotient), the float remainder must be
+the exact integer remainder, and the full div rule built on it must equal the
+oracle."""
 import numpy as np
 import pytest
 
@@ -13,16 +16,22 @@ from oracle import sfref
 
 
 def udiv_emulated(ua, ub, sh, ulp):
-    fa = (ua.astype(np.int64) << sh).astype(np.float32)          # exact: < 2^30 with <= 15 significant bits
-    fb = ub.astype(np.float32)
-    r = (np.float32(1.0) / fb).astype(np.float32)
+    fx = ua.astype(np.float32)                                    # exact: < 2^15
+    fd = ub.astype(np.float32)
+    r = (np.float32(1.0) / fd).astype(np.float32)
     if ulp:
         r = np.nextafter(r, np.float32(np.inf if ulp > 0 else 0.0)).astype(np.float32)
-    x = fa.astype(np.float64) * r.astype(np.float64)              # exact product of two float32
+    r2 = (r * np.float32(2.0 ** sh)).astype(np.float32)          # exact: a power of two
+    x = fx.astype(np.float64) * r2.astype(np.float64)             # exact product of two float32
     assert np.all(x < 2.0 ** 22)                                  # the 1.5 * 2^23 rounding bias applies
     q0 = np.rint(x).astype(np.int64)                              # the fused add of 1.5 * 2^23: nearest, ties even
+    # the second fused multiply-add: -q0 d + x 2^sh exactly, rounded once to float32
+    exact = -q0.astype(np.float64) * fd.astype(np.float64) + fx.astype(np.float64) * 2.0 ** sh
+    rem_f = exact.astype(np.float32)
     rem = (ua.astype(np.int64) << sh) - q0 * ub.astype(np.int64)
-    return q0 - (rem < 0)
+    np.testing.assert_array_equal(rem_f.astype(np.int64), rem)   # the float remainder is exact
+    assert np.all(np.abs(rem) < ub.astype(np.int64))
+    return q0 - (rem_f < 0)
 
 
 def pairs(rng):
