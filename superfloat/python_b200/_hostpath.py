@@ -19,7 +19,7 @@ _ARITY = {"add": 2, "sub": 2, "mul": 2, "div": 2, "fma": 3, "neg": 1, "abs": 1, 
 class HostPipeline:
     """Device staging for host-buffer elementwise ops on one B200Device."""
 
-    def __init__(self, dev, chunk: int = 1 << 22, slots: int = 2):
+    def __init__(self, dev, chunk: int = 1 << 23, slots: int = 2):
         import torch
         self.dev = dev
         self.chunk = chunk
