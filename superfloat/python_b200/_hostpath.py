@@ -2,7 +2,8 @@
 
 A caller whose codes live in host memory (int16, pinned) gets the same
 kernels with the copies hidden behind them: the element range is cut into
-chunks, and each chunk's host-to-device copies, kernel and device-to-host copy
+chunks (the last few smaller, so that the drain after the last copy in is
+short), and each chunk's host-to-device copies, kernel and device-to-host copy
 are queued on one of two streams, so one chunk's copies overlap the other's
 kernel and the copy engines run both directions at once.  Status counts
 accumulate on the device and are read once at the end.
@@ -16,10 +17,31 @@ from . import _lib
 _ARITY = {"add": 2, "sub": 2, "mul": 2, "div": 2, "fma": 3, "neg": 1, "abs": 1, "sqrt": 1, "pow": 1}
 
 
+def cuts(n: int, chunk: int) -> list:
+    """``[lo, hi)`` ranges covering ``n`` elements for the pipeline: full
+    chunks, then the last two chunks' worth halved step by step down to
+    chunk / 8.  After the last host-to-device copy only the smallest chunk's
+    kernel and copy back are left, so one op's drain is short.  Every ``lo``
+    is a multiple of 8 codes (16 bytes), which keeps the kernel's vector path."""
+    small = max(chunk // 8, 8)
+    out, lo = [], 0
+    while lo < n:
+        rem = n - lo
+        if rem > 2 * chunk:
+            m = chunk
+        elif rem > small:
+            m = min(chunk, (rem // 2 + 7) & ~7)
+        else:
+            m = rem
+        out.append((lo, lo + m))
+        lo += m
+    return out
+
+
 class HostPipeline:
     """Device staging for host-buffer elementwise ops on one B200Device."""
 
-    def __init__(self, dev, chunk: int = 1 << 23, slots: int = 2):
+    def __init__(self, dev, chunk: int = 1 << 24, slots: int = 2):
         import torch
         self.dev = dev
         self.chunk = chunk
@@ -46,9 +68,7 @@ class HostPipeline:
         cur = torch.cuda.current_stream(self.dev.torch_device)
         for s in self.streams:
             s.wait_stream(cur)
-        k = 0
-        for lo in range(0, n, self.chunk):
-            hi = min(n, lo + self.chunk)
+        for k, (lo, hi) in enumerate(cuts(n, self.chunk)):
             m = hi - lo
             slot = k % len(self.streams)
             st = self.streams[slot]
@@ -68,7 +88,6 @@ class HostPipeline:
                 out[lo:hi].copy_(o, non_blocking=True)
                 if flags_out is not None:
                     flags_out[lo:hi].copy_(fl, non_blocking=True)
-            k += 1
         for s in self.streams:
             cur.wait_stream(s)
         total = self.counts[0].clone()

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
     constexpr bool kB = OP == SFB_OP_ADD || OP == SFB_OP_SUB || OP == SFB_OP_MUL || OP == SFB_OP_DIV ||
                         OP == SFB_OP_FMA;
     constexpr bool kC = OP == SFB_OP_FMA;
+    constexpr bool kPacked = OP == SFB_OP_DIV && !FLAGS && !SM;   // div's two counts in one word
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     int64_t done = 0;
@@ -84,12 +85,21 @@ __global__ void __launch_bounds__(kThreads) ew_kernel(const int16_t *__restrict_
             for (int h = 0; h < 2; h++) {
                 if (h == 1 && !has2) break;
                 uint64_t fb = 0;
+                unsigned pk = 0;
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     Ev ev;
                     vo[h].h[j] = (int16_t)one(va[h].h[j], kB ? vb[h].h[j] : 0, kC ? vc[h].h[j] : 0, ev);
-                    tally(cnt, ev);
+                    if constexpr (kPacked) {
+                        pk += ev.pk;
+                    } else {
+                        tally(cnt, ev);
+                    }
                     if constexpr (FLAGS) fb |= (uint64_t)flag_byte(ev) << (8 * j);
+                }
+                if constexpr (kPacked) {
+                    cnt.over += pk & 0xFFFFu;
+                    cnt.div0 += pk >> 16;
                 }
                 const int64_t vv = h ? v2 : v;
                 __stcs(reinterpret_cast<uint4 *>(out) + vv, vo[h].u);

@@ -22,6 +22,9 @@ namespace ewops {
 // compiler drops the others from the tally.
 struct Ev {
     bool over = false, under = false, div0 = false, inval = false;
+    // div only: both events in one word, 0x10000 for a divide, else 1 for
+    // an overflow (a kernel that only counts adds these and splits the sum)
+    unsigned pk = 0;
 };
 
 // Width constants, folded at compile time for BITS != 0 (the sf16 kernels).
@@ -65,26 +68,29 @@ __device__ __forceinline__ int ew_one(int a, int b, int c, Width w0, int pow_n, 
         // |a| >= |b| > 0 (overflow) or b == 0 with a != 0 (divide); min(q, M)
         // with the sign of a b then gives +-M there, 0 for 0 / 0, and
         // trunc(a S / b) everywhere else.
-        // q: x times rcp.approx(d) 2^sh (relative error < 2^-22, so within
-        // 2^15 2^-22 < 0.01 of x 2^sh / d) rounded to the nearest integer by the
-        // 1.5 2^23 bias gives floor or floor + 1, and the sign of the remainder
-        // x 2^sh - q0 d tells which; one fused multiply-add gives that
-        // remainder exactly (every term is an integer below 2^31 and the result
-        // is below 2^15 in magnitude).
+        // With dp = d 2^-sh (exact), rcp.approx(dp) is 2^sh / d to a relative
+        // error below 2^-22, so x rcp(dp) is within 2^15 2^-22 < 0.01 of the
+        // quotient; the 1.5 2^23 bias rounds it to the nearest integer q0
+        // (floor or floor + 1), and the sign of x - q0 dp = (x 2^sh - q0 d) 2^-sh
+        // tells which.  One fused multiply-add gives that remainder exactly
+        // (an integer below 2^16 in magnitude times 2^-sh).
         const float fa = (float)a, fb = (float)b;
         const float fd = fmaxf(fabsf(fb), 1.0f), fx = fminf(fabsf(fa), fd);
+        const float fdp = fd * __int_as_float((127 - sh) << 23);           // d 2^-sh, exact
         float r;
-        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fd));
-        const float scale = __int_as_float((127 + sh) << 23);              // 2^sh, exact
-        const float qb = fmaf(fx, r * scale, 12582912.0f);
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(fdp));
+        const float qb = fmaf(fx, r, 12582912.0f);
         const int q0 = __float_as_int(qb) - 0x4B400000;
-        const float rem = fmaf(-(qb - 12582912.0f), fd, fx * scale);
+        const float rem = fmaf(-(qb - 12582912.0f), fdp, fx);
         const int q = q0 + (__float_as_int(rem) >> 31);                    // q0 - 1 when rem < 0
-        const int s = (a ^ b) >> 31;                 // -1 where the quotient is negative
         const int m = min(q, M);
-        ev.over = (q >> sh) != 0 && b != 0;
-        ev.div0 = b == 0;
-        return (m ^ s) - s;
+        // b == 0 and the quotient's sign read from the float copies, so the
+        // integer codes are only ever converted
+        const bool bz = fb == 0.0f;
+        ev.over = (q >> sh) != 0 && !bz;
+        ev.div0 = bz;
+        ev.pk = bz ? 0x10000u : (unsigned)(q >> sh);   // q >> sh is the overflow where b != 0
+        return (__float_as_int(fa) ^ __float_as_int(fb)) < 0 ? -m : m;
     } else if constexpr (OP == SFB_OP_NEG) {
         return -a;
     } else if constexpr (OP == SFB_OP_ABS) {

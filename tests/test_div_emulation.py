@@ -1,9 +1,9 @@
 """The elementwise div's quotient step, emulated on the CPU with the
 kernel's float32 arithmetic (sfb_ew_ops.cuh, the div branch of ew_one):
 operands exact in float32, a reciprocal off by up to one ulp either way (the
-rcp.approx error), one fused multiply-add rounding to the nearest integer, and
-the remainder x 2^sh - q0 d from a second fused multiply-add (one float32
-rounding of the exact value), whose sign corrects q0.  It must give
+rcp.approx error) of d 2^-sh, one fused multiply-add rounding to the nearest
+integer, and the remainder x - q0 d 2^-sh from a second fused multiply-add
+(one float32 rounding of the exact value), whose sign corrects q0.  It must give
 floor(ua 2^sh / ub) for every 0 <= ua <= ub < 2^15, ub >= 1 (ua == ub
 included: the kernel clamps the dividend to the divisor so that every
 saturating case goes through the same quotient), the float remainder must be
@@ -21,15 +21,17 @@ def udiv_emulated(ua, ub, sh, ulp):
     r = (np.float32(1.0) / fd).astype(np.float32)
     if ulp:
         r = np.nextafter(r, np.float32(np.inf if ulp > 0 else 0.0)).astype(np.float32)
-    r2 = (r * np.float32(2.0 ** sh)).astype(np.float32)          # exact: a power of two
+    # rcp.approx(d 2^-sh) = 2^sh rcp.approx(d): scaling by a power of two is exact
+    r2 = (r * np.float32(2.0 ** sh)).astype(np.float32)
+    fdp = (fd * np.float32(2.0 ** -sh)).astype(np.float32)       # exact
     x = fx.astype(np.float64) * r2.astype(np.float64)             # exact product of two float32
     assert np.all(x < 2.0 ** 22)                                  # the 1.5 * 2^23 rounding bias applies
     q0 = np.rint(x).astype(np.int64)                              # the fused add of 1.5 * 2^23: nearest, ties even
-    # the second fused multiply-add: -q0 d + x 2^sh exactly, rounded once to float32
-    exact = -q0.astype(np.float64) * fd.astype(np.float64) + fx.astype(np.float64) * 2.0 ** sh
+    # the second fused multiply-add: x - q0 dp exactly, rounded once to float32
+    exact = -q0.astype(np.float64) * fdp.astype(np.float64) + fx.astype(np.float64)
     rem_f = exact.astype(np.float32)
     rem = (ua.astype(np.int64) << sh) - q0 * ub.astype(np.int64)
-    np.testing.assert_array_equal(rem_f.astype(np.int64), rem)   # the float remainder is exact
+    np.testing.assert_array_equal(rem_f.astype(np.float64) * 2.0 ** sh, rem)   # the float remainder is exact
     assert np.all(np.abs(rem) < ub.astype(np.int64))
     return q0 - (rem_f < 0)
 

@@ -168,3 +168,17 @@ def test_device_registry_and_attributes():
     assert sf.get_device("b200-v481") is mine and mine.mx == "v4.8.1"
     with pytest.raises(ValueError):
         sf.B200Device(0, mx="v9")
+
+
+@pytest.mark.parametrize("n", [0, 1, 7, 8, 1000, (1 << 20) + 3, 3 << 20, (1 << 26) + 12345])
+def test_host_pipeline_cuts(n):
+    """The host pipeline's chunk ranges: contiguous cover of [0, n), no chunk
+    above the slot size, 16-byte aligned starts, and a short last chunk."""
+    from superfloat.python_b200._hostpath import cuts
+    chunk = 1 << 20
+    c = cuts(n, chunk)
+    assert [lo for lo, _ in c] == ([0] if c else []) + [hi for _, hi in c[:-1]]
+    assert (c[-1][1] if c else 0) == n
+    assert all(0 < hi - lo <= chunk and lo % 8 == 0 for lo, hi in c)
+    if n > 2 * chunk:
+        assert c[-1][1] - c[-1][0] <= chunk // 8
