@@ -228,10 +228,14 @@ def main():
     targs = {"add": (tx, ty), "sub": (tx, ty), "mul": (tx, ty), "fma": (tx, ty, tz), "div": (tx, td)}
     stream = torch.cuda.current_stream()
 
-    # one count buffer per step: a step's status all-reduce runs on NCCL's stream
-    # while the next step's kernels run; the timed region waits for every one
-    bufs = [torch.zeros_like(counts) for _ in range(max(args.steps, args.warmup))]
-    pending = []
+    # one count buffer per step, zeroed by the step itself.  The element ranges
+    # are independent, so no rank needs another's counts during the run: every
+    # step's counters are summed over the ranks in one all-reduce at the end of
+    # the timed region (a per-step all-reduce ran beside the next step's first
+    # kernel on NCCL's stream and slowed it)
+    allbufs = torch.zeros(max(args.steps, args.warmup), len(OPS), _lib.N_COUNTS, dtype=torch.int64,
+                          device=dev.torch_device)
+    bufs = list(allbufs.unbind(0))
 
     def step(evs=None, buf=None):
         buf.zero_()
@@ -241,12 +245,10 @@ def main():
             dev.run_device(op, fmt, *targs[op], out=outs[op], counts=buf[i])
             if evs is not None:
                 evs[op][1].record(stream)
-        if world > 1:
-            pending.append(dist.all_reduce(buf, async_op=True))
 
     def drain():
-        while pending:
-            pending.pop(0).wait()
+        if world > 1:
+            dist.all_reduce(allbufs)
 
     for i in range(args.warmup):
         step(buf=bufs[i])
@@ -269,7 +271,7 @@ def main():
         evs = {op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
         step(evs, bufs[i])
         evs_all.append(evs)
-    drain()                                  # the last reductions are part of the timed work
+    drain()                                  # the status reduction is part of the timed work
     t_end.record(stream)
     counts = bufs[args.steps - 1]
     torch.cuda.synchronize()
