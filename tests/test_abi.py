@@ -80,3 +80,47 @@ def test_missing_library_fails_loudly(tmp_path):
             _lib.load(str(tmp_path / "nope.so"))
     finally:
         _lib._lib = saved
+
+
+def _header_prototypes():
+    """name -> (return type, [parameter types]) from include/sfb200.h."""
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    out = {}
+    for ret, name, params in re.findall(r"SFB_API\s+([\w\s\*]+?)\s*\b(sfb_\w+)\s*\(([^)]*)\)\s*;", text):
+        ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        out[name] = (ret.strip(), [re.sub(r"\s*\b\w+$", "", p).strip() if not p.endswith("*") else p for p in ps])
+    return out
+
+
+def _ctype_of(c_type):
+    t = c_type.replace("const", "").strip()
+    if "*" in t or t == "sfb_stream":
+        return ctypes.c_void_p
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "double": ctypes.c_double,
+            "const char": ctypes.c_char_p}.get(t)
+
+
+def test_header_parameter_types_match_the_bindings():
+    """Every prototype's parameter list (count and C type) is the ctypes
+    signature the Python side binds, so no argument is passed at the wrong width."""
+    protos = _header_prototypes()
+    assert set(protos) == set(_lib.SIGNATURES)
+    for name, (ret, params) in protos.items():
+        res, args = _lib.SIGNATURES[name]
+        want_res = {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "const char *": ctypes.c_char_p}[ret]
+        assert res is want_res, (name, ret, res)
+        assert len(params) == len(args), (name, params)
+        for i, (p, a) in enumerate(zip(params, args)):
+            assert _ctype_of(p) is a, (name, i, p, a)
+
+
+def test_integration_stub_argtypes_match_the_bindings():
+    """The ctypes stub a maintainer copies into the reference
+    binds the same argument lists as this package."""
+    text = open(os.path.join(REPO, "INTEGRATION.md")).read()
+    kinds = {"P": ctypes.c_void_p, "I32": ctypes.c_int, "I64": ctypes.c_int64, "ctypes.c_double": ctypes.c_double}
+    found = re.findall(r"_lib\.(sfb_\w+)\.argtypes = \[([^\]]*)\]", text)
+    assert {n for n, _ in found} >= {"sfb_elementwise", "sfb_matmul_chain", "sfb_matmul_wide"}
+    for name, body in found:
+        got = [kinds[t.strip()] for t in body.replace("\n", " ").split(",") if t.strip()]
+        assert got == list(_lib.SIGNATURES[name][1]), name
