@@ -7,6 +7,8 @@ product (a bit-by-bit walk of the partial-product rows):
   16-entry tables F(x mod 16) and G(x >> 4) of two-bit words per (k, 32-column
   word), with w's sign and the +1 folded in (prep_kernel's column bits,
   wide_rem_kernel's table build);
+* prep_kernel's A records (two k per 32-bit word) and the hot loop's decode of
+  them (mask, byte permutes, sign-replicating permutes, the umulhi offset);
 * u for 32 products = the two-bit add of one F and one G entry with a's sign
   as an all-ones mask, and sum_k u through the kernel's carry-save bit-plane
   counters (blocks of 8 k, chunks of 32, the pending levels and the ripple of
@@ -80,6 +82,44 @@ def _tables(wm, sw):
             lo_t[:, :, idx], hi_t[:, :, idx] = e
         tabs.append((lo_t, hi_t))
     return tabs
+
+
+RTSTR8 = (32 * 4 + 1) * 8          # table entry stride in bytes (RTSTR 64-bit pairs)
+
+
+def _prmt(x, sel):
+    """prmt.b32 d, x, 0, sel (default mode): byte i of d is byte sel_i & 7 of
+    (x, 0), replicated from that byte's top bit when sel_i has bit 3 set."""
+    pool = [(x >> (8 * i)) & 0xFF for i in range(4)] + [np.zeros_like(x)] * 4
+    d = np.zeros_like(x)
+    for i in range(4):
+        n = (sel >> (4 * i)) & 0xF
+        v = pool[n & 7]
+        if n & 8:
+            v = np.where(v & 0x80, 0xFF, 0).astype(x.dtype)
+        d |= v << (8 * i)
+    return d
+
+
+def test_records_decode_as_the_hot_loop_reads_them(rng):
+    """prep_kernel's A records (two k per 32-bit word: byte 0 = (x & 15) | s << 7,
+    byte 1 = x >> 4, bytes 2-3 the next k) read back with the hot loop's
+    operations: the F / G table offsets, and a's sign as an all-ones mask."""
+    codes = rng.integers(-32767, 32768, (64, 2))
+    codes[:4] = [[0, -1], [32767, -32767], [-256, 255], [16, -15]]
+    a = np.abs(codes) & 255
+    s = (codes < 0).astype(np.uint64)
+    rec16 = (a & 15).astype(np.uint64) | (s << np.uint64(7)) | ((a >> 4).astype(np.uint64) << np.uint64(8))
+    r = rec16[:, 0] | (rec16[:, 1] << np.uint64(16))
+    # even k: r & 0xF, prmt 0x4441, sign prmt 0x8888
+    np.testing.assert_array_equal((r & np.uint64(0xF)) * RTSTR8, (a[:, 0] & 15) * RTSTR8)
+    np.testing.assert_array_equal(_prmt(r, 0x4441), a[:, 0] >> 4)
+    np.testing.assert_array_equal(_prmt(r, 0x8888), np.where(codes[:, 0] < 0, 0xFFFFFFFF, 0))
+    # odd k: umulhi(r & 0xF0000, stride << 16), prmt 0x4443, sign prmt 0xAAAA
+    umulhi = ((r & np.uint64(0xF0000)) * np.uint64(RTSTR8 << 16)) >> np.uint64(32)
+    np.testing.assert_array_equal(umulhi, (a[:, 1] & 15) * RTSTR8)
+    np.testing.assert_array_equal(_prmt(r, 0x4443), a[:, 1] >> 4)
+    np.testing.assert_array_equal(_prmt(r, 0xAAAA), np.where(codes[:, 1] < 0, 0xFFFFFFFF, 0))
 
 
 def _u_words(am, sa, tabs):
