@@ -124,3 +124,25 @@ def test_integration_stub_argtypes_match_the_bindings():
     for name, body in found:
         got = [kinds[t.strip()] for t in body.replace("\n", " ").split(",") if t.strip()]
         assert got == list(_lib.SIGNATURES[name][1]), name
+
+
+def test_device_side_failures_surface_as_errors():
+    """A kernel that gave up on a bounded wait, a chain whose no-saturation
+    proof did not hold, and a sign-magnitude word wider than the format each
+    leave a count in a reserved slot of sfb_counts; the host turns each into an
+    error instead of returning the outputs (no GPU: the counters are host data)."""
+    import numpy as np
+    from superfloat.python_b200._errors import SFDeviceError
+    ok = np.zeros(_lib.N_COUNTS, np.int64)
+    ok[:4] = [5, 1, 2, 0]                      # ordinary events are not failures
+    _lib.check_counts(ok)
+    _lib.check_patterns(ok, 16)
+    for slot, what in ((5, "gave up waiting"), (6, "left the range")):
+        c = ok.copy()
+        c[slot] = 3
+        with pytest.raises(SFDeviceError, match=what):
+            _lib.check_counts(c)
+    c = ok.copy()
+    c[7] = 2
+    with pytest.raises(ValueError, match="do not fit in 12 bits"):
+        _lib.check_patterns(c, 12)
