@@ -140,11 +140,27 @@ def _cpu_pool_worker(n):
     return cpu_sample(n)
 
 
+def host_cores() -> int:
+    """CPUs this process may run on: the affinity mask, capped by a cgroup v2
+    CPU quota when one is set (a container can see more cores than it gets)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        quota, period = open("/sys/fs/cgroup/cpu.max").read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     import multiprocessing as mp
-    cores = os.cpu_count() or 1
+    cores = host_cores()
     n_sample = 1 << 22                             # per process per step
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
