@@ -32,7 +32,6 @@ from dataclasses import dataclass
 import torch
 
 from .. import _lib
-from .._format import FORMATS
 from . import _core
 
 # (W, F) of the MX units per chip and block (src/sf/_linalg.py:144-147)

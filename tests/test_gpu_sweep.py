@@ -1,7 +1,6 @@
 """The exhaustive sweep kernel against the reference's digests
 (tests/golden/sweep.json): every pair of sf16, sf8 and sf4 codes for add,
 sub, mul and div, plus oracle rows and row-range sharding."""
-import numpy as np
 import pytest
 
 from conftest import golden

@@ -11,7 +11,6 @@ inside int32 up to K = 16384 (the accumulators are 32-bit)."""
 import numpy as np
 import pytest
 
-from oracle import sfref
 
 
 def planes(codes, bits, is_a):
