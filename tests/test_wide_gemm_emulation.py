@@ -12,7 +12,6 @@ import numpy as np
 import pytest
 
 
-
 def planes(codes, bits, is_a):
     """The nine planes of prep_kernel as int64 values of their int8 bytes,
     read signed or unsigned as the GEMM reads them: (9, rows, K)."""
