@@ -237,7 +237,8 @@ SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B
  * The same arguments and results as sfb_matmul_wide, minus the workspace: the
  * scratch is a fixed 64 MiB array inside the library, held on every GPU that
  * loads the library until the process exits.  The first call on a device
- * looks up that array's address (with that device current).  Problems whose
+ * looks up that array's address (with that device current), so make that
+ * first call before any CUDA stream capture on the device.  Problems whose
  * scratch exceeds 64 MiB (sfb_matmul_wide_workspace() > 64 MiB: 1536^3 fits, 2048^3
  * needs about 105 MiB) are refused with SFB_ERANGE.  All calls share the one
  * array, so calls whose kernels overlap on the GPU (other streams or host

@@ -1131,7 +1131,8 @@ extern "C" int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const
                                        int64_t stride_a, int64_t stride_b, int64_t stride_out, int64_t shift_sb,
                                        int64_t shift_sm, int64_t shift_sn, sfb_counts *counts, sfb_stream stream) {
     using namespace sfb;
-    // the array's device address, looked up once per device with that device current
+    // the array's device address, looked up by the first call on each device with
+    // that device current (so that first call belongs before any stream capture)
     static void *scratch[64] = {};
     static std::mutex lock;
     int dev = 0;
