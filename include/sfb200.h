@@ -229,6 +229,17 @@ SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B
                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
                     void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
 
+/* Failure-detection hook with no counterpart in the reference: the wide
+ * tensor-core GEMM launches that the CALLING THREAD makes from now on bound
+ * each of their pipeline waits (an mbarrier poll loop) by `polls` polls
+ * (0 restores the default, 2^26), and with `stall` nonzero their MMA thread
+ * first waits on a barrier that nothing arrives on.  A wait that runs out
+ * adds 1 per CTA to counts->reserved[0]; the kernel still lets its copies in
+ * flight land and frees its tensor memory before it returns, so the context
+ * stays usable and the host reports the failure from the counts.  Tests
+ * only: a stalled call's outputs are not valid.  Always returns SFB_OK. */
+SFB_API int sfb_wide_wait_limit(unsigned polls, int stall);
+
 /* sfb_matmul_wide without any device allocation, for callers that cannot
  * allocate device memory while they run: a host program that has handed all
  * of the GPU's memory to its own pool, a plugin host that forbids allocation
@@ -238,9 +249,10 @@ SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B
  * scratch is a fixed 64 MiB array inside the library, held on every GPU that
  * loads the library until the process exits.  The first call on a device
  * looks up that array's address (with that device current), so make that
- * first call before any CUDA stream capture on the device.  Problems whose
- * scratch exceeds 64 MiB (sfb_matmul_wide_workspace() > 64 MiB: 1536^3 fits, 2048^3
- * needs about 105 MiB) are refused with SFB_ERANGE.  All calls share the one
+ * first call before any CUDA stream capture on the device; after a device
+ * reset the next call looks it up again.  Problems whose scratch exceeds
+ * 64 MiB (sfb_matmul_wide_workspace() > 64 MiB: 1536^3 fits, 2048^3 needs
+ * about 109 MiB) are refused with SFB_ERANGE.  All calls share the one
  * array, so calls whose kernels overlap on the GPU (other streams or host
  * threads) race; serialise them. */
 SFB_API int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr,

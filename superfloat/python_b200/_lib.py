@@ -42,6 +42,7 @@ SIGNATURES = {
                                _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
+    "sfb_wide_wait_limit": (_i32, [ctypes.c_uint, _i32]),
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),

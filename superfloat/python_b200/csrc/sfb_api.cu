@@ -1,6 +1,9 @@
 // Library-level entry points of libsfb200: version, errors, device checks.
+#include <cuda.h>
 #include <stdarg.h>
 #include <stdio.h>
+
+#include <mutex>
 
 #include "sfb_common.cuh"
 
@@ -27,6 +30,30 @@ int sm_count() {
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
     return n;
+}
+
+unsigned long long context_id() {
+    typedef CUresult (*GetCurrent)(CUcontext *);
+    typedef CUresult (*GetId)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+    if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
 }
 
 }  // namespace sfb

@@ -668,19 +668,21 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
         return set_error(SFB_ERANGE, "%s: %lld x %lld x %lld (batch %lld) exceeds the launch limits", what,
                          (long long)M, (long long)N, (long long)K, (long long)batch);
     dim3 grid((unsigned)nt, (unsigned)mt, (unsigned)batch);
-    static bool attr[64][3] = {};
+    // shared-memory limits set once per CUDA context (a device reset starts a new one)
+    static unsigned long long attr[64][3] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
+    const unsigned long long ctx = context_id();
     const Width w = width(bits);
     const int vec = (lda % 8 == 0) && (ldb % 8 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0) &&
                     (sa % 8 == 0) && (sb % 8 == 0);
     if (safe) {
-        if (!attr[dev][2]) {
+        if (ctx == 0 || attr[dev][2] != ctx) {
             if (cudaFuncSetAttribute(chain_pk_kernel<TMP, NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      pk_smem<TMP, NTP>()) != cudaSuccess)
                 return check_launch(what);
-            attr[dev][2] = true;
+            attr[dev][2] = context_id();
         }
         chain_pk_kernel<TMP, NTP><<<grid, NTP, pk_smem<TMP, NTP>(), st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa,
                                                                           sb, so, w, e, vec, 1u, counts);
@@ -692,21 +694,21 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
         const dim3 g2((unsigned)nt, (unsigned)((M + 31) / 32), (unsigned)batch);
         const int smem = 2 * (int)sizeof(Stage<32>);
         auto kern = b16 ? chain2_kernel<false, true, 4, 128> : chain2_kernel<false, false, 4, 128>;
-        static bool attr_s[64][2] = {};
-        if (!attr_s[dev][b16]) {
+        static unsigned long long attr_s[64][2] = {};
+        if (ctx == 0 || attr_s[dev][b16] != ctx) {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
                 return check_launch(what);
-            attr_s[dev][b16] = true;
+            attr_s[dev][b16] = context_id();
         }
         kern<<<g2, 128, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
         return check_launch(what);
     }
     const int smem = 2 * (int)sizeof(Stage<64>);
     auto kern = b16 ? chain2_kernel<false, true, 4> : chain2_kernel<false, false, 4>;
-    if (!attr[dev][b16]) {
+    if (ctx == 0 || attr[dev][b16] != ctx) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch(what);
-        attr[dev][b16] = true;
+        attr[dev][b16] = context_id();
     }
     kern<<<grid, THREADS, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
     return check_launch(what);
@@ -799,14 +801,15 @@ extern "C" int sfb_matmul_chain_ws(int bits, const int16_t *A, const int16_t *B,
     const int vec = (lda % 8 == 0) && (ldb % 8 == 0) && ((uintptr_t)A % 16 == 0) && ((uintptr_t)B % 16 == 0);
     const int smem = 2 * (int)sizeof(Stage<64>);
     auto kern = bits == 16 ? chain_piece_kernel<true> : chain_piece_kernel<false>;
-    static bool attr[64][2] = {};
+    static unsigned long long attr[64][2] = {};      // set once per CUDA context
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (!attr[dev][bits == 16]) {
+    const unsigned long long ctx = context_id();
+    if (ctx == 0 || attr[dev][bits == 16] != ctx) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch("sfb_matmul_chain_ws");
-        attr[dev][bits == 16] = true;
+        attr[dev][bits == 16] = context_id();
     }
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + 63) / 64), (unsigned)np);
     Piece *ws = reinterpret_cast<Piece *>(workspace);

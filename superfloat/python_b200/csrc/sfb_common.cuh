@@ -64,4 +64,11 @@ int set_error(int code, const char *fmt, ...);
 int check_launch(const char *what);
 int sm_count();
 
+// A number naming the calling thread's current CUDA context for the life of
+// the process (the driver's cuCtxGetId): the context that replaces one torn
+// down by a device reset gets a new number, so per-device set-up cached
+// under it (kernel attributes, a static array's device address) is redone
+// rather than reused.  0 when no context is current yet.
+unsigned long long context_id();
+
 }  // namespace sfb

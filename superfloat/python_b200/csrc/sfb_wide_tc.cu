@@ -66,7 +66,7 @@ constexpr int NPLANES = 9;         // int8 operand planes per matrix
 constexpr int STAGE_BYTES = TILE * TILE + GN * TILE;
 constexpr int GEMM_SMEM = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int KMAX = 16384;        // |D| < 2^31 up to this K
-constexpr unsigned kSpinLimit = 1u << 26;
+constexpr unsigned kSpinLimit = 1u << 26;     // polls of one bounded wait, unless the launch gives fewer
 
 // --- PTX wrappers --------------------------------------------------------------------------
 
@@ -92,9 +92,9 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// bounded wait: false after kSpinLimit polls
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (unsigned i = 0; i < kSpinLimit; i++)
+// bounded wait: false after `limit` polls
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned limit = kSpinLimit) {
+    for (unsigned i = 0; i < limit; i++)
         if (mbar_try(bar, parity)) return true;
     return false;
 }
@@ -308,8 +308,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const int16_t *__restrict__ X
 // Warp 0 lane 0 issues the TMA loads (A and B tiles of each pass, both
 // phases, in one ring of stages); warp 1 lane 0 issues the MMAs (one thread,
 // as tcgen05 requires); warps 2..5 fold and write out (warp w reaches TMEM
-// lanes 32 (w mod 4) .. + 31).  Every wait is bounded: on timeout the kernel
-// records an error in the caller's counters and returns after freeing TMEM.
+// lanes 32 (w mod 4) .. + 31).  Every wait is bounded: the pipeline's waits by
+// `spin` polls, after which the kernel records an error in the caller's
+// counters; the teardown then waits (by kSpinLimit polls) for the copies and
+// the MMA commits still in flight, frees TMEM and returns.  `stall` (tests
+// only) makes the MMA thread first wait on a barrier nothing arrives on, so
+// a test can watch a wait run out.
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
@@ -356,15 +360,17 @@ __device__ __forceinline__ Pass pass_of(int it, int nkb) {
 __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                                                                   const __grid_constant__ CUtensorMap tmB, int nkb,
                                                                   int32_t *__restrict__ SX, int Np,
-                                                                  unsigned long long *__restrict__ err) {
+                                                                  unsigned long long *__restrict__ err,
+                                                                  unsigned spin, int stall) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
-    // bars[0..S): full, [S..2S): empty, [2S]: phase 1 done, [2S+1]: fold done, [2S+2]: all done
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 3);
+    // bars[0..S): full, [S..2S): empty, [2S]: phase 1 done, [2S+1]: fold done, [2S+2]: all done,
+    // [2S+3]: the barrier nothing arrives on (the stall test)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
     __shared__ int s_fail;
     const uint32_t bar_p1 = smem_u32(&bars[2 * STAGES]), bar_fold = smem_u32(&bars[2 * STAGES + 1]),
-                   bar_done = smem_u32(&bars[2 * STAGES + 2]);
+                   bar_done = smem_u32(&bars[2 * STAGES + 2]), bar_never = smem_u32(&bars[2 * STAGES + 3]);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // grouped order: GROUP_M row tiles at a time sweep the column tiles, so the
@@ -383,6 +389,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
         mbar_init(bar_p1, 1);
         mbar_init(bar_fold, 4);
         mbar_init(bar_done, 1);
+        mbar_init(bar_never, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
         // TMA producer
         for (int it = 0; it < total; it++) {
             const int s = it % STAGES, round = it / STAGES;
-            if (round > 0 && !mbar_wait(smem_u32(&bars[STAGES + s]), (round - 1) & 1)) {
+            if (round > 0 && !mbar_wait(smem_u32(&bars[STAGES + s]), (round - 1) & 1, spin)) {
                 s_fail = 1;
                 break;
             }
@@ -418,18 +425,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
         }
     } else if (threadIdx.x == 32) {
         // MMA issuer
+        if (stall && !mbar_wait(bar_never, 0, spin)) ok = false;
         for (int it = 0; it < total && ok; it++) {
             if (it == P1 * nkb) {
                 // phase 1 complete: let the fold run, then overwrite D0's columns
                 mma_commit(bar_p1);
-                if (!mbar_wait(bar_fold, 0)) {
+                if (!mbar_wait(bar_fold, 0, spin)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
             }
             const int s = it % STAGES, round = it / STAGES;
-            if (!mbar_wait(smem_u32(&bars[s]), round & 1)) {
+            if (!mbar_wait(smem_u32(&bars[s]), round & 1, spin)) {
                 ok = false;
                 break;
             }
@@ -453,7 +461,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
         const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
         // the fold: E = 2^8 D0 + D1 (mod 2^32) into D1's columns
         // each decision is the whole warp's: the TMEM loads and stores are warp-collective
-        bool fine = __all_sync(0xffffffffu, mbar_wait(bar_p1, 0) && !*(volatile int *)&s_fail);
+        bool fine = __all_sync(0xffffffffu, mbar_wait(bar_p1, 0, spin) && !*(volatile int *)&s_fail);
         tc_fence_after();
         if (fine) {
             for (int c = 0; c < GN / 32; c++) {
@@ -470,7 +478,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_fold);
         // the epilogue: E + floor(D2 / 256)
-        const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_done, 0));
+        const bool landed = __all_sync(0xffffffffu, mbar_wait(bar_done, 0, spin));
         fine = __all_sync(0xffffffffu, landed && !*(volatile int *)&s_fail);
         tc_fence_after();
         if (fine) {
@@ -497,9 +505,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) tc_gemm_kernel(const __grid_c
     __syncthreads();
     if (s_fail && threadIdx.x == 0) {
         atomicAdd(err, 1ull);
-        // let this CTA's copies still in flight land before its shared memory is released
+        // let this CTA's copies still in flight land before its shared memory is
+        // released, and the MMAs (the commit on bar_done follows them) finish
+        // before TMEM is freed: full-length waits, whatever `spin` was
         for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; it++)
             (void)mbar_wait(smem_u32(&bars[it % STAGES]), (it / STAGES) & 1);
+        (void)mbar_wait(bar_done, 0);
     }
     tc_fence_before();
     __syncthreads();
@@ -967,6 +978,11 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
     return L;
 }
 
+// The calling thread's wait settings for the GEMM launches it makes
+// (sfb_wide_wait_limit): 0 polls = kSpinLimit, and the stall test off.
+thread_local unsigned t_wait_polls = 0;
+thread_local int t_wait_stall = 0;
+
 bool eligible(int bits, int mx, int64_t M, int64_t N, int64_t K) {
     return mx == SFB_MX_V492 && bits >= 9 && bits <= 16 && K >= 1 && K <= KMAX && M >= 1 && N >= 1 &&
            (double)M * (double)N * (double)K >= (double)(1 << 22) && up(M, TILE) <= (1 << 20) &&
@@ -1024,17 +1040,20 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         return set_error(SFB_EINVAL, "sfb_matmul_wide: workspace of %lld bytes is smaller than the %lld needed",
                          (long long)ws_bytes, (long long)L.total);
     if (counts == nullptr) return set_error(SFB_EINVAL, "sfb_matmul_wide: the tensor-core path needs counts");
-    static bool smem_set[64] = {};
+    // the kernels' shared-memory limits, set once per CUDA context (a device
+    // reset starts a new context, which needs them again)
+    static unsigned long long smem_ctx[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (!smem_set[dev]) {
+    const unsigned long long ctx = context_id();
+    if (ctx == 0 || smem_ctx[dev] != ctx) {
         if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(wide_rem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  REM_SMEM) != cudaSuccess)
             return check_launch("sfb_matmul_wide (attributes)");
-        smem_set[dev] = true;
+        smem_ctx[dev] = context_id();
     }
     uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);
     uint8_t *pa = base + L.off_pa, *pb = base + L.off_pb;
@@ -1089,7 +1108,8 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.counts = counts;
         in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
         tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), GEMM_THREADS, GEMM_SMEM, st>>>(
-            tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0]);
+            tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0], t_wait_polls ? t_wait_polls : kSpinLimit,
+            t_wait_stall);
         wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
         const int64_t fx = (N + 255) / 256;
         const dim3 fgrid((unsigned)fx, (unsigned)std::max<int64_t>(1, std::min<int64_t>(M, (int64_t)sm_count() * 8 / fx)));
@@ -1125,15 +1145,28 @@ static __device__ __align__(256) unsigned char g_wide_scratch[kNoAllocScratchByt
 
 }  // namespace
 
+extern "C" int sfb_wide_wait_limit(unsigned polls, int stall) {
+    sfb::t_wait_polls = polls;
+    sfb::t_wait_stall = stall != 0;
+    return SFB_OK;
+}
+
 extern "C" int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const int16_t *B,
                                        const int8_t *shift_arr, int shift, int16_t *out, uint8_t *flags,
                                        int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                                        int64_t stride_a, int64_t stride_b, int64_t stride_out, int64_t shift_sb,
                                        int64_t shift_sm, int64_t shift_sn, sfb_counts *counts, sfb_stream stream) {
     using namespace sfb;
-    // the array's device address, looked up by the first call on each device with
-    // that device current (so that first call belongs before any stream capture)
-    static void *scratch[64] = {};
+    // The array's device address, looked up by the first call on each device
+    // with that device current (so that first call belongs before any stream
+    // capture), and again whenever the device's CUDA context has changed: a
+    // device reset reloads the library's module and the array may then sit at
+    // another address.
+    struct Slot {
+        unsigned long long ctx;
+        void *ptr;
+    };
+    static Slot scratch[64] = {};
     static std::mutex lock;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
@@ -1141,14 +1174,18 @@ extern "C" int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const
     void *ptr = nullptr;
     {
         std::lock_guard<std::mutex> g(lock);
-        if (scratch[dev] == nullptr) {
-            const cudaError_t e = cudaGetSymbolAddress(&scratch[dev], g_wide_scratch);
+        Slot &slot = scratch[dev];
+        const unsigned long long ctx = context_id();
+        if (slot.ptr == nullptr || ctx == 0 || slot.ctx != ctx) {
+            slot.ptr = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&slot.ptr, g_wide_scratch);
             if (e != cudaSuccess) {
-                scratch[dev] = nullptr;
+                slot.ptr = nullptr;
                 return set_error(SFB_ECUDA, "sfb_matmul_wide_noalloc: scratch lookup failed: %s", cudaGetErrorString(e));
             }
+            slot.ctx = context_id();     // the lookup makes the device's context current if none was
         }
-        ptr = scratch[dev];
+        ptr = slot.ptr;
     }
     const int64_t need = sfb_matmul_wide_workspace(bits, mx, batch, M, N, K);
     if (need < 0) return (int)need;

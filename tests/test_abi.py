@@ -96,7 +96,7 @@ def _ctype_of(c_type):
     t = c_type.replace("const", "").strip()
     if "*" in t or t == "sfb_stream":
         return ctypes.c_void_p
-    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "double": ctypes.c_double,
+    return {"int": ctypes.c_int, "unsigned": ctypes.c_uint, "int64_t": ctypes.c_int64, "double": ctypes.c_double,
             "const char": ctypes.c_char_p}.get(t)
 
 

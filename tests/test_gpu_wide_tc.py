@@ -97,3 +97,27 @@ def test_batched(gpu):
     got, _, _ = _run(gpu, 16, A, B, -1)
     want, _ = _want(16, A.reshape(-1, 300), B, -1)
     np.testing.assert_array_equal(got.reshape(-1, 140), want)
+
+
+def test_a_wait_that_runs_out_is_reported_and_the_next_call_is_exact(gpu):
+    """Failure detection without a fault: with a 64-poll limit and the MMA
+    thread first waiting on a barrier nothing arrives on, every CTA of the
+    GEMM gives up, lets its copies in flight land, frees its tensor memory and
+    counts the failure; the host raises SFDeviceError from that count, and the
+    next call on the same context (default limit) is bit-exact."""
+    from superfloat.python_b200._errors import SFDeviceError
+    lib = _lib.load()
+    rng = np.random.default_rng(21)
+    A = rng.integers(-3000, 3001, (300, 1000))
+    B = rng.integers(-32767, 32768, (1000, 260))
+    try:
+        assert lib.sfb_wide_wait_limit(64, 1) == _lib.SFB_OK
+        with pytest.raises(SFDeviceError, match="gave up waiting"):
+            _run(gpu, 16, A, B, -1)
+    finally:
+        lib.sfb_wide_wait_limit(0, 0)
+    got, cnt, fl = _run(gpu, 16, A, B, -1)
+    want, ev = _want(16, A, B, -1)
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal((fl & 1) != 0, ev["overflow"])
+    assert int(cnt[5]) == 0

@@ -37,11 +37,13 @@ def test_noalloc_equals_the_workspace_entry_point_twice(gpu):
     lib = _lib.load()
     dev = torch.device("cuda", 0)
     rng = np.random.default_rng(2024)
-    M = N = K = 1024
-    need = lib.sfb_matmul_wide_workspace(16, 0, 1, M, N, K)
-    assert 0 < need <= 64 << 20                       # the tensor-core path, within the fixed scratch
-    ws = torch.empty(need, dtype=torch.uint8, device=dev)
-    for call in range(2):                             # two calls in a row: stale scratch must not leak in
+    # two calls in a row, the second at a smaller, ragged shape: its padding
+    # rows / columns and its scratch layout differ from the first call's, so
+    # whatever the first call left in the array must not leak into it
+    for call, (M, N, K) in enumerate(((1536, 1536, 1536), (1000, 1100, 900))):
+        need = lib.sfb_matmul_wide_workspace(16, 0, 1, M, N, K)
+        assert 0 < need <= 64 << 20                   # the tensor-core path, within the fixed scratch
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)      # a fresh workspace for the reference call
         A = torch.from_numpy(rng.integers(-3000 * (call + 1), 3000 * (call + 1) + 1, (M, K))).to(torch.int16).to(dev)
         B = torch.from_numpy(rng.integers(-32767, 32768, (K, N))).to(torch.int16).to(dev)
         shift = -call
