@@ -58,20 +58,69 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_from_profiles(kernel_key):
-    """DRAM bytes per launch recorded by ncu (profiles/ncu_traffic.txt:
-    '<key> <bytes per launch>' lines), or None."""
-    p = os.path.join(HERE, "profiles", "ncu_traffic.txt")
+def _profile_value(fname, key, col=1):
+    """A number recorded from an ncu capture in profiles/<fname> (lines of
+    '<key> <value> ...'), or None."""
+    p = os.path.join(HERE, "profiles", fname)
     if not os.path.exists(p):
         return None
     for line in open(p):
         parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel_key:
+        if len(parts) > col and parts[0] == key:
             try:
-                return float(parts[1])
+                return float(parts[col])
             except ValueError:
                 return None
     return None
+
+
+def traffic_from_profiles(kernel_key):
+    """DRAM bytes per launch recorded by ncu (profiles/ncu_traffic.txt)."""
+    return _profile_value("ncu_traffic.txt", kernel_key)
+
+
+def insts_from_profiles(kernel_key):
+    """Warp instructions per launch recorded by ncu (profiles/ncu_inst.txt,
+    smsp__inst_executed.sum of one launch of the same workload)."""
+    return _profile_value("ncu_inst.txt", kernel_key)
+
+
+def issue_roofline(torch, kernel, keys, ms, clocks):
+    """Roofline of an integer kernel that is bound by instruction issue: the
+    warp instructions its launches execute (ncu, profiles/ncu_inst.txt) over
+    their CUDA-event time, against one warp instruction per scheduler per
+    clock (SMs x 4 x the highest SM clock seen)."""
+    insts = [insts_from_profiles(k) for k in keys]
+    if any(v is None for v in insts):
+        return None
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    mhz = (clocks or {}).get("sm_max_mhz") or 1965.0
+    peak = sms * 4 * mhz * 1e6 / 1e12
+    achieved = sum(insts) / (ms / 1e3) / 1e12
+    return {"bound": "int", "achieved": achieved, "peak": peak, "unit": "T warp-instructions/s",
+            "frac": achieved / peak, "traffic": None, "kernel": kernel,
+            "peak_kind": f"{sms} SMs x 4 schedulers x 1 warp-instruction per clock at {mhz:.0f} MHz",
+            "warp_instructions": sum(insts), "source": "ncu smsp__inst_executed.sum, profiles/ncu_inst.txt"}
+
+
+def int8_peak(torch, n=8192, reps=10):
+    """Dense int8 GEMM rate of this GPU in this run: torch._int_mm (cuBLASLt)
+    on n^3, CUDA events, int8 TOPS (2 n^3 / t)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+    b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        torch._int_mm(a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del a, b
+    return 2 * n ** 3 / (ms / 1e3) / 1e12
 
 
 class ClockSampler:
@@ -123,21 +172,52 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_sample(n_sample):
-    """The oracle's NumPy ops (the reference's own NumPy formulation) on
-    n_sample elements of the same workload, single-threaded."""
+def reference_site():
+    """The directory holding the reference package ``sf`` (an offline install
+    under baseline/_ref, or SF_REFERENCE_SITE), or None."""
+    for d in (os.environ.get("SF_REFERENCE_SITE"), os.path.join(HERE, "baseline", "_ref")):
+        if d and os.path.isfile(os.path.join(d, "sf", "__init__.py")):
+            return d
+    return None
+
+
+def _import_reference():
+    site = reference_site()
+    if site is None:
+        return None
+    if site not in sys.path:
+        sys.path.insert(0, site)
+    import tempfile
+    os.environ.setdefault("SF_CACHE_DIR", os.path.join(tempfile.gettempdir(), "sf_bench_cache"))
+    import sf
+    return sf
+
+
+def cpu_ops():
+    """(fn(op, *codes), kind): the reference's own sf._vectorized ops
+    (src/sf/_vectorized.py:94-131) when the reference is installed, else the
+    oracle's NumPy restatement of them."""
+    sf = _import_reference()
+    if sf is not None:
+        from sf import _vectorized as vec
+        from sf._format import FORMATS
+        f16 = FORMATS[16]
+        return (lambda op, *xs: getattr(vec, op)(f16, *xs)), "reference"
     from oracle import sfref
+    return (lambda op, *xs: sfref.ew(op, 16, *xs)), "port"
+
+
+def cpu_sample(n_sample):
+    """The five ops on n_sample elements of the same workload, single-threaded
+    (the reference's own code when installed, else the oracle port)."""
     from superfloat.python_b200 import workloads
+    fn, _ = cpu_ops()
     x, y, z, d = workloads.elementwise(n_sample, 0)
     args = {"add": (x, y), "sub": (x, y), "mul": (x, y), "fma": (x, y, z), "div": (x, d)}
     t0 = time.perf_counter()
     for op in OPS:
-        sfref.ew(op, 16, *args[op])
+        fn(op, *args[op])
     return time.perf_counter() - t0
-
-
-def _cpu_pool_worker(n):
-    return cpu_sample(n)
 
 
 def host_cores() -> int:
@@ -156,12 +236,123 @@ def host_cores() -> int:
     return max(1, n)
 
 
+def cpu_matmul_baselines():
+    """CPU baselines of the matmul, GPT-2 and sweep configs, each on a bounded
+    sample of its workload, timed with the reference's own code when it is
+    installed (else the oracle's restatement, or the reference's own C
+    accumulator built into oracle/_ref).  Runs in a child process
+    (``bench.py --cpu-baselines``): the reference and this package both
+    register a TorchDynamo backend named ``superfloat``."""
+    from superfloat.python_b200 import workloads
+    sf = _import_reference()
+    res = {}
+    # chain 512^3: src/sf/_linalg.py:61-81, one core (NumPy's K-loop)
+    A, B = workloads.chain_square(512, 0)
+    if sf is not None:
+        from sf import _linalg
+        from sf._format import FORMATS
+        f16 = FORMATS[16]
+        t0 = time.perf_counter()
+        _linalg.matmul_codes(f16, A, B)
+        kind, what = "reference", "sf._linalg.matmul_codes"
+    else:
+        from oracle import sfref
+        t0 = time.perf_counter()
+        sfref.matmul_chain(16, A, B)
+        kind, what = "port", "the oracle's NumPy restatement of _linalg.matmul_codes"
+    dt = time.perf_counter() - t0
+    res["chain_512"] = {"value": 2 * 512 ** 3 / dt / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)", "cores": 1,
+                        "kind": kind, "sample": f"{what} on the whole 512^3 workload, {dt:.2f} s"}
+    # wide 8192^3: a 64-row slice (rows are independent), src/sf/_linalg.py:330-348 with
+    # the compiled _fastmx loop (src/sf/_fastmx.py:176-198) on its own thread count
+    rows = 64
+    A, B = workloads.wide_square(8192, 8192, 8192, 0)
+    A = np.ascontiguousarray(A[:rows])
+    if sf is not None:
+        from sf import _fastmx, _linalg
+        threads = _fastmx._threads() if _fastmx.available() else 1
+        t0 = time.perf_counter()
+        _linalg.matmul_wide_codes(f16, A, B, 0)
+        kind, what = "reference", f"sf._linalg.matmul_wide_codes (compiled _fastmx loop, {threads} threads)"
+    else:
+        from oracle import native
+        threads = min(8, host_cores())
+        t0 = time.perf_counter()
+        if native.ref_available():
+            native.ref_wide_acc(16, A, B, threads=threads)
+            kind, what = "reference", f"the reference's own C accumulator (oracle/_ref), {threads} threads"
+        else:
+            native.wide_acc(16, A, B)
+            kind, what = "port", "the oracle's C accumulator"
+    dt = time.perf_counter() - t0
+    res["wide_8192"] = {"value": 2 * rows * 8192 * 8192 / dt / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)",
+                        "cores": threads, "kind": kind,
+                        "sample": f"{what}, rows 0..{rows - 1} of 8192 ({dt:.1f} s), extrapolated by rows"}
+    del A, B
+    # the converted GPT-2-small: the reference's own sft.convert forward on 1 x 16 tokens
+    if sf is not None:
+        import warnings
+        import torch
+        import sf.torch as sft
+        from transformers import GPT2Config, GPT2LMHeadModel
+        torch.manual_seed(0)
+        cfg = GPT2Config(n_layer=12, n_embd=768, n_head=12, n_inner=3072, vocab_size=50257, n_positions=1024)
+        model = sft.convert(GPT2LMHeadModel(cfg).eval(), dtype="sf16")
+        tokens = 16
+        ids = torch.randint(0, 50257, (1, tokens), generator=torch.Generator().manual_seed(0))
+        torch.set_num_threads(1)
+        with torch.no_grad(), warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            t0 = time.perf_counter()
+            model(ids)
+            dt = time.perf_counter() - t0
+        res["gpt2_small_convert"] = {
+            "value": tokens / dt, "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"the reference's sft.convert(sf16) GPT-2-small forward on 1 x {tokens} tokens ({dt:.1f} s; "
+                      "host path, one core), taken as linear in tokens (its cost per token at 64 tokens is about 0.8x "
+                      "that at 8)"}
+    else:
+        res["gpt2_small_convert"] = None
+    # the exhaustive sweep: a few a-rows through the four ops
+    fn, kind = cpu_ops()
+    M = 32767
+    arows = np.arange(-3, 3)
+    b = np.arange(-M, M + 1)
+    ka, kb = np.repeat(arows, b.size), np.tile(b, arows.size)
+    t0 = time.perf_counter()
+    for op in ("add", "sub", "mul", "div"):
+        fn(op, ka, kb)
+    dt = time.perf_counter() - t0
+    res["sweep"] = {"value": 4 * ka.size / dt / 1e9, "unit": "Gpairs/s", "cores": 1, "kind": kind,
+                    "sample": f"{arows.size} a-rows x {b.size} b, add/sub/mul/div ({dt:.2f} s)"}
+    return res
+
+
+def run_cpu_baselines_child():
+    """``bench.py --cpu-baselines`` in a child process; None when it fails."""
+    try:
+        p = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-baselines"], capture_output=True,
+                           text=True, timeout=600, cwd=HERE)
+        return json.loads(p.stdout.strip().splitlines()[-1]) if p.returncode == 0 else None
+    except (subprocess.TimeoutExpired, ValueError, IndexError):
+        return None
+
+
+def elementwise_config(n, world):
+    """The ``config`` of the headline line; the reference arm prints the same dict."""
+    return {"workload": "sf16 elementwise add/sub/mul/fma/div with exact status counts, "
+                        f"{n} elements per op per rank (seeded 2^26 generator)",
+            "elements_per_op_per_rank": n, "l2": "inputs larger than L2 (3 x 128 MiB per op)",
+            "parallelism": f"element-range shards x{world}, status all-reduce"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     import multiprocessing as mp
     cores = host_cores()
     n_sample = 1 << 22                             # per process per step
+    _, kind = cpu_ops()
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         for _ in range(args.warmup):
@@ -174,14 +365,16 @@ def run_reference(args, rank, world):
     elems = len(OPS) * n_sample * cores
     ms = 1e3 * statistics.median(times)
     v = elems / (ms / 1e3) / 1e9
+    what = ("the reference's own sf._vectorized ops" if kind == "reference"
+            else "the oracle's NumPy restatement of sf._vectorized")
     line = {"metric": METRIC, "value": v, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": "sf16 elementwise add/sub/mul/fma/div with status, seeded (2^26 generator)",
-                       "sample_elements_per_op": n_sample * cores, "processes": cores},
+            "config": elementwise_config(args.elements, world),
             "impl": "reference",
-            "cpu_baseline": {"value": v, "unit": "Gelem/s", "cores": cores, "kind": "port",
-                             "sample": f"{n_sample} elements x 5 ops per process, {cores} spawn processes"},
+            "cpu_baseline": {"value": v, "unit": "Gelem/s", "cores": cores, "kind": kind,
+                             "sample": f"{what}: {n_sample} elements x 5 ops per process and step, {cores} spawn "
+                                       f"processes (a bounded sample of the {args.elements}-element workload)"},
             "e2e": {"value": v, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -204,6 +397,8 @@ def main():
     ap.add_argument("--chain-only", action="store_true",
                     help="time only the proven chain kernel on the GPT-2-small projection shapes")
     ap.add_argument("--sweep-only", action="store_true", help="time only the exhaustive sf16 pair sweep")
+    ap.add_argument("--cpu-baselines", action="store_true",
+                    help="print the CPU baselines of the matmul / GPT-2 / sweep configs (a child process)")
     ap.add_argument("--gpt2-only", type=int, default=0, metavar="TOKENS",
                     help="time only the converted GPT-2-small forward on 8 x TOKENS ids")
     args = ap.parse_args()
@@ -211,6 +406,9 @@ def main():
     rank, world, local = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.cpu_baselines:
+        print(json.dumps(cpu_matmul_baselines()), flush=True)
+        return 0
 
     import torch
     import torch.distributed as dist
@@ -322,10 +520,7 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int16", "data": "synthetic",
-            "config": {"workload": "sf16 elementwise add/sub/mul/fma/div with exact status counts, "
-                                   f"{n} elements per op per rank (seeded 2^26 generator)",
-                       "elements_per_op_per_rank": n, "l2": "inputs larger than L2 (3 x 128 MiB per op)",
-                       "parallelism": f"element-range shards x{world}, status all-reduce"},
+            "config": elementwise_config(n, world),
             "gpu_launches": len(OPS) * args.steps, "roofline": roofline,
             "status_counts_last_step": {op: {"overflow": int(cnt[i][0]), "underflow": int(cnt[i][1]),
                                              "divide": int(cnt[i][2])} for i, op in enumerate(OPS)}}
@@ -381,13 +576,23 @@ def main():
         reps = 3
         ts = [cpu_sample(n_sample) for _ in range(reps)]
         v = len(OPS) * n_sample / statistics.median(ts) / 1e9
-        line["cpu_baseline"] = {"value": v, "unit": "Gelem/s", "cores": 1, "kind": "port",
-                                "sample": f"{n_sample} elements x 5 ops, NumPy, median of {reps}"}
+        _, kind = cpu_ops()
+        what = "the reference's own sf._vectorized" if kind == "reference" else "the oracle's NumPy restatement"
+        line["cpu_baseline"] = {"value": v, "unit": "Gelem/s", "cores": 1, "kind": kind,
+                                "sample": f"{what}: {n_sample} elements x 5 ops, one core, median of {reps}"}
+
+    # CPU baselines of the other configs (rank 0, N = 1), in a child process
+    cpu_mm = run_cpu_baselines_child() if rank == 0 and world == 1 and not args.no_cpu else None
 
     # the exhaustive pair sweep beside it, row-sharded over all ranks: not part of `value`
     if not args.no_sweep:
-        sw = bench_sweep(torch, dist, rank, world, cpu=(rank == 0 and world == 1 and not args.no_cpu))
+        sw = bench_sweep(torch, dist, rank, world)
         if rank == 0:
+            if cpu_mm:
+                sw["cpu_baseline"] = cpu_mm.get("sweep")
+            rl = issue_roofline(torch, "sweep_kernel<op, 16> (add, sub, mul, div)",
+                                [f"sweep_{op}_16" for op in ("add", "sub", "mul", "div")], sw["ms"] * world, clocks)
+            sw["roofline"] = rl                # per GPU: 1 / world of the instructions in sw["ms"]
             line["sweep"] = sw
 
     # the matmuls beside it: not part of `value`.  The wide one row-sharded over all
@@ -398,7 +603,12 @@ def main():
             mm["chain_gpt2_projections"] = bench_chain_shapes(torch)
             mm["gpt2_small_convert"] = bench_gpt2(torch)
             mm["gpt2_small_convert_wide"] = bench_gpt2(torch, accumulate="wide")
+        if rank == 0 and cpu_mm:
+            for key in ("chain_512", "wide_8192", "gpt2_small_convert"):
+                if key in mm:
+                    mm[key]["cpu_baseline"] = cpu_mm.get(key)
         if rank == 0:
+            add_matmul_rooflines(torch, mm, clocks, world)
             line["matmul"] = mm
 
     if world > 1:
@@ -407,6 +617,41 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
+
+
+GPT2_LAYERS = ((768, 2304), (768, 768), (768, 3072), (3072, 768))       # (K, N) of one block's four layers
+
+
+def add_matmul_rooflines(torch, mm, clocks, world):
+    """Roofline objects for the matmul entries: the wide call against the
+    limb-adjusted int8 rate (11 int8 passes per sf16 product, int8 peak
+    measured here with torch._int_mm), the chain kernels against the issue
+    rate (their ncu instruction counts)."""
+    for key, e in mm.items():
+        if key.startswith("wide_"):
+            n = int(key.split("_")[1])
+            peak = int8_peak(torch)
+            achieved = 11 * 2 * (n // world) * n * n / (e["ms"] / 1e3) / 1e12
+            e["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "int8 TOPS",
+                             "frac": achieved / peak, "traffic": None,
+                             "kernel": "the wide call (prep x2, tc_gemm, wide_rem, finish)",
+                             "peak_kind": "measured in this run: torch._int_mm (cuBLASLt) int8 8192^3",
+                             "note": "11 tcgen05 int8 passes per sf16 product; frac = sf16 rate / (int8 rate / 11)"}
+    if "chain_512" in mm:
+        mm["chain_512"]["roofline"] = issue_roofline(torch, "chain2_kernel (general mode, 512^3)", ["chain2_512"],
+                                                     mm["chain_512"]["ms"], clocks)
+    for shape, e in mm.get("chain_gpt2_projections", {}).items():
+        if isinstance(e, dict):
+            e["roofline"] = issue_roofline(torch, f"chain_pk_kernel ({shape})", [f"chain_pk_{shape}"], e["ms"],
+                                           clocks)
+    g = mm.get("gpt2_small_convert")
+    if g:
+        keys = [f"chain_pk_4096x{k}x{n}" for k, n in GPT2_LAYERS] * 12 + ["chain_pk_4096x768x50257"]
+        rl = issue_roofline(torch, "chain_pk_kernel, the 49 SF layers of one forward", keys, g["ms_per_forward"],
+                            clocks)
+        if rl:
+            rl["note"] = "the chain kernels' instructions over the whole forward's time (float parts included)"
+        g["roofline"] = rl
 
 
 def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
@@ -471,7 +716,7 @@ def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
     return res
 
 
-def bench_sweep(torch, dist, rank, world, bits=16, cpu=False):
+def bench_sweep(torch, dist, rank, world, bits=16):
     """Every sf16 code pair through add, sub, mul and div (4 x 65535^2 =
     1.7e10 pairs), the a-rows split evenly over the ranks; each row folds
     into two 64-bit digests on the device.  Device time is the max over
@@ -511,17 +756,6 @@ def bench_sweep(torch, dist, rank, world, bits=16, cpu=False):
             res[op] = {"sha256": sha[:16], "overflow": int(c[0]), "underflow": int(c[1]), "divide": int(c[2])}
     if rank == 0:
         res["digests_match_reference"] = bool(match) if ref is not None else None
-    if cpu:
-        from oracle import sfref
-        rows = np.arange(-3, 3)
-        b = np.arange(-M, M + 1)
-        ka, kb = np.repeat(rows, n), np.tile(b, rows.size)
-        t0 = time.perf_counter()
-        for op in sweep.OPS:
-            sfref.ew(op, bits, ka, kb)
-        dt = time.perf_counter() - t0
-        res["cpu_baseline"] = {"value": len(sweep.OPS) * ka.size / dt / 1e9, "unit": "Gpairs/s", "cores": 1,
-                               "kind": "port", "sample": f"{rows.size} a-rows x {n} b, 4 ops, NumPy oracle"}
     return res
 
 
@@ -568,7 +802,10 @@ def bench_chain_shapes(torch, reps=10):
 def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     """sft.convert(dtype=sf16) GPT-2-small (12 layers, d_model 768, 12 heads,
     FFN 3072, vocab 50257; random init, seed 0) forward on batch x seq token
-    ids, on the GPU; 49 SF layers (chain accumulation, headroom "bound")."""
+    ids, on the GPU, through torch.compile(backend="superfloat") (the timed
+    forward; the first compiled call, which traces, is not timed); 49 SF
+    layers (chain accumulation, headroom "bound").  The eager forward is
+    timed beside it, and the compiled logits must equal the eager ones."""
     import warnings
     from transformers import GPT2Config, GPT2LMHeadModel
     import superfloat.python_b200.torch as sft
@@ -577,24 +814,38 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     kw = {"accumulate": "wide", "attention": False} if accumulate == "wide" else {}
     model = sft.convert(GPT2LMHeadModel(cfg).eval(), dtype="sf16", **kw).cuda()
     ids = torch.randint(0, 50257, (batch, seq), generator=torch.Generator().manual_seed(0)).cuda()
-    with torch.no_grad(), warnings.catch_warnings():
-        warnings.simplefilter("ignore")
-        model(ids)                                        # prepares the weights (cached per weight)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            model(ids)
+            out = fn(ids)
         e1.record()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+        return e0.elapsed_time(e1) / reps, out
+
+    torch._dynamo.reset()
+    with torch.no_grad(), warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        eager_logits = model(ids).logits                  # prepares the weights (cached per weight)
+        eager_ms, _ = timed(model)
+        n_rep = len(sft.compile_reports())
+        compiled = torch.compile(model, backend="superfloat")
+        compiled(ids)                                     # traces and compiles
+        ms, out = timed(compiled)
+    reps_new = sft.compile_reports()[n_rep:]
+    same = bool(torch.equal(out.logits, eager_logits))
+    torch._dynamo.reset()
     R = batch * seq
     products = R * (768 * 2304 + 768 * 768 + 768 * 3072 + 3072 * 768) * 12 + R * 768 * 50257
     st = sft.last_status(model)
     return {"ms_per_forward": ms, "tokens_per_s": R / (ms / 1e3), "sf_layers": len(st),
             "sf16_TOPS": 2 * products / (ms / 1e3) / 1e12, "saturated": sum(v.saturated or 0 for v in st.values()),
-            "workload": f"GPT-2-small sft.convert(sf16, accumulate={accumulate!r}) forward, {batch} x {seq} tokens, "
-                        "float parts on the GPU"}
+            "eager_ms_per_forward": eager_ms, "compiled_equals_eager": same,
+            "sf_ops_on_device": sum(len(r.on_device) for r in reps_new), "graphs": len(reps_new),
+            "workload": f"GPT-2-small sft.convert(sf16, accumulate={accumulate!r}) forward through "
+                        f"torch.compile(backend='superfloat'), {batch} x {seq} tokens, float parts on the GPU"}
 
 
 if __name__ == "__main__":

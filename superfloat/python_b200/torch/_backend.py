@@ -17,8 +17,10 @@ from torch._dynamo import register_backend
 
 from ._ops import SF_OP_ARGS, SF_OPS, linear_impl, linear_wide_impl, matmul_impl, matmul_wide_impl
 
-_UNCONVERTED = {"linear", "matmul", "mm", "bmm", "conv2d", "conv1d", "conv3d", "addmm", "baddbmm", "einsum",
-                "__matmul__", "scaled_dot_product_attention"}
+# float linear algebra that convert() did not turn into SF ops: reported as
+# "not converted" (it runs in float, off the device)
+_FLOAT_LINALG = frozenset({"linear", "matmul", "mm", "bmm", "conv1d", "conv2d", "conv3d", "addmm", "baddbmm",
+                           "einsum", "__matmul__", "scaled_dot_product_attention"})
 
 
 @dataclass
@@ -48,102 +50,107 @@ class GraphReport:
         return "\n".join(lines)
 
 
-_lock = threading.Lock()
-_reports: list = []
+class _ReportLog:
+    """Every graph report this process has produced, oldest first."""
+
+    def __init__(self):
+        self._items: list = []
+        self._guard = threading.Lock()
+
+    def add(self, rep: GraphReport) -> None:
+        with self._guard:
+            self._items.append(rep)
+
+    def all(self) -> list:
+        with self._guard:
+            return list(self._items)
+
+
+_LOG = _ReportLog()
 
 
 def compile_reports() -> list:
-    with _lock:
-        return list(_reports)
+    """The reports of every graph compiled with backend='superfloat'."""
+    return _LOG.all()
 
 
 def compile_report() -> GraphReport:
-    with _lock:
-        if not _reports:
-            raise ValueError("no graph has been compiled with backend='superfloat' yet")
-        return _reports[-1]
+    """The report of the graph compiled last."""
+    reps = _LOG.all()
+    if not reps:
+        raise ValueError("no graph has been compiled with backend='superfloat' yet")
+    return reps[-1]
 
 
-def _require_no_grad(*tensors):
-    if torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
+def _inference_only(tensors) -> None:
+    """The compiled SF ops have no backward: refuse inputs that need one."""
+    if not torch.is_grad_enabled():
+        return
+    if any(isinstance(t, torch.Tensor) and t.requires_grad for t in tensors):
         from .._errors import SFUnsupportedError
         raise SFUnsupportedError("the superfloat compile backend is inference-only; wrap the call in "
                                  "torch.no_grad(), or train with the eager layers from sft.convert")
 
 
-def _device_linear(device):
-    def run(x, weight, bias, bits, wscale, headroom, name):
-        _require_no_grad(x, weight, bias)
-        return linear_impl(x, weight, bias, bits, wscale, headroom, name)
-    run.__name__ = f"sf_linear_on_{device}"
-    return run
+# op -> (the function the node is retargeted to, how many leading tensor arguments it checks)
+_DEVICE_IMPLS = {"linear": (linear_impl, 3), "matmul": (matmul_impl, 2), "linear_wide": (linear_wide_impl, 3),
+                 "matmul_wide": (matmul_wide_impl, 2)}
 
 
-def _device_matmul(device):
-    def run(a, b, bits, headroom, name):
-        _require_no_grad(a, b)
-        return matmul_impl(a, b, bits, headroom, name)
-    run.__name__ = f"sf_matmul_on_{device}"
-    return run
+def _on_device(op: str, device_name: str):
+    """The node target for ``op`` on the device: the eager op's own
+    implementation (so compiled == eager, bit for bit) behind the
+    inference-only check."""
+    impl, n_tensors = _DEVICE_IMPLS[op]
+
+    def call(*args):
+        _inference_only(args[:n_tensors])
+        return impl(*args)
+    call.__name__ = f"sf_{op}_on_{device_name}"
+    return call
 
 
-def _device_linear_wide(device):
-    def run(x, weight, bias, bits, shift, name):
-        _require_no_grad(x, weight, bias)
-        return linear_wide_impl(x, weight, bias, bits, shift, name)
-    run.__name__ = f"sf_linear_wide_on_{device}"
-    return run
+def _node_arg(node, position: int, keyword: str):
+    """An argument of an FX node, given by position or by keyword."""
+    return node.args[position] if position < len(node.args) else node.kwargs.get(keyword)
 
 
-def _device_matmul_wide(device):
-    def run(a, b, bits, shift, name):
-        _require_no_grad(a, b)
-        return matmul_wide_impl(a, b, bits, shift, name)
-    run.__name__ = f"sf_matmul_wide_on_{device}"
-    return run
-
-
-def _arg(node, i, key):
-    return node.args[i] if len(node.args) > i else node.kwargs.get(key)
-
-
-def _target_name(node):
-    t = node.target
-    return t if isinstance(t, str) else (getattr(t, "__name__", None) or str(t))
+def _describe(gm, node) -> tuple[str, str]:
+    """(short op name for the float-linear-algebra test, label for the report)."""
+    if node.op == "call_module":
+        mod = gm.get_submodule(node.target)
+        return type(mod).__name__.lower(), f"{node.target} ({type(mod).__name__})"
+    target = node.target
+    label = target if isinstance(target, str) else (getattr(target, "__name__", None) or str(target))
+    return label.split(".")[-1], label
 
 
 @register_backend
 def superfloat(gm: torch.fx.GraphModule, example_inputs, **kwargs):
+    """Retarget every SF op node of ``gm`` that the default device runs at
+    its width; report what runs where."""
     from .. import _config
     from .._device import get_device
     dev = get_device(_config.get("default_device"))
     report = GraphReport()
-    impl = {"linear": _device_linear(dev.name), "matmul": _device_matmul(dev.name),
-            "linear_wide": _device_linear_wide(dev.name), "matmul_wide": _device_matmul_wide(dev.name)}
+    targets = {}
     for node in gm.graph.nodes:
         if node.op not in ("call_function", "call_method", "call_module"):
             continue
-        name = _target_name(node)
-        if node.op == "call_function" and str(node.target) in SF_OPS:
-            op = SF_OPS[str(node.target)]
-            ib, iname = SF_OP_ARGS[op]
-            bits, layer = _arg(node, ib, "bits"), _arg(node, iname, "name")
-            if bits in dev.widths_for(op):
-                node.target = impl[op]
-                report.on_device.append((node.name, op, layer, dev.name))
-            else:
+        op = SF_OPS.get(str(node.target)) if node.op == "call_function" else None
+        if op is not None:
+            bits_at, name_at = SF_OP_ARGS[op]
+            bits, layer = _node_arg(node, bits_at, "bits"), _node_arg(node, name_at, "name")
+            if bits not in dev.widths_for(op):
                 report.host_emulated.append((node.name, op, layer, f"sf{bits} is not supported on {dev.name}"))
+                continue
+            if op not in targets:
+                targets[op] = _on_device(op, dev.name)
+            node.target = targets[op]
+            report.on_device.append((node.name, op, layer, dev.name))
             continue
-        short = name.split(".")[-1]
-        if node.op == "call_module":
-            sub = gm.get_submodule(node.target)
-            short = type(sub).__name__.lower()
-            name = f"{node.target} ({type(sub).__name__})"
-        if short in _UNCONVERTED:
-            report.unconverted.append((node.name, name))
-        else:
-            report.cpu.append((node.name, name))
+        short, label = _describe(gm, node)
+        (report.unconverted if short in _FLOAT_LINALG else report.cpu).append((node.name, label))
     gm.recompile()
-    with _lock:
-        _reports.append(report)
+    _LOG.add(report)
     return gm.forward

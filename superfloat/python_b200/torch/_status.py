@@ -59,65 +59,104 @@ class SFLayerStatus:
                 f"underflow={self.underflow}, headroom_bits={self.headroom_bits:.2f})")
 
 
-_lock = threading.Lock()
-_last: dict = {}
-_captures = contextvars.ContextVar("sfb200_status_captures", default=())
+class _Ledger:
+    """The newest status of every SF layer, by name (all threads), plus the
+    collectors that the calling context has open.  A context's collectors
+    are a chain of frames held in a context variable: a frame is (its dict,
+    the frame it was opened inside), so nested and concurrent captures each
+    see exactly the layers run inside them."""
+
+    def __init__(self):
+        self._newest: dict = {}
+        self._guard = threading.Lock()
+        self._frames = contextvars.ContextVar("sfb200_layer_status_frames", default=None)
+
+    def post(self, st: SFLayerStatus) -> None:
+        with self._guard:
+            self._newest[st.name] = st
+        frame = self._frames.get()
+        while frame is not None:
+            sink, frame = frame
+            sink[st.name] = st
+
+    def open(self, sink: dict):
+        return self._frames.set((sink, self._frames.get()))
+
+    def close(self, token) -> None:
+        self._frames.reset(token)
+
+    def snapshot(self) -> dict:
+        with self._guard:
+            return dict(self._newest)
+
+    def clear(self) -> None:
+        with self._guard:
+            self._newest.clear()
+
+
+_LEDGER = _Ledger()
 
 
 def record(st: SFLayerStatus) -> None:
-    with _lock:
-        _last[st.name] = st
-    for sink in _captures.get():
-        sink[st.name] = st
+    """Publish one layer call's status (the custom ops call this)."""
+    _LEDGER.post(st)
 
 
 class capture_status:
     """Collect the statuses of the SF layers run inside this context (this
-    thread or task only); also a decorator (the dict is then ``fn.last``)."""
+    thread or task only): ``with capture_status() as st: ...`` fills the dict
+    ``st``.  Used as a decorator, each call of the function collects afresh
+    and the dict of the latest call is the function's ``last`` attribute."""
 
     def __init__(self):
-        self.statuses = {}
-        self._tokens = []
+        self.statuses: dict = {}
+        self._open: list = []
 
-    def __enter__(self):
-        self._tokens.append(_captures.set(_captures.get() + (self.statuses,)))
+    def __enter__(self) -> dict:
+        self._open.append(_LEDGER.open(self.statuses))
         return self.statuses
 
-    def __exit__(self, *exc):
-        _captures.reset(self._tokens.pop())
+    def __exit__(self, *exc) -> None:
+        _LEDGER.close(self._open.pop())
 
     def __call__(self, fn):
-        if inspect.iscoroutinefunction(fn):
-            @functools.wraps(fn)
-            async def awrap(*a, **k):
-                with capture_status() as st:
-                    out = await fn(*a, **k)
-                awrap.last = st
-                return out
-            awrap.last = {}
-            return awrap
+        def collect():
+            sink = {}
+            return sink, _LEDGER.open(sink)
 
-        @functools.wraps(fn)
-        def wrap(*a, **k):
-            with capture_status() as st:
-                out = fn(*a, **k)
-            wrap.last = st
-            return out
-        wrap.last = {}
-        return wrap
+        if inspect.iscoroutinefunction(fn):
+            async def runner(*args, **kwargs):
+                sink, token = collect()
+                try:
+                    out = await fn(*args, **kwargs)
+                finally:
+                    _LEDGER.close(token)
+                runner.last = sink                 # only a call that returned replaces it
+                return out
+        else:
+            def runner(*args, **kwargs):
+                sink, token = collect()
+                try:
+                    out = fn(*args, **kwargs)
+                finally:
+                    _LEDGER.close(token)
+                runner.last = sink
+                return out
+        functools.update_wrapper(runner, fn)
+        runner.last = {}
+        return runner
 
 
 def last_status(model=None) -> dict:
     """Status of the latest call of every SF layer, by layer name; with
-    ``model``, only its SF layers, in module order."""
-    with _lock:
-        snap = dict(_last)
+    ``model``, only that model's SF layers that have run, in module order."""
+    newest = _LEDGER.snapshot()
     if model is None:
-        return snap
-    names = [m.sf_name for m in model.modules() if hasattr(m, "sf_name")]
-    return {n: snap[n] for n in names if n in snap}
+        return newest
+    order = (m.sf_name for m in model.modules() if hasattr(m, "sf_name"))
+    return {name: newest[name] for name in order if name in newest}
 
 
 def reset_status() -> None:
-    with _lock:
-        _last.clear()
+    """Forget every recorded status (captures already open keep theirs)."""
+    _LEDGER.clear()
