@@ -843,7 +843,8 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     return {"ms_per_forward": ms, "tokens_per_s": R / (ms / 1e3), "sf_layers": len(st),
             "sf16_TOPS": 2 * products / (ms / 1e3) / 1e12, "saturated": sum(v.saturated or 0 for v in st.values()),
             "eager_ms_per_forward": eager_ms, "compiled_equals_eager": same,
-            "sf_ops_on_device": sum(len(r.on_device) for r in reps_new), "graphs": len(reps_new),
+            "sf_op_nodes_on_device": sum(len(r.on_device) for r in reps_new),
+            "sf_op_nodes_host_emulated": sum(len(r.host_emulated) for r in reps_new), "graphs": len(reps_new),
             "workload": f"GPT-2-small sft.convert(sf16, accumulate={accumulate!r}) forward through "
                         f"torch.compile(backend='superfloat'), {batch} x {seq} tokens, float parts on the GPU"}
 

@@ -114,6 +114,7 @@ class B200Device(Device):
         self.launches = 0
         self._lock = threading.Lock()
         self._ws = None
+        self._stager = None
 
     # --- device plumbing -------------------------------------------------------------------
     @property
@@ -313,6 +314,16 @@ class B200Device(Device):
             out_shape = np.broadcast_shapes(*(o.shape for o in ops))
         if int(np.prod(out_shape)) == 0:
             return np.zeros(out_shape, np.int64), {e: np.zeros(out_shape, bool) for e in OP_EVENTS[op]}
+        if (op not in ("matmul", "matmul_wide", "sum") and int(np.prod(out_shape)) >= STAGED_MIN_ELEMENTS
+                and all(o.shape == out_shape for o in ops)):
+            # large equal-shape elementwise calls: the pooled, chunked host pipeline
+            self._ready()
+            if self._stager is None:
+                from ._hostpath import PluginStager
+                self._stager = PluginStager(self)
+            codes, masks, _ = self._stager.run(op, fmt.bits, [np.ascontiguousarray(o) for o in ops],
+                                               OP_EVENTS[op], _EVENT_BIT, pow_n=int(kw.get("n", 0)))
+            return codes, masks
         xs = [self.upload(o) for o in ops]
         if op == "matmul_wide" and "shift" in kw and not isinstance(kw["shift"], (int, np.integer)):
             kw = dict(kw)

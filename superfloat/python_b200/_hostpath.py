@@ -100,24 +100,96 @@ class HostPipeline:
         return res
 
 
-def plugin_run(dev, pipe: HostPipeline, op, fmt, *operands, n_pow: int = 0):
-    """The ``Device.run`` contract (int64 codes in, int64 codes and boolean
-    masks out) for equal-shape operands, through the host pipeline: narrowing
-    and widening on the host with torch's threaded copies, the rest on the GPU."""
-    import torch
-    ops = [np.ascontiguousarray(o, dtype=np.int64) for o in operands]
-    shape = ops[0].shape
-    n = ops[0].size
-    xs = []
-    for o in ops:
-        t = torch.empty(n, dtype=torch.int16, pin_memory=True)
-        t.copy_(torch.from_numpy(o.reshape(-1)))
-        xs.append(t)
-    out = torch.empty(n, dtype=torch.int16, pin_memory=True)
-    fl = torch.empty(n, dtype=torch.uint8, pin_memory=True)
-    counts = pipe.run(op, fmt, *xs, out=out, flags_out=fl, pow_n=n_pow)
-    codes = torch.empty(n, dtype=torch.int64)
-    codes.copy_(out)
-    from ._device import OP_EVENTS, _EVENT_BIT
-    masks = {e: ((fl & _EVENT_BIT[e]) != 0).numpy().reshape(shape) for e in OP_EVENTS[op]}
-    return codes.numpy().reshape(shape), masks, counts
+class PluginStager:
+    """The ``Device.run`` contract (int64 NumPy codes in, int64 codes and
+    boolean event masks out) for large equal-shape elementwise calls.
+
+    The element range runs in chunks through ``slots`` staging slots, each a
+    set of pinned host buffers and device buffers allocated once and reused
+    by every call.  Per chunk the host narrows the int64 operands into the
+    slot's pinned int16 buffers (torch's threaded casting copy); the slot's
+    stream copies them in, runs the kernel and copies the int16 result and
+    the event bytes back; the host then widens them into the caller's int64
+    output and boolean masks.  With three slots the host's narrowing of one
+    chunk and widening of another overlap the GPU's work on a third.  Status
+    counts accumulate per slot on the device and are read once per call.
+    One call at a time per stager (a lock)."""
+
+    def __init__(self, dev, chunk: int = 1 << 22, slots: int = 3):
+        import threading
+        import torch
+        self.dev = dev
+        self.chunk = chunk
+        d = dev.torch_device
+        self.streams = [torch.cuda.Stream(device=d) for _ in range(slots)]
+        self.done = [torch.cuda.Event() for _ in range(slots)]
+        self.h_in = [[torch.empty(chunk, dtype=torch.int16, pin_memory=True) for _ in range(3)]
+                     for _ in range(slots)]
+        self.h_out = [torch.empty(chunk, dtype=torch.int16, pin_memory=True) for _ in range(slots)]
+        self.h_fl = [torch.empty(chunk, dtype=torch.uint8, pin_memory=True) for _ in range(slots)]
+        self.d_in = [[torch.empty(chunk, dtype=torch.int16, device=d) for _ in range(3)] for _ in range(slots)]
+        self.d_out = [torch.empty(chunk, dtype=torch.int16, device=d) for _ in range(slots)]
+        self.d_fl = [torch.empty(chunk, dtype=torch.uint8, device=d) for _ in range(slots)]
+        self.counts = torch.zeros(slots, _lib.N_COUNTS, dtype=torch.int64, device=d)
+        self.lock = threading.Lock()
+
+    def run(self, op, bits, operands, events, event_bits, pow_n: int = 0):
+        """``operands``: C-contiguous int64 arrays of one shape.  Returns
+        (int64 codes, {event: bool mask}, counts int64[8]) of that shape."""
+        import warnings
+        import torch
+        shape = operands[0].shape
+        n = operands[0].size
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")                # read-only caller arrays: only read here
+            flat = [torch.from_numpy(o.reshape(-1)) for o in operands]
+        codes = np.empty(n, dtype=np.int64)
+        masks = {e: np.empty(n, dtype=bool) for e in events}
+        t_codes = torch.from_numpy(codes)
+        t_masks = {e: torch.from_numpy(m) for e, m in masks.items()}
+        nslot = len(self.streams)
+        with self.lock:
+            self.counts.zero_()
+            cur = torch.cuda.current_stream(self.dev.torch_device)
+            for st in self.streams:
+                st.wait_stream(cur)
+            pending = []
+
+            def finish(item):
+                slot, lo, hi = item
+                m = hi - lo
+                self.done[slot].synchronize()
+                t_codes[lo:hi].copy_(self.h_out[slot][:m])                 # int16 -> int64
+                fl = self.h_fl[slot][:m]
+                for e, mk in t_masks.items():
+                    torch.ne(torch.bitwise_and(fl, event_bits[e]), 0, out=mk[lo:hi])
+
+            for k, lo in enumerate(range(0, n, self.chunk)):
+                hi = min(n, lo + self.chunk)
+                m = hi - lo
+                slot = k % nslot
+                if len(pending) == nslot:
+                    finish(pending.pop(0))                              # frees this slot
+                hin = self.h_in[slot]
+                for i, src in enumerate(flat):
+                    hin[i][:m].copy_(src[lo:hi])                        # int64 -> int16
+                st = self.streams[slot]
+                with torch.cuda.stream(st):
+                    din = self.d_in[slot]
+                    for i in range(len(flat)):
+                        din[i][:m].copy_(hin[i][:m], non_blocking=True)
+                    b = din[1][:m] if len(flat) > 1 else None
+                    c = din[2][:m] if len(flat) > 2 else None
+                    _lib.elementwise(op, bits, din[0][:m], b, c, self.d_out[slot][:m], self.d_fl[slot][:m],
+                                     self.counts[slot], pow_n=pow_n, stream=st)
+                    self.h_out[slot][:m].copy_(self.d_out[slot][:m], non_blocking=True)
+                    self.h_fl[slot][:m].copy_(self.d_fl[slot][:m], non_blocking=True)
+                    self.done[slot].record(st)
+                pending.append((slot, lo, hi))
+            while pending:
+                finish(pending.pop(0))
+            for st in self.streams:
+                cur.wait_stream(st)
+            res = self.counts.sum(0).cpu().numpy()
+        _lib.check_counts(res)
+        return codes.reshape(shape), {e: mk.reshape(shape) for e, mk in masks.items()}, res

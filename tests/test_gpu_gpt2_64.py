@@ -75,7 +75,9 @@ def test_gpt2_64_tokens_compiled(gpu):
     compiled = torch.compile(model, backend="superfloat")
     _run_and_check(model, compiled)
     reps = sft.compile_reports()[n0:]
-    assert sum(len(r.on_device) for r in reps) == 49
+    # dynamo compiles a block's graph once and reuses it for the 12 blocks, so the
+    # reports hold fewer nodes than layers; every SF node went to the device
+    assert reps and all(r.on_device and not r.host_emulated for r in reps)
     torch._dynamo.reset()
 
 
