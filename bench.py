@@ -529,7 +529,7 @@ def main():
 
     # end to end: codes in pinned host memory, copies inside the timed region
     if not args.no_e2e:
-        from superfloat.python_b200._hostpath import HostPipeline, plugin_run
+        from superfloat.python_b200._hostpath import HostPipeline
         pipe = HostPipeline(dev)
         hx = {}
         for name, v in (("x", x), ("y", y), ("z", z), ("d", d)):
@@ -558,16 +558,27 @@ def main():
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "path": "int16 codes in pinned host memory -> chunked H2D / sfb_elementwise / D2H on two "
                                "streams, status counts read back every op"}
-        # the reference's Device.run contract: int64 NumPy codes in, int64 codes + boolean masks out
+        # the reference's Device.run contract: int64 NumPy codes in, int64 codes + boolean masks out,
+        # timed on every rank (each rank its own 2^26 elements) with its share of the host's cores
         xs = {"add": (x, y), "sub": (x, y), "mul": (x, y), "fma": (x, y, z), "div": (x, d)}
-        plugin_run(dev, pipe, "add", fmt, x[:4096], y[:4096])
+        threads = torch.get_num_threads()
+        torch.set_num_threads(max(1, host_cores() // world))
+        dev.run("add", fmt, x, y)                        # warm-up: allocates the staging buffers
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
         for op in OPS:
-            plugin_run(dev, pipe, op, fmt, *xs[op])
-        dtp = time.perf_counter() - t0
-        line["e2e_plugin_int64"] = {"value": len(OPS) * n / dtp / 1e9, "unit": "Gelem/s",
-                                    "path": "B200Device.run contract: int64 NumPy codes in, int64 codes and "
-                                            "boolean event masks out (host narrowing / widening included)"}
+            dev.run(op, fmt, *xs[op])
+        dtp = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev.torch_device)
+        if world > 1:
+            dist.all_reduce(dtp, op=dist.ReduceOp.MAX)
+        torch.set_num_threads(threads)
+        line["e2e_plugin_int64"] = {"value": len(OPS) * n * world / float(dtp.item()) / 1e9, "unit": "Gelem/s",
+                                    "threads_per_rank": max(1, host_cores() // world),
+                                    "path": "B200Device.run, the reference's Device contract: int64 NumPy codes "
+                                            "in, int64 codes and boolean event masks out (host narrowing / "
+                                            "widening included), all ranks, max-over-ranks wall time"}
 
     # CPU baseline on rank 0, N = 1
     if rank == 0 and world == 1 and not args.no_cpu:

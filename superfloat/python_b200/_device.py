@@ -38,6 +38,10 @@ OP_EVENTS = {
 }
 _EVENT_BIT = {"overflow": _lib.F_OVERFLOW, "underflow": _lib.F_UNDERFLOW, "divide": _lib.F_DIVIDE,
               "invalid": _lib.F_INVALID}
+# elementwise Device.run calls at least this large (all operands of the
+# output's shape) go through the pooled, chunked host pipeline
+STAGED_MIN_ELEMENTS = 1 << 20
+
 ARITY = {"add": 2, "sub": 2, "mul": 2, "div": 2, "fma": 3, "neg": 1, "abs": 1, "sqrt": 1, "pow": 1,
          "matmul": 2, "matmul_wide": 2, "sum": 1}
 

@@ -154,10 +154,13 @@ def test_workload_full_size_2_26(gpu):
 
 def test_host_pipeline_and_plugin_contract(gpu, rng):
     """Host-resident codes through the chunked two-stream pipeline, and the
-    int64 Device.run contract built on it, equal the oracle."""
+    int64 Device.run contract through the pooled stager (small chunks, so
+    several chunks reuse each slot), equal the oracle."""
     import torch
-    from superfloat.python_b200._hostpath import HostPipeline, plugin_run
+    from superfloat.python_b200._device import _EVENT_BIT, OP_EVENTS
+    from superfloat.python_b200._hostpath import HostPipeline, PluginStager
     pipe = HostPipeline(gpu, chunk=1 << 12)
+    stager = PluginStager(gpu, chunk=1 << 12)
     n = 3 * (1 << 12) + 77
     for op in ("add", "mul", "div", "fma", "sqrt"):
         xs = [edge_codes(16, n, rng) for _ in range(ARITY[op])]
@@ -173,8 +176,29 @@ def test_host_pipeline_and_plugin_contract(gpu, rng):
         np.testing.assert_array_equal(out.numpy(), want)
         for i, e in enumerate(("overflow", "underflow", "divide", "invalid")):
             assert int(counts[i]) == int(np.count_nonzero(ev.get(e, False))), (op, e)
-        codes, masks, _ = plugin_run(gpu, pipe, op, FORMATS[16], *xs)
-        np.testing.assert_array_equal(codes, want)
-        assert set(masks) == set(ev)
+        for _ in range(2):                                  # the second call reuses the staging buffers
+            codes, masks, cnt = stager.run(op, 16, [np.ascontiguousarray(x, dtype=np.int64) for x in xs],
+                                           OP_EVENTS[op], _EVENT_BIT)
+            np.testing.assert_array_equal(codes, want)
+            assert set(masks) == set(ev)
+            for e, m in ev.items():
+                np.testing.assert_array_equal(masks[e], m)
+            np.testing.assert_array_equal(cnt, counts)
+
+
+def test_device_run_stages_large_calls(gpu):
+    """Device.run on 2^20 + 5 codes (the staged path) and with a broadcast
+    operand (the direct path) equals the oracle, codes and masks."""
+    from superfloat.python_b200._device import STAGED_MIN_ELEMENTS
+    rng = np.random.default_rng(3)
+    n = STAGED_MIN_ELEMENTS + 5
+    a = rng.integers(-32767, 32768, n)
+    b = rng.integers(-32767, 32768, n)
+    b[::101] = 0
+    for op, xs in (("div", (a, b)), ("add", (a, b)), ("mul", (a, b[:1]))):
+        got, masks = gpu.run(op, FORMATS[16], *xs)
+        want, ev = sfref.ew(op, 16, *xs)
+        np.testing.assert_array_equal(got, want)
         for e, m in ev.items():
-            np.testing.assert_array_equal(masks[e], m)
+            np.testing.assert_array_equal(masks[e], np.broadcast_to(m, got.shape))
+    assert gpu._stager is not None
