@@ -75,9 +75,10 @@ def test_gpt2_64_tokens_compiled(gpu):
     compiled = torch.compile(model, backend="superfloat")
     _run_and_check(model, compiled)
     reps = sft.compile_reports()[n0:]
-    # dynamo compiles a block's graph once and reuses it for the 12 blocks, so the
-    # reports hold fewer nodes than layers; every SF node went to the device
-    assert reps and all(r.on_device and not r.host_emulated for r in reps)
+    # dynamo compiles a block's graph once and reuses it for the 12 blocks (and some
+    # graphs between breaks hold only float ops), so the reports hold fewer SF nodes
+    # than layers: none of them was left on the host
+    assert sum(len(r.on_device) for r in reps) > 0 and not any(r.host_emulated for r in reps)
     torch._dynamo.reset()
 
 
