@@ -458,9 +458,22 @@ __global__ void __launch_bounds__(NT, 1) chain_pk_kernel(const int16_t *__restri
 
     Counts cnt;
     unsigned bad = 0;
+    // The converted layer's float output (one of y32 / y64, no codes or flags)
+    // is staged through shared memory, free once the last k-tile is done, and
+    // written out a row at a time by whole warps: a thread's own outputs are
+    // 8 consecutive columns of 8 rows, which stored directly leave every
+    // 32-byte sector of a row to 4-byte writes from several store instructions.
+    const bool stage = (e.y32 != nullptr) != (e.y64 != nullptr) && !e.codes && !e.flags;
+    constexpr int SROW = PK_BN + 4;                       // floats per staged row (16-byte aligned rows)
+    constexpr int DROW = PK_BN + 2;                       // doubles per staged row
+    static_assert(PK_BM * DROW * 8 <= (int)sizeof(PkStage<PK_BM>) * 2, "staged tile fits the stages");
+    float *tile32 = reinterpret_cast<float *>(smem_raw);
+    double *tile64 = reinterpret_cast<double *>(smem_raw);
+    const double ascale = (e.y32 || e.y64) ? (e.a_dev ? __ldg(e.a_dev) : e.a) : 0.0;
 #pragma unroll
     for (int i = 0; i < PK_TM; i++) {
-        const int gm = m0 + ty * PK_TM + i;
+        const int rl = ty * PK_TM + i, gm = m0 + rl;
+        double yv[2 * PK_TP];
 #pragma unroll
         for (int p = 0; p < PK_TP; p++) {
             const int lo = (int)(int16_t)(acc[i][p] & 0xFFFFu);
@@ -468,6 +481,7 @@ __global__ void __launch_bounds__(NT, 1) chain_pk_kernel(const int16_t *__restri
 #pragma unroll
             for (int l = 0; l < 2; l++) {
                 const int gn = n0 + tx * 2 * PK_TP + 2 * p + l;
+                yv[2 * p + l] = 0.0;
                 if (gm < M && gn < N) {
                     int v = l ? hi : lo;
                     if (v > w.M || v < -w.M) {                // the caller's proof did not hold
@@ -475,7 +489,46 @@ __global__ void __launch_bounds__(NT, 1) chain_pk_kernel(const int16_t *__restri
                         v = clampi(v, -w.M, w.M);
                     }
                     const bool un = ((uf[i][p] >> (15 + 16 * l)) & 1u) == 0;
-                    emit(e, w, z * so + (int64_t)gm * N + gn, gn, v, false, un, cnt);
+                    if (stage) {
+                        bool o = false;
+                        if (e.bias) {
+                            const int sum = v + (int)e.bias[gn];
+                            o = sum > w.M || sum < -w.M;
+                            v = clampi(sum, -w.M, w.M);
+                        }
+                        yv[2 * p + l] = (double)v / (double)(1 << w.sh) * ascale * e.s_col[gn];
+                        cnt.over += o;
+                        cnt.under += un;
+                    } else {
+                        emit(e, w, z * so + (int64_t)gm * N + gn, gn, v, false, un, cnt);
+                    }
+                }
+            }
+        }
+        if (stage) {
+            if (e.y32) {
+                float4 *d = reinterpret_cast<float4 *>(tile32 + rl * SROW + tx * 2 * PK_TP);
+                d[0] = make_float4((float)yv[0], (float)yv[1], (float)yv[2], (float)yv[3]);
+                d[1] = make_float4((float)yv[4], (float)yv[5], (float)yv[6], (float)yv[7]);
+            } else {
+                double2 *d = reinterpret_cast<double2 *>(tile64 + rl * DROW + tx * 2 * PK_TP);
+#pragma unroll
+                for (int q = 0; q < PK_TP; q++) d[q] = make_double2(yv[2 * q], yv[2 * q + 1]);
+            }
+        }
+    }
+    if (stage) {
+        __syncthreads();
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int rl = warp; rl < PK_BM; rl += NT / 32) {
+            const int gm = m0 + rl;
+            if (gm >= M) break;
+            const int64_t base = z * so + (int64_t)gm * N + n0;
+#pragma unroll
+            for (int c = lane; c < PK_BN; c += 32) {
+                if (n0 + c < N) {
+                    if (e.y32) e.y32[base + c] = tile32[rl * SROW + c];
+                    else e.y64[base + c] = tile64[rl * DROW + c];
                 }
             }
         }

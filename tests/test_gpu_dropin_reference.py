@@ -41,7 +41,7 @@ def _run_child(device, tmp_path):
 def test_b200_plugged_into_the_reference_runtime(gpu, tmp_path):
     r = _run_child("b200", tmp_path)
     assert r["mismatches"] == [], r["mismatches"]
-    assert len(r["checks"]) == 42, r["checks"]          # the flagged mock's 37 plus the 5 div checks
+    assert len(r["checks"]) == 43, r["checks"]          # the flagged mock's 37 plus codes and status of div at 3 widths
     assert r["launches"] > 100                           # every heavy op and converted layer reached the B200
 
 
