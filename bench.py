@@ -172,6 +172,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _cpu_pool_worker(n):
+    return cpu_sample(n)
+
+
 def reference_site():
     """The directory holding the reference package ``sf`` (an offline install
     under baseline/_ref, or SF_REFERENCE_SITE), or None."""
@@ -316,7 +320,7 @@ def cpu_matmul_baselines():
     # the exhaustive sweep: a few a-rows through the four ops
     fn, kind = cpu_ops()
     M = 32767
-    arows = np.arange(-3, 3)
+    arows = np.arange(-128, 128)
     b = np.arange(-M, M + 1)
     ka, kb = np.repeat(arows, b.size), np.tile(b, arows.size)
     t0 = time.perf_counter()
@@ -638,10 +642,11 @@ def add_matmul_rooflines(torch, mm, clocks, world):
     limb-adjusted int8 rate (11 int8 passes per sf16 product, int8 peak
     measured here with torch._int_mm), the chain kernels against the issue
     rate (their ncu instruction counts)."""
+    peak = None
     for key, e in mm.items():
-        if key.startswith("wide_"):
+        if key.startswith("wide_") and e:
             n = int(key.split("_")[1])
-            peak = int8_peak(torch)
+            peak = peak or int8_peak(torch)
             achieved = 11 * 2 * (n // world) * n * n / (e["ms"] / 1e3) / 1e12
             e["roofline"] = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "int8 TOPS",
                              "frac": achieved / peak, "traffic": None,
@@ -706,7 +711,10 @@ def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
     if rank == 0:
         import hashlib
         res[f"wide_{n}"]["codes_sha256"] = hashlib.sha256(full.cpu().numpy().astype("<i2").tobytes()).hexdigest()[:16]
-    del tA, tB, out, full
+    del tA, out
+    res[f"wide_{n}_prepared_b"] = bench_wide_prepared(torch, tB, n, rank, world, dist,
+                                                      res[f"wide_{n}"].get("codes_sha256"))
+    del tB, full
     if rank != 0:
         return res
     # chain 512^3
@@ -725,6 +733,69 @@ def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
     ms = e0.elapsed_time(e1) / reps
     res["chain_512"] = {"ms": ms, "TOPS": 2 * 512 ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)"}
     return res
+
+
+def bench_wide_prepared(torch, tB, n, rank, world, dist, want_sha):
+    """The wide n^3 matmul with B prepared once (a replicated, static
+    operand: the reference's prepared weight), its output rows gathered on
+    every rank while the next rows compute.  Rows go to ranks block-cyclically
+    in ``parts`` pieces of P rows (piece j of rank r = global rows
+    [(j world + r) P, (j world + r + 1) P)), so the all-gather of piece j lands
+    contiguously, in global order, in rows [j world P, (j + 1) world P) of the
+    full output, with no copy; it runs on NCCL's stream beside piece j + 1's
+    kernels.  ``ms`` = compute + gather, CUDA events, max over ranks."""
+    import hashlib
+    from superfloat.python_b200 import _lib, _shard, workloads
+    parts = 2 if world > 1 else 1
+    if n % (world * parts):
+        return None
+    P = n // (world * parts)
+    dev = tB.device
+    A, _ = workloads.wide_square(n, n, n, 0)
+    rows = np.concatenate([A[lo:hi] for lo, hi in _shard.cyclic_pieces(n, world, parts, rank)])
+    del A
+    tA = torch.from_numpy(rows).to(torch.int16).to(dev)
+    prep = torch.empty(_lib.wide_prepared_b_bytes(16, "v4.9.2", n, n), dtype=torch.uint8, device=dev)
+    _lib.wide_prepare_b(16, "v4.9.2", tB, n, n, n, prep)
+    ws = torch.empty(_lib.wide_workspace(16, "v4.9.2", 1, P, n, n), dtype=torch.uint8, device=dev)
+    loc = torch.empty(parts, P, n, dtype=torch.int16, device=dev)
+    full = torch.empty(n, n, dtype=torch.int16, device=dev)
+    cnt = torch.zeros(8, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        works = []
+        for j in range(parts):
+            _lib.matmul_wide_prepared(16, "v4.9.2", tA[j * P:(j + 1) * P], tB, prep, None, 0, loc[j], None, cnt, 1,
+                                      P, n, n, n, n, 0, P * n, 0, 0, 0, ws)
+            works.append(_shard.gather_piece(full, loc[j], j, dist, world, async_op=True))
+        for w in works:
+            if w is not None:
+                w.wait()
+
+    for _ in range(2):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = _shard.max_over_ranks(e0.elapsed_time(e1) / reps, "cuda", dist, world)
+    _lib.check_counts(cnt.cpu().numpy())
+    out = {"ms": ms, "TOPS": 2 * n ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)",
+           "includes": "compute and the all-gather of the output rows (overlapped); B prepared once, outside",
+           "sharding": f"rows of A block-cyclic over {world} GPU(s) in {parts} piece(s) of {P} rows, B replicated"}
+    if rank == 0:
+        sha = hashlib.sha256(full.cpu().numpy().astype("<i2").tobytes()).hexdigest()[:16]
+        out["codes_sha256"] = sha
+        out["codes_equal_unprepared"] = sha == want_sha if want_sha else None
+    del tA, prep, ws, loc, full
+    return out
 
 
 def bench_sweep(torch, dist, rank, world, bits=16):

@@ -229,6 +229,33 @@ SFB_API int sfb_matmul_wide(int bits, int mx, const int16_t *A, const int16_t *B
                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
                     void *workspace, int64_t workspace_bytes, sfb_counts *counts, sfb_stream stream);
 
+/* Bytes of the prepared form of a wide B operand (N columns, K rows), 0 when
+ * this width / MX version has none (the calls then read B's codes).  The
+ * prepared form is the reference's prepared weight of its compiled MX loop
+ * (_fastmx.prep_b, src/sf/_fastmx.py:168-173, used by
+ * _linalg.matmul_wide_acc_prepared, src/sf/_linalg.py:311-321): B's operand
+ * planes, bit slices and column statistics for the tensor-core path. */
+SFB_API int64_t sfb_wide_prepared_b_bytes(int bits, int mx, int64_t N, int64_t K);
+
+/* Prepare B (K x N codes, row stride ldb) once into `prep` (device memory
+ * of sfb_wide_prepared_b_bytes() bytes) for sfb_matmul_wide_prepared; a B
+ * that many calls share (a layer's weights, a replicated operand) is then
+ * not re-prepared per call.  Asynchronous on `stream`. */
+SFB_API int sfb_wide_prepare_b(int bits, int mx, const int16_t *B, int64_t N, int64_t K, int64_t ldb, void *prep,
+                               int64_t prep_bytes, sfb_stream stream);
+
+/* sfb_matmul_wide with B prepared by sfb_wide_prepare_b (the reference's
+ * _linalg.matmul_wide_acc_prepared then POP, src/sf/_linalg.py:311-321 and
+ * :201-220): one B for every batch entry; B's codes are still passed, for
+ * the outputs the exact CUDA-core path recomputes.  `prep` NULL: exactly
+ * sfb_matmul_wide with stride_b 0. */
+SFB_API int sfb_matmul_wide_prepared(int bits, int mx, const int16_t *A, const int16_t *B, const void *prep,
+                                     const int8_t *shift_arr, int shift, int16_t *out, uint8_t *flags, int64_t batch,
+                                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t stride_a,
+                                     int64_t stride_out, int64_t shift_sb, int64_t shift_sm, int64_t shift_sn,
+                                     void *workspace, int64_t workspace_bytes, sfb_counts *counts,
+                                     sfb_stream stream);
+
 /* Failure-detection hook with no counterpart in the reference: the wide
  * tensor-core GEMM launches that the CALLING THREAD makes from now on bound
  * each of their pipeline waits (an mbarrier poll loop) by `polls` polls

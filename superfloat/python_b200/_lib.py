@@ -43,6 +43,10 @@ SIGNATURES = {
     "sfb_matmul_wide_noalloc": (_i32, [_i32, _i32, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
     "sfb_wide_wait_limit": (_i32, [ctypes.c_uint, _i32]),
+    "sfb_wide_prepared_b_bytes": (_i64, [_i32, _i32, _i64, _i64]),
+    "sfb_wide_prepare_b": (_i32, [_i32, _i32, _p, _i64, _i64, _i64, _p, _i64, _p]),
+    "sfb_matmul_wide_prepared": (_i32, [_i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
@@ -304,6 +308,28 @@ def wide_finish(bits, mx, acc, M, N, row_exp, col_exp, row_norm, col_norm, h, us
                                 _ptr(col_norm), int(h), int(bool(use_rule)), int(shift), _ptr(bias), _ptr(y32),
                                 _ptr(y64), _ptr(flags), _ptr(stats), _ptr(counts), _stream(stream))
     check(rc, "sf wide finish")
+
+
+def wide_prepared_b_bytes(bits, mx, N, K) -> int:
+    n = load().sfb_wide_prepared_b_bytes(bits, MX[mx], N, K)
+    if n < 0:
+        check(int(n), "sf wide prepared B size")
+    return int(n)
+
+
+def wide_prepare_b(bits, mx, B, N, K, ldb, prep, stream=None) -> None:
+    nbytes = 0 if prep is None else prep.numel() * prep.element_size()
+    check(load().sfb_wide_prepare_b(bits, MX[mx], _ptr(B), N, K, ldb, _ptr(prep), nbytes, _stream(stream)),
+          "sf wide prepare B")
+
+
+def matmul_wide_prepared(bits, mx, A, B, prep, shift_arr, shift, out, flags, counts, batch, M, N, K, lda, ldb, sa,
+                         so, ssb, ssm, ssn, workspace, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = load().sfb_matmul_wide_prepared(bits, MX[mx], _ptr(A), _ptr(B), _ptr(prep), _ptr(shift_arr), int(shift),
+                                         _ptr(out), _ptr(flags), batch, M, N, K, lda, ldb, sa, so, ssb, ssm, ssn,
+                                         _ptr(workspace), ws_bytes, _ptr(counts), _stream(stream))
+    check(rc, "sf matmul (wide, prepared B)")
 
 
 def matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, counts, batch, M, N, K, lda, ldb, sa, sb, so,

@@ -61,6 +61,35 @@ def gather_rows(local, cuts, dist=None, world: int = 1):
     return torch.cat([parts[r][:cuts[r + 1] - cuts[r]] for r in range(world)])
 
 
+def cyclic_pieces(n: int, world: int, parts: int, rank: int) -> list[tuple[int, int]]:
+    """Rows of ``rank`` when n rows go to the ranks block-cyclically in
+    ``parts`` pieces of P = n / (world parts) rows: piece j is global rows
+    [(j world + rank) P, (j world + rank + 1) P).  The pieces j of all ranks
+    then form rows [j world P, (j + 1) world P) in rank order, so gathering
+    piece j needs no reordering."""
+    if n % (world * parts):
+        raise ValueError(f"{n} rows do not split into {world} x {parts} equal pieces")
+    P = n // (world * parts)
+    return [((j * world + rank) * P, (j * world + rank + 1) * P) for j in range(parts)]
+
+
+def gather_piece(full, piece, j: int, dist=None, world: int = 1, async_op: bool = False):
+    """All-gather every rank's piece j (P rows, block-cyclic order) into rows
+    [j world P, (j + 1) world P) of ``full`` (contiguous, every rank).
+    Returns the collective's work handle when ``async_op`` (NCCL runs it on
+    its own stream beside later kernels), else None."""
+    import torch
+    P = piece.shape[0]
+    dst = full[j * world * P:(j + 1) * world * P]
+    if dist is None or world == 1:
+        dst.copy_(piece)
+        return None
+    src = piece.contiguous()
+    if not _nccl_type(piece.dtype):                  # NCCL has no int16: send the bytes
+        dst, src = dst.view(torch.uint8), src.view(torch.uint8)
+    return dist.all_gather_into_tensor(dst, src, async_op=async_op)
+
+
 def sharded_matmul(compute, A, B, rank: int, world: int, dist=None):
     """Row-sharded matmul: this rank computes rows [lo, hi) of A @ B with
     ``compute(A_block, B) -> (codes, flags, counts)`` (B replicated), then

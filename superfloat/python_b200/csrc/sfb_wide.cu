@@ -17,8 +17,11 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
                 int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
                 int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn,
                 void *ws, int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled,
-                int32_t *acc_out = nullptr);
+                int32_t *acc_out = nullptr, const void *bprep = nullptr);
 int64_t wide_tc_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N, int64_t K);
+int64_t wide_tc_prepared_b_bytes(int bits, int mx, int64_t N, int64_t K);
+int wide_tc_prepare_b(int bits, int mx, const int16_t *B, int64_t N, int64_t K, int64_t ldb, void *prep,
+                      int64_t prep_bytes, cudaStream_t st);
 
 namespace {
 
@@ -224,4 +227,52 @@ extern "C" int sfb_matmul_wide_acc(int bits, int mx, const int16_t *A, const int
     if (rc != SFB_OK || handled) return rc;
     return wide_simt(bits, mx, A, B, nullptr, 0, nullptr, clipped, batch, M, N, K, lda, ldb, stride_a, stride_b,
                      stride_acc, 0, 0, 0, counts, st, acc);
+}
+
+extern "C" int64_t sfb_wide_prepared_b_bytes(int bits, int mx, int64_t N, int64_t K) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16 || (mx != SFB_MX_V492 && mx != SFB_MX_V481) || N < 0 || K < 0)
+        return set_error(SFB_EINVAL, "sfb_wide_prepared_b_bytes: bad argument");
+    return wide_tc_prepared_b_bytes(bits, mx, N, K);
+}
+
+extern "C" int sfb_wide_prepare_b(int bits, int mx, const int16_t *B, int64_t N, int64_t K, int64_t ldb, void *prep,
+                                  int64_t prep_bytes, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_wide_prepare_b: width %d is not 4..16", bits);
+    if (mx != SFB_MX_V492 && mx != SFB_MX_V481) return set_error(SFB_EINVAL, "sfb_wide_prepare_b: unknown mx %d", mx);
+    if (N < 0 || K < 0) return set_error(SFB_EINVAL, "sfb_wide_prepare_b: negative size");
+    if (N == 0 || K == 0) return SFB_OK;
+    return wide_tc_prepare_b(bits, mx, B, N, K, ldb, prep, prep_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int sfb_matmul_wide_prepared(int bits, int mx, const int16_t *A, const int16_t *B, const void *prep,
+                                        const int8_t *shift_arr, int shift, int16_t *out, uint8_t *flags,
+                                        int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                        int64_t stride_a, int64_t stride_out, int64_t shift_sb, int64_t shift_sm,
+                                        int64_t shift_sn, void *workspace, int64_t workspace_bytes,
+                                        sfb_counts *counts, sfb_stream stream) {
+    using namespace sfb;
+    if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: width %d is not 4..16", bits);
+    if (mx != SFB_MX_V492 && mx != SFB_MX_V481)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: unknown mx %d", mx);
+    if (shift_arr == nullptr && (shift < -32 || shift > 31))
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: shift %d is not in -32..31", shift);
+    if (batch < 0 || M < 0 || N < 0 || K < 0) return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: negative size");
+    if (batch == 0 || M == 0 || N == 0) return SFB_OK;
+    if (out == nullptr || (K > 0 && (A == nullptr || B == nullptr)))
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: null operand or output");
+    if (K > 0 && (lda < K || ldb < N)) return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: lda < K or ldb < N");
+    if (stride_out < M * N && batch > 1)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: output batch entries overlap");
+    if (prep != nullptr && wide_tc_prepared_b_bytes(bits, mx, N, K) == 0)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide_prepared: this problem has no prepared form of B");
+    cudaStream_t st = (cudaStream_t)stream;
+    bool handled = false;
+    const int rc = wide_tc_try(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a, 0,
+                               stride_out, shift_sb, shift_sm, shift_sn, workspace, workspace_bytes, counts, st,
+                               &handled, nullptr, prep);
+    if (rc != SFB_OK || handled) return rc;
+    return wide_simt(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a, 0,
+                     stride_out, shift_sb, shift_sm, shift_sn, counts, st, nullptr);
 }

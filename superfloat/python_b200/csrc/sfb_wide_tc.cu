@@ -983,6 +983,36 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
 thread_local unsigned t_wait_polls = 0;
 thread_local int t_wait_stall = 0;
 
+// The prepared form of a B operand (sfb_wide_prepare_b): its nine int8
+// planes, column-sliced bit planes and column statistics, laid out as in the
+// workspace but in a buffer of their own, so that a B used by many calls
+// (a layer's weights) is prepared once.
+struct BLayout {
+    int64_t Np, Kp, off_pb, off_bn, off_l1b, off_mxb, total;
+};
+
+BLayout blayout_for(int64_t N, int64_t K) {
+    BLayout L;
+    L.Np = up(N, GN);
+    L.Kp = up(K, TILE);
+    int64_t o = 0;
+    auto take = [&](int64_t bytes) {
+        const int64_t at = o;
+        o = up(o + bytes, 1024);
+        return at;
+    };
+    L.off_pb = take(NPLANES * L.Np * L.Kp);
+    L.off_bn = take(4 * 9 * L.Kp * (L.Np / 32));
+    L.off_l1b = take(8 * L.Np);
+    L.off_mxb = take(4 * L.Np);
+    L.total = o + 1024;            // slack for aligning the caller's base
+    return L;
+}
+
+bool b_eligible(int bits, int mx, int64_t N, int64_t K) {
+    return mx == SFB_MX_V492 && bits >= 9 && bits <= 16 && K >= 1 && K <= KMAX && N >= 1 && up(N, TILE) <= (1 << 20);
+}
+
 bool eligible(int bits, int mx, int64_t M, int64_t N, int64_t K) {
     return mx == SFB_MX_V492 && bits >= 9 && bits <= 16 && K >= 1 && K <= KMAX && M >= 1 && N >= 1 &&
            (double)M * (double)N * (double)K >= (double)(1 << 22) && up(M, TILE) <= (1 << 20) &&
@@ -1032,9 +1062,12 @@ int64_t wide_tc_workspace(int bits, int mx, int64_t batch, int64_t M, int64_t N,
 int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8_t *shift_arr, int shift,
                 int16_t *out, uint8_t *flags, int64_t batch, int64_t M, int64_t N, int64_t K, int64_t lda,
                 int64_t ldb, int64_t sa, int64_t sb, int64_t so, int64_t ssb, int64_t ssm, int64_t ssn, void *ws,
-                int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled, int32_t *acc_out) {
+                int64_t ws_bytes, sfb_counts *counts, cudaStream_t st, bool *handled, int32_t *acc_out,
+                const void *bprep) {
     *handled = false;
     if (!eligible(bits, mx, M, N, K)) return SFB_OK;
+    if (bprep && batch > 1 && sb != 0)
+        return set_error(SFB_EINVAL, "sfb_matmul_wide: a prepared B serves one matrix (stride_b must be 0)");
     const Layout L = layout_for(M, N, K);
     if (ws == nullptr || ws_bytes < L.total)
         return set_error(SFB_EINVAL, "sfb_matmul_wide: workspace of %lld bytes is smaller than the %lld needed",
@@ -1062,6 +1095,14 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     long long *l1a = reinterpret_cast<long long *>(base + L.off_l1a);
     long long *l1b = reinterpret_cast<long long *>(base + L.off_l1b);
     int *mxa = reinterpret_cast<int *>(base + L.off_mxa), *mxb = reinterpret_cast<int *>(base + L.off_mxb);
+    if (bprep) {                   // B's planes, bit slices and statistics from its prepared buffer
+        const BLayout BL = blayout_for(N, K);
+        uint8_t *bb = reinterpret_cast<uint8_t *>(((uintptr_t)bprep + 1023) & ~(uintptr_t)1023);
+        pb = bb + BL.off_pb;
+        bn = reinterpret_cast<uint32_t *>(bb + BL.off_bn);
+        l1b = reinterpret_cast<long long *>(bb + BL.off_l1b);
+        mxb = reinterpret_cast<int *>(bb + BL.off_mxb);
+    }
     int32_t *SX = reinterpret_cast<int32_t *>(base + L.off_sx);
     CUtensorMap tmA, tmB;
     int rc = make_map(&tmA, pa, L.Mp, L.Kp, TILE);
@@ -1074,9 +1115,10 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
             return check_launch("sfb_matmul_wide (stats reset)");
         prep_kernel<true><<<dim3((unsigned)(L.Mp / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
             A + z * sa, lda, (int)M, (int)K, (int)L.Mp, (int)L.Kp, bits, pa, ra, l1a, mxa, nullptr, 0);
-        prep_kernel<false><<<dim3((unsigned)(L.Np / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
-            B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb, bn,
-            (int)(L.Np / 32));
+        if (!bprep)
+            prep_kernel<false><<<dim3((unsigned)(L.Np / PR), (unsigned)(L.Kp / PK)), 256, 0, st>>>(
+                B + z * sb, ldb, (int)N, (int)K, (int)L.Np, (int)L.Kp, bits, pb, nullptr, l1b, mxb, bn,
+                (int)(L.Np / 32));
         RemIn in;
         in.rec = ra;
         in.bn = bn;
@@ -1119,6 +1161,28 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
     }
     *handled = true;
     return SFB_OK;
+}
+
+int64_t wide_tc_prepared_b_bytes(int bits, int mx, int64_t N, int64_t K) {
+    return b_eligible(bits, mx, N, K) ? blayout_for(N, K).total : 0;
+}
+
+int wide_tc_prepare_b(int bits, int mx, const int16_t *B, int64_t N, int64_t K, int64_t ldb, void *prep,
+                      int64_t prep_bytes, cudaStream_t st) {
+    if (!b_eligible(bits, mx, N, K)) return SFB_OK;        // no prepared form: calls read B's codes
+    const BLayout BL = blayout_for(N, K);
+    if (prep == nullptr || prep_bytes < BL.total)
+        return set_error(SFB_EINVAL, "sfb_wide_prepare_b: buffer of %lld bytes is smaller than the %lld needed",
+                         (long long)prep_bytes, (long long)BL.total);
+    if (B == nullptr || ldb < N) return set_error(SFB_EINVAL, "sfb_wide_prepare_b: null B or ldb < N");
+    uint8_t *bb = reinterpret_cast<uint8_t *>(((uintptr_t)prep + 1023) & ~(uintptr_t)1023);
+    if (cudaMemsetAsync(bb + BL.off_l1b, 0, BL.off_mxb + 4 * BL.Np - BL.off_l1b, st) != cudaSuccess)
+        return check_launch("sfb_wide_prepare_b (stats reset)");
+    prep_kernel<false><<<dim3((unsigned)(BL.Np / PR), (unsigned)(BL.Kp / PK)), 256, 0, st>>>(
+        B, ldb, (int)N, (int)K, (int)BL.Np, (int)BL.Kp, bits, bb + BL.off_pb, nullptr,
+        reinterpret_cast<long long *>(bb + BL.off_l1b), reinterpret_cast<int *>(bb + BL.off_mxb),
+        reinterpret_cast<uint32_t *>(bb + BL.off_bn), (int)(BL.Np / 32));
+    return check_launch("sfb_wide_prepare_b");
 }
 
 }  // namespace sfb

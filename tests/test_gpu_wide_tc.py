@@ -121,3 +121,55 @@ def test_a_wait_that_runs_out_is_reported_and_the_next_call_is_exact(gpu):
     np.testing.assert_array_equal(got, want)
     np.testing.assert_array_equal((fl & 1) != 0, ev["overflow"])
     assert int(cnt[5]) == 0
+
+
+def test_prepared_b_equals_the_plain_call(gpu):
+    """B prepared once (sfb_wide_prepare_b) and used by calls with different
+    A (ragged, batched, shift arrays) gives the plain call's codes, flags and
+    counts; a width with no prepared form (sf8) falls back to B's codes."""
+    import torch
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(31)
+    K, N = 700, 300
+    B = rng.integers(-32767, 32768, (K, N))
+    tB = torch.from_numpy(B).to(torch.int16).to(dev)
+    nbytes = _lib.wide_prepared_b_bytes(16, "v4.9.2", N, K)
+    assert nbytes > 0 and _lib.wide_prepared_b_bytes(8, "v4.9.2", N, K) == 0
+    prep = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _lib.wide_prepare_b(16, "v4.9.2", tB, N, K, N, prep)
+    for batch, M, shift in ((1, 257, -2), (3, 130, 0), (1, 400, rng.integers(-6, 3, (400, N)))):
+        A = rng.integers(-3000, 3001, (batch, M, K))
+        tA = torch.from_numpy(A).to(torch.int16).to(dev)
+        ws = torch.empty(max(1, _lib.wide_workspace(16, "v4.9.2", batch, M, N, K)), dtype=torch.uint8, device=dev)
+        sh_t = None if np.isscalar(shift) else torch.from_numpy(np.asarray(shift)).to(torch.int8).to(dev)
+        sh = 0 if sh_t is not None else int(shift)
+        ss = (0, N, 1) if sh_t is not None else (0, 0, 0)
+        res = []
+        for use_prep in (False, True):
+            out = torch.empty(batch, M, N, dtype=torch.int16, device=dev)
+            fl = torch.empty(batch, M, N, dtype=torch.uint8, device=dev)
+            cnt = torch.zeros(8, dtype=torch.int64, device=dev)
+            if use_prep:
+                _lib.matmul_wide_prepared(16, "v4.9.2", tA, tB, prep, sh_t, sh, out, fl, cnt, batch, M, N, K, K, N,
+                                          M * K, M * N, *ss, ws)
+            else:
+                _lib.matmul_wide(16, "v4.9.2", tA, tB, sh_t, sh, out, fl, cnt, batch, M, N, K, K, N, M * K, 0, M * N,
+                                 *ss, ws)
+            torch.cuda.synchronize()
+            res.append((out.cpu().numpy(), fl.cpu().numpy(), cnt.cpu().numpy()))
+        for x, y in zip(*res):
+            np.testing.assert_array_equal(x, y)
+        want, _ = _want(16, A[0], B, shift)
+        np.testing.assert_array_equal(res[1][0][0], want)
+        assert int(res[1][2][5]) == 0
+    # sf8 has no prepared form: prep NULL reads B's codes
+    A8 = rng.integers(-127, 128, (200, K))
+    B8 = rng.integers(-127, 128, (K, N))
+    tA8 = torch.from_numpy(A8).to(torch.int16).to(dev)
+    tB8 = torch.from_numpy(B8).to(torch.int16).to(dev)
+    out = torch.empty(200, N, dtype=torch.int16, device=dev)
+    cnt = torch.zeros(8, dtype=torch.int64, device=dev)
+    _lib.matmul_wide_prepared(8, "v4.9.2", tA8, tB8, None, None, -1, out, None, cnt, 1, 200, N, K, K, N, 0, 200 * N,
+                              0, 0, 0, None)
+    want, _ = sfref.matmul_wide(8, A8, B8, -1)
+    np.testing.assert_array_equal(out.cpu().numpy(), want)

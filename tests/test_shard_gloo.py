@@ -43,9 +43,16 @@ def _worker(rank, world, port, out):
         lo, hi = _shard.block(255, world, rank, start=-127)
         rows = torch.arange(lo, hi, dtype=torch.int64)[:, None].repeat(1, 2)
         allrows = _shard.gather_rows(rows, _shard.row_cuts(255, world, -127), dist, world)
+        # block-cyclic pieces gathered one at a time land in global row order
+        full = torch.empty(24, 3, dtype=torch.int16)
+        pieces = _shard.cyclic_pieces(24, world, 3, rank)
+        works = [_shard.gather_piece(full, torch.arange(lo, hi, dtype=torch.int16)[:, None].repeat(1, 3), j, dist,
+                                     world, async_op=True) for j, (lo, hi) in enumerate(pieces)]
+        for w in works:
+            w.wait()
         if rank == 0:
             np.save(out, {"g16": g16.numpy(), "codes": codes.numpy(), "flags": flags.numpy(), "cnt": cnt.numpy(), "t": t,
-                          "rows": allrows.numpy()}, allow_pickle=True)
+                          "rows": allrows.numpy(), "cyclic": full.numpy()}, allow_pickle=True)
     finally:
         dist.destroy_process_group()
 
@@ -67,6 +74,7 @@ def test_sharded_matmul_and_gathers_over_gloo(tmp_path):
     np.testing.assert_array_equal(r["rows"][:, 0], np.arange(-127, 128))
     assert r["g16"].dtype == np.int16
     np.testing.assert_array_equal(r["g16"], (np.arange(9)[:, None] * 1000 - 4000).repeat(3, 1))
+    np.testing.assert_array_equal(r["cyclic"], np.arange(24)[:, None].repeat(3, 1))
 
 
 def test_row_cuts_cover_every_row():
