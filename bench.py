@@ -911,10 +911,12 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     with torch.no_grad(), warnings.catch_warnings():
         warnings.simplefilter("ignore")
         eager_logits = model(ids).logits                  # prepares the weights (cached per weight)
+        model(ids)
         eager_ms, _ = timed(model)
         n_rep = len(sft.compile_reports())
         compiled = torch.compile(model, backend="superfloat")
         compiled(ids)                                     # traces and compiles
+        compiled(ids)
         ms, out = timed(compiled)
     reps_new = sft.compile_reports()[n_rep:]
     same = bool(torch.equal(out.logits, eager_logits))
