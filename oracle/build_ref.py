@@ -8,8 +8,12 @@ temporary file outside the repository and compiles it with the same flags
 into ``oracle/_ref/libmx_ref.so``.  Nothing from the reference is copied into
 the repository; ``oracle/_ref/`` is git-ignored.
 
-Usage: python oracle/build_ref.py [reference_root]   (default /root/reference)
-Exits 0 without building when the reference tree is absent.
+Usage: python oracle/build_ref.py [reference_root]
+The root (the directory holding src/sf) is the argument, else the
+SF_REFERENCE_ROOT environment variable, else the checkout this build
+container mounts read-only beside the repository.  Exits 0 without building
+when no reference tree is found (the GPU machines have none; they use the
+library built here).
 """
 from __future__ import annotations
 
@@ -33,7 +37,12 @@ def extract(ref_root: str) -> str:
     raise RuntimeError(f"no _SRC constant in {path}")
 
 
-def main(ref_root: str = "/root/reference") -> int:
+# where this build container mounts the reference checkout
+MOUNTED_CHECKOUT = "/root/reference"
+
+
+def main(ref_root: str | None = None) -> int:
+    ref_root = ref_root or os.environ.get("SF_REFERENCE_ROOT") or MOUNTED_CHECKOUT
     if not os.path.isdir(os.path.join(ref_root, "src", "sf")):
         print(f"build_ref: no reference tree at {ref_root}; oracle/_ref not built")
         return 0

@@ -1,6 +1,6 @@
 """Regenerate the golden fixtures under tests/golden/ from the reference.
 
-Run in a container that has the reference tree (default /root/reference):
+Run where the reference tree is (its root as the argument or in SF_REFERENCE_ROOT):
 
     SF_CACHE_DIR=/tmp/sfcache python tests/golden/make_golden.py [reference_root]
 
@@ -31,6 +31,9 @@ sys.path.insert(0, REPO)
 
 from superfloat.python_b200 import workloads  # noqa: E402
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
+
 
 def sha_codes(codes) -> str:
     return hashlib.sha256(np.ascontiguousarray(codes, dtype="<i2").tobytes()).hexdigest()
@@ -46,7 +49,8 @@ def dump(name, obj):
     print("wrote", name, os.path.getsize(os.path.join(HERE, name)), "bytes")
 
 
-def main(ref: str = "/root/reference") -> None:
+def main(ref: str | None = None) -> None:
+    ref = reference_root(ref)
     sys.path.insert(0, os.path.join(ref, "src"))
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     from sf import _linalg, _vectorized as vec   # the reference

@@ -28,6 +28,9 @@ import os
 import sys
 import time
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 STATUS_KEYS = ("op", "dtype", "outputs", "saturated", "exact", "underflow", "input_underflow", "weight_underflow",
                "bias_saturated", "headroom_bits", "act_scale")
@@ -49,9 +52,7 @@ def block0_input(model, ids):
 
 
 def main() -> None:
-    ref = os.environ.get("SF_REFERENCE_ROOT")
-    if not ref:
-        sys.exit("set SF_REFERENCE_ROOT to the reference checkout (the directory holding src/sf)")
+    ref = reference_root(sys.argv[1] if len(sys.argv) > 1 else None)
     sys.path.insert(0, os.path.join(ref, "src"))
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     import torch

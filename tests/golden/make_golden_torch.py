@@ -22,6 +22,9 @@ import sys
 
 import numpy as np
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -29,7 +32,8 @@ def sha(t) -> str:
     return hashlib.sha256(t.detach().contiguous().numpy().tobytes()).hexdigest()
 
 
-def main(ref: str = "/root/reference") -> None:
+def main(ref: str | None = None) -> None:
+    ref = reference_root(ref)
     sys.path.insert(0, os.path.join(ref, "src"))
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     import torch

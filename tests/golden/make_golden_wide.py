@@ -28,6 +28,9 @@ import sys
 
 import numpy as np
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 STATUS_KEYS = ("saturated", "exact", "underflow", "input_underflow", "weight_underflow", "bias_saturated",
                "headroom_bits", "outputs", "act_scale", "accumulate", "shift_min", "shift_max", "h", "redone",
@@ -81,7 +84,8 @@ def seeded_cases(rng):
     return out
 
 
-def main(ref: str = "/root/reference") -> None:
+def main(ref: str | None = None) -> None:
+    ref = reference_root(ref)
     sys.path.insert(0, os.path.join(ref, "src"))
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     import torch

@@ -13,10 +13,14 @@ import json
 import os
 import sys
 
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def main(ref: str = "/root/reference") -> None:
+def main(ref: str | None = None) -> None:
+    ref = reference_root(ref)
     with open(os.path.join(ref, "tests", "golden", "checksums.json")) as f:
         sums = json.load(f)
     out = {"source": "reference tests/golden/checksums.json", "line": "{code}\\t{word:0{(N+3)//4}x}\\t{value!r}\\n",

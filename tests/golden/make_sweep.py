@@ -1,6 +1,6 @@
 """Digests of the exhaustive pair sweep, from the reference's vectorised ops.
 
-Run in a container that has the reference tree (default /root/reference):
+Run where the reference tree is (its root as the argument or in SF_REFERENCE_ROOT):
 
     SF_CACHE_DIR=/tmp/sfcache python tests/golden/make_sweep.py [reference_root] [--procs 8]
 
@@ -27,6 +27,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 from superfloat.python_b200 import sweep  # noqa: E402
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from _refroot import reference_root  # noqa: E402
 
 WIDTHS = (16, 8, 4)
 SAMPLE_ROWS = 8
@@ -65,15 +68,14 @@ def _work(args):
 
 
 def main(argv):
-    ref = "/root/reference"
+    ref = None
     procs = 8
     args = list(argv)
     if "--procs" in args:
         i = args.index("--procs")
         procs = int(args[i + 1])
         del args[i:i + 2]
-    if args:
-        ref = args[0]
+    ref = reference_root(args[0] if args else None)
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     out = {"source": "reference src/sf/_vectorized.py OPS over every code pair",
            "fold": "row digests of superfloat.python_b200.sweep.fold_rows; sha256 of codes then flags, "

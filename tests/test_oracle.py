@@ -173,3 +173,29 @@ def test_sf16_product_closed_form_exhaustive_low_bits():
     a = rng.integers(0, 32768, 1 << 16)
     w = rng.integers(0, 32768, 1 << 16)
     assert (sfref.t16_closed(a, w) == sfref.mx_product16(a, w, u)).all()
+
+
+def test_oracle_wide_acc_equals_the_references_own_c_loop():
+    """The oracle's C accumulator (a bit-walk restatement) against the
+    reference's own compiled MX loop (oracle/_ref, built from the reference's
+    source string by oracle/build_ref.py) on random 2-D problems: every width's
+    block, both MX versions, full-range and clipping operands."""
+    from oracle import native
+    if not native.ref_available():
+        pytest.skip("oracle/_ref was not built (no reference tree in this container)")
+    rng = np.random.default_rng(41)
+    for mx in ("v4.9.2", "v4.8.1"):
+        for bits in (16, 13, 9, 8, 5, 4):
+            M_ = (1 << (bits - 1)) - 1
+            for (m, k, n) in ((23, 57, 19), (64, 300, 40), (8, 2400, 6)):
+                A = rng.integers(-M_, M_ + 1, (m, k))
+                B = rng.integers(-M_, M_ + 1, (k, n))
+                A[:2] = np.abs(A[:2])                    # same-sign rows clip for real
+                B[:, :2] = np.abs(B[:, :2])
+                got = native.wide_acc(bits, A, B, mx)
+                want = native.ref_wide_acc(bits, A, B, mx, threads=2)
+                np.testing.assert_array_equal(got[0], want[0], err_msg=f"sf{bits} {mx} {m}x{k}x{n}")
+                np.testing.assert_array_equal(got[1], want[1])
+                assert got[2] == want[2]
+                if k == 2400 and bits == 16:
+                    assert got[1][:2, :2].all()            # the accumulator's limit is reached
