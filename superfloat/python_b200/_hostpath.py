@@ -108,12 +108,15 @@ class PluginStager:
     set of pinned host buffers and device buffers allocated once and reused
     by every call.  Per chunk the host narrows the int64 operands into the
     slot's pinned int16 buffers (torch's threaded casting copy); the slot's
-    stream copies them in, runs the kernel and copies the int16 result and
-    the event bytes back; the host then widens them into the caller's int64
-    output and boolean masks.  With three slots the host's narrowing of one
+    stream copies them in, runs the kernel, splits the event byte into one
+    bool mask per event, and copies the int16 result and the masks back; the
+    host then widens the result into the caller's int64 output and copies
+    the masks into its boolean arrays.  With three slots the host's narrowing of one
     chunk and widening of another overlap the GPU's work on a third.  Status
     counts accumulate per slot on the device and are read once per call.
     One call at a time per stager (a lock)."""
+
+    MAX_EVENTS = 2                  # events an op reports (fma: overflow, underflow)
 
     def __init__(self, dev, chunk: int = 1 << 22, slots: int = 3):
         import threading
@@ -121,15 +124,18 @@ class PluginStager:
         self.dev = dev
         self.chunk = chunk
         d = dev.torch_device
+        E = self.MAX_EVENTS
         self.streams = [torch.cuda.Stream(device=d) for _ in range(slots)]
         self.done = [torch.cuda.Event() for _ in range(slots)]
         self.h_in = [[torch.empty(chunk, dtype=torch.int16, pin_memory=True) for _ in range(3)]
                      for _ in range(slots)]
         self.h_out = [torch.empty(chunk, dtype=torch.int16, pin_memory=True) for _ in range(slots)]
-        self.h_fl = [torch.empty(chunk, dtype=torch.uint8, pin_memory=True) for _ in range(slots)]
+        self.h_mask = [torch.empty(E, chunk, dtype=torch.bool, pin_memory=True) for _ in range(slots)]
         self.d_in = [[torch.empty(chunk, dtype=torch.int16, device=d) for _ in range(3)] for _ in range(slots)]
         self.d_out = [torch.empty(chunk, dtype=torch.int16, device=d) for _ in range(slots)]
         self.d_fl = [torch.empty(chunk, dtype=torch.uint8, device=d) for _ in range(slots)]
+        self.d_mask = [torch.empty(E, chunk, dtype=torch.bool, device=d) for _ in range(slots)]
+        self.d_tmp = [torch.empty(chunk, dtype=torch.uint8, device=d) for _ in range(slots)]
         self.counts = torch.zeros(slots, _lib.N_COUNTS, dtype=torch.int64, device=d)
         self.lock = threading.Lock()
 
@@ -155,14 +161,17 @@ class PluginStager:
                 st.wait_stream(cur)
             pending = []
 
+            evs = list(t_masks)
+            if len(evs) > self.MAX_EVENTS:
+                raise ValueError(f"{op} reports {len(evs)} events; the stager carries {self.MAX_EVENTS}")
+
             def finish(item):
                 slot, lo, hi = item
                 m = hi - lo
                 self.done[slot].synchronize()
                 t_codes[lo:hi].copy_(self.h_out[slot][:m])                 # int16 -> int64
-                fl = self.h_fl[slot][:m]
-                for e, mk in t_masks.items():
-                    torch.ne(torch.bitwise_and(fl, event_bits[e]), 0, out=mk[lo:hi])
+                for i, e in enumerate(evs):
+                    t_masks[e][lo:hi].copy_(self.h_mask[slot][i, :m])       # bool bytes, a plain copy
 
             for k, lo in enumerate(range(0, n, self.chunk)):
                 hi = min(n, lo + self.chunk)
@@ -183,7 +192,13 @@ class PluginStager:
                     _lib.elementwise(op, bits, din[0][:m], b, c, self.d_out[slot][:m], self.d_fl[slot][:m],
                                      self.counts[slot], pow_n=pow_n, stream=st)
                     self.h_out[slot][:m].copy_(self.d_out[slot][:m], non_blocking=True)
-                    self.h_fl[slot][:m].copy_(self.d_fl[slot][:m], non_blocking=True)
+                    # each event's mask as bool bytes, split from the event byte on the device
+                    for i, e in enumerate(evs):
+                        tmp = self.d_tmp[slot][:m]
+                        torch.bitwise_and(self.d_fl[slot][:m], event_bits[e], out=tmp)
+                        torch.ne(tmp, 0, out=self.d_mask[slot][i, :m])
+                    for i in range(len(evs)):
+                        self.h_mask[slot][i, :m].copy_(self.d_mask[slot][i, :m], non_blocking=True)
                     self.done[slot].record(st)
                 pending.append((slot, lo, hi))
             while pending:

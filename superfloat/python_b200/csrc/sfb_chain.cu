@@ -49,6 +49,7 @@
 // underflow word is clear.  A 384-thread CTA owns a 192 x 128 tile, 8 rows x
 // 4 lane pairs per thread, one CTA per SM.
 #include <algorithm>
+#include <type_traits>
 
 #include "sfb_common.cuh"
 
@@ -71,6 +72,15 @@ union Pack8 {
     uint4 u;
     int16_t h[8];
 };
+
+union Pack4 {
+    uint2 u;
+    int16_t h[4];
+};
+
+// V int16 codes loaded as one vector: 16 bytes (V = 8) or 8 bytes (V = 4)
+template <int V>
+using PackV = typename std::conditional<V == 8, Pack8, Pack4>::type;
 
 struct Epi {
     const int16_t *bias;      // nullable, N codes
@@ -104,9 +114,11 @@ __device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, 
 }
 
 // TM rows per thread: 8 when the clip is proven unnecessary, 4 with the
-// per-step clip and overflow tracking, to stay within registers.  NT threads:
-// 256 (BM = 16 TM rows per CTA), or 128 (BM = 8 TM) so that small problems
-// still spread over the SMs.
+// per-step clip and overflow tracking, to stay within registers, and 2 for
+// problems so small that even 32-row tiles leave SMs idle (twice the warps
+// per output tile, to hide the shared-memory and dependency latencies).  NT
+// threads: 256 (BM = 16 TM rows per CTA), or 128 (BM = 8 TM) so that small
+// problems still spread over the SMs.
 template <bool SAFE, bool BITS16, int TM, int NT = THREADS>
 __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict__ A, const int16_t *__restrict__ B,
                                                            int M, int N, int K, int64_t lda, int64_t ldb, int64_t sa,
@@ -134,24 +146,26 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
 
     // loader roles.  A: PER = 32 / (NT / BM) k of one row per thread; B: 8
     // columns of BPASS k rows per thread.  16-byte loads when the rows are aligned.
-    constexpr int TPR = NT / BM;               // threads per A row: 2 or 4
-    constexpr int PER = BK / TPR;              // k per thread: 16 or 8
+    constexpr int TPR = NT / BM;               // threads per A row: 2, 4 or 8
+    constexpr int PER = BK / TPR;              // k per thread: 16, 8 or 4
+    constexpr int AV = PER < 8 ? PER : 8;      // codes per A vector load
     constexpr int BROWS = NT / 8, BPASS = BK / BROWS;
-    static_assert(PER % 8 == 0 && BPASS * BROWS == BK, "chain2 loader shape");
+    static_assert(PER % AV == 0 && (AV == 8 || AV == 4) && BPASS * BROWS == BK, "chain2 loader shape");
     const int ar = tid / TPR, ah = tid % TPR;
     const int bk = tid >> 3, bc = (tid & 7) * 8;
-    Pack8 ra[PER / 8], rb[BPASS];
+    PackV<AV> ra[PER / AV];
+    Pack8 rb[BPASS];
     auto load_regs = [&](int k0) {
         const int gm = m0 + ar;
         const int ka = k0 + ah * PER;
 #pragma unroll
-        for (int q = 0; q < PER / 8; q++) {
-            const int kq = ka + q * 8;
-            if (vec && gm < M && kq + 8 <= K) {
-                ra[q].u = __ldg(reinterpret_cast<const uint4 *>(A + (int64_t)gm * lda + kq));
+        for (int q = 0; q < PER / AV; q++) {
+            const int kq = ka + q * AV;
+            if (vec && gm < M && kq + AV <= K) {
+                ra[q].u = __ldg(reinterpret_cast<const decltype(ra[q].u) *>(A + (int64_t)gm * lda + kq));
             } else {
 #pragma unroll
-                for (int j = 0; j < 8; j++)
+                for (int j = 0; j < AV; j++)
                     ra[q].h[j] = (gm < M && kq + j < K) ? A[(int64_t)gm * lda + kq + j] : (int16_t)0;
             }
         }
@@ -170,11 +184,11 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
     auto store_regs = [&](Stage<BM> &s) {
         uint32_t bits = 0;
 #pragma unroll
-        for (int q = 0; q < PER / 8; q++)
+        for (int q = 0; q < PER / AV; q++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < AV; j++) {
                 const int v = ra[q].h[j];
-                const int kk = ah * PER + q * 8 + j;
+                const int kk = ah * PER + q * AV + j;
                 s.a_abs[kk][ar] = (uint32_t)abs(v);
                 s.a_sgn[kk][ar] = v >> 31;
                 bits |= (uint32_t)(v < 0) << kk;
@@ -212,12 +226,20 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
         for (int k = 0; k < BK; k++) {
             uint32_t aa[TM];
             int32_t as_[TM];
+            if constexpr (TM >= 4) {
 #pragma unroll
-            for (int q = 0; q < TM / 4; q++) {
-                const uint4 av = *reinterpret_cast<const uint4 *>(&cur.a_abs[k][ty * TM + 4 * q]);
-                const int4 sv = *reinterpret_cast<const int4 *>(&cur.a_sgn[k][ty * TM + 4 * q]);
-                aa[4 * q] = av.x, aa[4 * q + 1] = av.y, aa[4 * q + 2] = av.z, aa[4 * q + 3] = av.w;
-                as_[4 * q] = sv.x, as_[4 * q + 1] = sv.y, as_[4 * q + 2] = sv.z, as_[4 * q + 3] = sv.w;
+                for (int q = 0; q < TM / 4; q++) {
+                    const uint4 av = *reinterpret_cast<const uint4 *>(&cur.a_abs[k][ty * TM + 4 * q]);
+                    const int4 sv = *reinterpret_cast<const int4 *>(&cur.a_sgn[k][ty * TM + 4 * q]);
+                    aa[4 * q] = av.x, aa[4 * q + 1] = av.y, aa[4 * q + 2] = av.z, aa[4 * q + 3] = av.w;
+                    as_[4 * q] = sv.x, as_[4 * q + 1] = sv.y, as_[4 * q + 2] = sv.z, as_[4 * q + 3] = sv.w;
+                }
+            } else {
+                static_assert(TM == 2, "two rows per thread");
+                const uint2 av = *reinterpret_cast<const uint2 *>(&cur.a_abs[k][ty * TM]);
+                const int2 sv = *reinterpret_cast<const int2 *>(&cur.a_sgn[k][ty * TM]);
+                aa[0] = av.x, aa[1] = av.y;
+                as_[0] = sv.x, as_[1] = sv.y;
             }
             const uint4 bv = *reinterpret_cast<const uint4 *>(&cur.b_abs[k][tx * TN]);
             const int4 bs = *reinterpret_cast<const int4 *>(&cur.b_sgn[k][tx * TN]);
@@ -742,6 +764,21 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
         return check_launch(what);
     }
     const bool b16 = bits == 16;
+    if (batch * ((M + 31) / 32) * nt < (int64_t)sm_count()) {
+        // so few outputs that 32 x 64 tiles would not give every SM one: 16 x 64 tiles
+        // on 128-thread CTAs, two rows per thread
+        const dim3 g1((unsigned)nt, (unsigned)((M + 15) / 16), (unsigned)batch);
+        const int smem = 2 * (int)sizeof(Stage<16>);
+        auto kern = b16 ? chain2_kernel<false, true, 2, 128> : chain2_kernel<false, false, 2, 128>;
+        static unsigned long long attr_t[64][2] = {};
+        if (ctx == 0 || attr_t[dev][b16] != ctx) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+                return check_launch(what);
+            attr_t[dev][b16] = context_id();
+        }
+        kern<<<g1, 128, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
+        return check_launch(what);
+    }
     if (batch * mt * nt < 2 * (int64_t)sm_count()) {
         // few 64 x 64 tiles: 32 x 64 tiles on 128-thread CTAs, twice the CTAs
         const dim3 g2((unsigned)nt, (unsigned)((M + 31) / 32), (unsigned)batch);
