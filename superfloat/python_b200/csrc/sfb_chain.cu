@@ -13,22 +13,24 @@
 // the result is dequantized in float64 as y = acc / 2^(N-1) * a * s[n]
 // (src/sf/torch/_core.py:381-382).
 //
-// Per product, on magnitudes |a|, |b| and sign masks sa, sb (0 or -1) kept
-// apart in shared memory:
-//     p = |a| |b|,  t = p >> (N-1),  x = t ^ sa ^ sb  (= t, or -t - 1 when negative)
-// so the signed step is x plus 1 for a negative product; those +1s are
-// counted per 32 k at once, popc(signword_a ^ signword_b).  Underflow is
-// tracked as the running minimum of p - 1 (unsigned): it dips below
-// 2^(N-1) - 1 exactly when some nonzero product is smaller than one unit.
-// When the caller has proven that no partial sum can saturate (the
-// reference's L1 bound; always the case under headroom="bound") the clip is
-// dropped and the chain is a plain sum, any order; otherwise every step
-// clips in k order and overflow is tracked per step.
+// Underflow is tracked as the running minimum of p - 1 (unsigned, p =
+// |a| |b|): it dips below 2^(N-1) - 1 exactly when some nonzero product is
+// smaller than one unit.  When the caller has proven that no partial sum can
+// saturate (the reference's L1 bound; always the case under
+// headroom="bound") the clip is dropped and the chain is a plain sum, any
+// order; otherwise every step clips in k order and overflow is tracked per
+// step.
 //
 // General mode (chain2_kernel): a 256-thread CTA owns a 64 x 64 output tile,
-// 4 x 4 outputs per thread; k-tiles of 32 staged through double-buffered
-// shared memory.  Zero padding past K is neutral (a 0 product changes
-// nothing, raises nothing).
+// 4 x 4 outputs per thread (or 128 threads on 32 x 64 / 16 x 64 tiles for
+// small problems); k-tiles of 32 staged through double-buffered shared
+// memory as |a|, |a| << (32 - (N-1)), sign(a) = +-1, |b|, sign(b) = +-1.  A
+// step is t = umulhi(|a| << (32 - (N-1)), |b|) (the truncated magnitude),
+// the underflow minimum of |a| |b| - 1, s = t (sa sb) + acc: four IMADs on
+// the FMA pipe; and the clip to [-M, M] (two min / max) and the overflow OR
+// of s ^ clip(s) on the ALU pipe, which the clip in k order keeps serial.
+// Zero padding past K is neutral (a 0 product changes nothing, raises
+// nothing).
 //
 // Proven mode (chain_pk_kernel): every partial sum stays within [-M, M], so
 // two outputs (n, n+1) share one 32-bit accumulator as two 16-bit lanes and
@@ -113,23 +115,37 @@ __device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, 
     cnt.under += un;
 }
 
-// TM rows per thread: 8 when the clip is proven unnecessary, 4 with the
-// per-step clip and overflow tracking, to stay within registers, and 2 for
-// problems so small that even 32-row tiles leave SMs idle (twice the warps
-// per output tile, to hide the shared-memory and dependency latencies).  NT
-// threads: 256 (BM = 16 TM rows per CTA), or 128 (BM = 8 TM) so that small
-// problems still spread over the SMs.
-template <bool SAFE, bool BITS16, int TM, int NT = THREADS>
+// General-mode operands of one k-tile, kept apart so that each step is
+// multiplies on the FMA pipe and min / max / logic on the ALU pipe:
+//     t   = umulhi(|a| << (32 - (N-1)), |b|)   = trunc(|a| |b| / 2^(N-1))
+//     p-1 = |a| |b| - 1 (unsigned)              (the underflow minimum)
+//     s   = t * (sa sb) + acc                   (sa, sb = +-1)
+//     acc = clip(s, -M, M),  overflow |= s ^ acc
+template <int BM>
+struct GStage {
+    uint32_t a_abs[BK][BM];   // |a|
+    uint32_t a_hi[BK][BM];    // |a| << (32 - (N-1))
+    int32_t a_sgn[BK][BM];    // +1 or -1
+    uint32_t b_abs[BK][BN];
+    int32_t b_sgn[BK][BN];    // +1 or -1
+};
+
+// TM rows per thread: 4, or 2 for problems so small that even 32-row tiles
+// leave SMs idle (twice the warps per output tile).  NT threads: 256 (BM =
+// 16 TM rows per CTA), or 128 (BM = 8 TM) so that small problems still
+// spread over the SMs.
+template <bool BITS16, int TM, int NT = THREADS>
 __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict__ A, const int16_t *__restrict__ B,
                                                            int M, int N, int K, int64_t lda, int64_t ldb, int64_t sa,
                                                            int64_t sb, int64_t so, Width w0, Epi e, int vec,
                                                            sfb_counts *counts) {
     constexpr int BM = (NT / 16) * TM;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    Stage<BM> *st = reinterpret_cast<Stage<BM> *>(smem_raw);
+    GStage<BM> *st = reinterpret_cast<GStage<BM> *>(smem_raw);
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
     const Width w = BITS16 ? Width{16, 15, 32767} : w0;
+    const int hi_shift = 32 - w.sh;
     const int tid = threadIdx.x;
     const int tx = tid % (BN / TN), ty = tid / (BN / TN);
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
@@ -145,9 +161,9 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
         for (int j = 0; j < TN; j++) acc[i][j] = 0, um[i][j] = 0xFFFFFFFFu, ov[i][j] = 0;
 
     // loader roles.  A: PER = 32 / (NT / BM) k of one row per thread; B: 8
-    // columns of BPASS k rows per thread.  16-byte loads when the rows are aligned.
-    constexpr int TPR = NT / BM;               // threads per A row: 2, 4 or 8
-    constexpr int PER = BK / TPR;              // k per thread: 16, 8 or 4
+    // columns of BPASS k rows per thread.  Vector loads when the rows are aligned.
+    constexpr int TPR = NT / BM;               // threads per A row: 4 or 8
+    constexpr int PER = BK / TPR;              // k per thread: 8 or 4
     constexpr int AV = PER < 8 ? PER : 8;      // codes per A vector load
     constexpr int BROWS = NT / 8, BPASS = BK / BROWS;
     static_assert(PER % AV == 0 && (AV == 8 || AV == 4) && BPASS * BROWS == BK, "chain2 loader shape");
@@ -181,28 +197,25 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
             }
         }
     };
-    auto store_regs = [&](Stage<BM> &s) {
-        uint32_t bits = 0;
+    auto store_regs = [&](GStage<BM> &s) {
 #pragma unroll
         for (int q = 0; q < PER / AV; q++)
 #pragma unroll
             for (int j = 0; j < AV; j++) {
                 const int v = ra[q].h[j];
                 const int kk = ah * PER + q * AV + j;
-                s.a_abs[kk][ar] = (uint32_t)abs(v);
-                s.a_sgn[kk][ar] = v >> 31;
-                bits |= (uint32_t)(v < 0) << kk;
+                const uint32_t mag = (uint32_t)abs(v);
+                s.a_abs[kk][ar] = mag;
+                s.a_hi[kk][ar] = mag << hi_shift;
+                s.a_sgn[kk][ar] = v < 0 ? -1 : 1;
             }
-#pragma unroll
-        for (int o = 1; o < TPR; o <<= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
-        if (ah == 0) s.a_sw[ar] = bits;
 #pragma unroll
         for (int p = 0; p < BPASS; p++)
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int v = rb[p].h[j];
                 s.b_abs[bk + p * BROWS][bc + j] = (uint32_t)abs(v);
-                s.b_sgn[bk + p * BROWS][bc + j] = v >> 31;
+                s.b_sgn[bk + p * BROWS][bc + j] = v < 0 ? -1 : 1;
             }
     };
 
@@ -213,32 +226,29 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
     }
     __syncthreads();
     for (int kt = 0; kt < nk; kt++) {
-        Stage<BM> &cur = st[kt & 1];
-        if (tid < BN) {                       // column sign words of this k-tile
-            uint32_t bits = 0;
-#pragma unroll 8
-            for (int k = 0; k < BK; k++) bits |= (uint32_t)(cur.b_sgn[k][tid] & 1) << k;
-            cur.b_sw[tid] = bits;
-        }
+        GStage<BM> &cur = st[kt & 1];
         if (kt + 1 < nk) load_regs((kt + 1) * BK);
-        __syncthreads();
 #pragma unroll 2
         for (int k = 0; k < BK; k++) {
-            uint32_t aa[TM];
+            uint32_t aa[TM], ahi[TM];
             int32_t as_[TM];
             if constexpr (TM >= 4) {
 #pragma unroll
                 for (int q = 0; q < TM / 4; q++) {
                     const uint4 av = *reinterpret_cast<const uint4 *>(&cur.a_abs[k][ty * TM + 4 * q]);
+                    const uint4 hv = *reinterpret_cast<const uint4 *>(&cur.a_hi[k][ty * TM + 4 * q]);
                     const int4 sv = *reinterpret_cast<const int4 *>(&cur.a_sgn[k][ty * TM + 4 * q]);
                     aa[4 * q] = av.x, aa[4 * q + 1] = av.y, aa[4 * q + 2] = av.z, aa[4 * q + 3] = av.w;
+                    ahi[4 * q] = hv.x, ahi[4 * q + 1] = hv.y, ahi[4 * q + 2] = hv.z, ahi[4 * q + 3] = hv.w;
                     as_[4 * q] = sv.x, as_[4 * q + 1] = sv.y, as_[4 * q + 2] = sv.z, as_[4 * q + 3] = sv.w;
                 }
             } else {
                 static_assert(TM == 2, "two rows per thread");
                 const uint2 av = *reinterpret_cast<const uint2 *>(&cur.a_abs[k][ty * TM]);
+                const uint2 hv = *reinterpret_cast<const uint2 *>(&cur.a_hi[k][ty * TM]);
                 const int2 sv = *reinterpret_cast<const int2 *>(&cur.a_sgn[k][ty * TM]);
                 aa[0] = av.x, aa[1] = av.y;
+                ahi[0] = hv.x, ahi[1] = hv.y;
                 as_[0] = sv.x, as_[1] = sv.y;
             }
             const uint4 bv = *reinterpret_cast<const uint4 *>(&cur.b_abs[k][tx * TN]);
@@ -249,52 +259,31 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
             for (int i = 0; i < TM; i++)
 #pragma unroll
                 for (int j = 0; j < TN; j++) {
-                    const uint32_t p = aa[i] * ba[j];
-                    const int32_t t = (int32_t)(p >> w.sh);
-                    um[i][j] = min(um[i][j], p - 1u);
-                    if (SAFE) {
-                        acc[i][j] += t ^ as_[i] ^ bs_[j];             // + popc term below
-                    } else {
-                        const int32_t sg = as_[i] ^ bs_[j];
-                        const int32_t s = acc[i][j] + ((t ^ sg) - sg);
-                        const int32_t c = clampi(s, -w.M, w.M);
-                        ov[i][j] |= (uint32_t)(s ^ c);
-                        acc[i][j] = c;
-                    }
+                    const uint32_t t = __umulhi(ahi[i], ba[j]);
+                    um[i][j] = min(um[i][j], aa[i] * ba[j] + 0xFFFFFFFFu);
+                    const int32_t s = (int32_t)t * (as_[i] * bs_[j]) + acc[i][j];
+                    const int32_t c = clampi(s, -w.M, w.M);
+                    ov[i][j] |= (uint32_t)(s ^ c);
+                    acc[i][j] = c;
                 }
         }
-        if (SAFE) {
-#pragma unroll
-            for (int i = 0; i < TM; i++) {
-                const uint32_t sa_w = cur.a_sw[ty * TM + i];
-#pragma unroll
-                for (int j = 0; j < TN; j++) acc[i][j] += __popc(sa_w ^ cur.b_sw[tx * TN + j]);
-            }
-        }
+        // the other buffer was last read before the previous barrier
         if (kt + 1 < nk) store_regs(st[(kt + 1) & 1]);
         __syncthreads();
     }
 
     Counts cnt;
     const uint32_t unit_m1 = (1u << w.sh) - 1u;   // um < 2^(N-1) - 1  <=>  some 0 < p < 2^(N-1)
-    unsigned bad = 0;
 #pragma unroll
     for (int i = 0; i < TM; i++) {
         const int gm = m0 + ty * TM + i;
 #pragma unroll
         for (int j = 0; j < TN; j++) {
             const int gn = n0 + tx * TN + j;
-            if (gm < M && gn < N) {
-                int v = acc[i][j];
-                if (SAFE && (v > w.M || v < -w.M)) {           // the caller's proof did not hold
-                    bad++;
-                    v = clampi(v, -w.M, w.M);
-                }
-                emit(e, w, z * so + (int64_t)gm * N + gn, gn, v, ov[i][j] != 0, um[i][j] < unit_m1, cnt);
-            }
+            if (gm < M && gn < N)
+                emit(e, w, z * so + (int64_t)gm * N + gn, gn, acc[i][j], ov[i][j] != 0, um[i][j] < unit_m1, cnt);
         }
     }
-    if (SAFE && bad && counts) atomicAdd(&counts->reserved[1], (unsigned long long)bad);
     flush_counts(cnt, counts, sc);
 }
 
@@ -768,8 +757,8 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
         // so few outputs that 32 x 64 tiles would not give every SM one: 16 x 64 tiles
         // on 128-thread CTAs, two rows per thread
         const dim3 g1((unsigned)nt, (unsigned)((M + 15) / 16), (unsigned)batch);
-        const int smem = 2 * (int)sizeof(Stage<16>);
-        auto kern = b16 ? chain2_kernel<false, true, 2, 128> : chain2_kernel<false, false, 2, 128>;
+        const int smem = 2 * (int)sizeof(GStage<16>);
+        auto kern = b16 ? chain2_kernel<true, 2, 128> : chain2_kernel<false, 2, 128>;
         static unsigned long long attr_t[64][2] = {};
         if (ctx == 0 || attr_t[dev][b16] != ctx) {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -782,8 +771,8 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
     if (batch * mt * nt < 2 * (int64_t)sm_count()) {
         // few 64 x 64 tiles: 32 x 64 tiles on 128-thread CTAs, twice the CTAs
         const dim3 g2((unsigned)nt, (unsigned)((M + 31) / 32), (unsigned)batch);
-        const int smem = 2 * (int)sizeof(Stage<32>);
-        auto kern = b16 ? chain2_kernel<false, true, 4, 128> : chain2_kernel<false, false, 4, 128>;
+        const int smem = 2 * (int)sizeof(GStage<32>);
+        auto kern = b16 ? chain2_kernel<true, 4, 128> : chain2_kernel<false, 4, 128>;
         static unsigned long long attr_s[64][2] = {};
         if (ctx == 0 || attr_s[dev][b16] != ctx) {
             if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -793,8 +782,8 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
         kern<<<g2, 128, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
         return check_launch(what);
     }
-    const int smem = 2 * (int)sizeof(Stage<64>);
-    auto kern = b16 ? chain2_kernel<false, true, 4> : chain2_kernel<false, false, 4>;
+    const int smem = 2 * (int)sizeof(GStage<64>);
+    auto kern = b16 ? chain2_kernel<true, 4> : chain2_kernel<false, 4>;
     if (ctx == 0 || attr[dev][b16] != ctx) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return check_launch(what);
