@@ -38,21 +38,12 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
     zero_counts_smem(sc);
     const int M = w.M, n = 2 * w.M + 1;
     const int r0 = a_lo + blockIdx.x * RB;
-    // A digest sum_j x_j w_j (mod 2^64) with 0 <= x_j < 2^16 is accumulated as
-    // sum_j x_j w_lo(j) in 64 bits plus 2^32 sum_j x_j w_hi(j) in 32 bits: two
-    // 32 x 32 multiply-adds per term.  The code digest adds the code biased by
-    // M (k + M >= 0) and takes M sum_j w_j off at the end, so the digests are
-    // those of sum_j k_j w_j and sum_j flags_j w_j exactly.
-    unsigned long long lc[RB], lf[RB];
-    uint32_t hc[RB], hf[RB];
+    unsigned long long dc[RB], df[RB];
 #pragma unroll
-    for (int r = 0; r < RB; r++) lc[r] = lf[r] = 0, hc[r] = hf[r] = 0;
-    unsigned long long wsum = 0;
+    for (int r = 0; r < RB; r++) dc[r] = 0, df[r] = 0;
     Counts cnt;
     for (int j = threadIdx.x; j < n; j += SW_THREADS) {
         const unsigned long long wj = splitmix64((unsigned long long)j);
-        const uint32_t wlo = (uint32_t)wj, whi = (uint32_t)(wj >> 32);
-        wsum += wj;
         const int b = j - M;
 #pragma unroll
         for (int r = 0; r < RB; r++) {
@@ -60,20 +51,11 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
             if (a < a_hi) {
                 Ev ev;
                 const int k = ew_one<OP, BITS>(a, b, 0, w, 0, ev);
-                const uint32_t kb = (uint32_t)(k + M), fb = flag_byte(ev);
-                lc[r] += (unsigned long long)kb * wlo;
-                hc[r] += kb * whi;
-                lf[r] += (unsigned long long)fb * wlo;
-                hf[r] += fb * whi;
+                dc[r] += (unsigned long long)(long long)k * wj;
+                df[r] += (unsigned long long)flag_byte(ev) * wj;
                 tally(cnt, ev);
             }
         }
-    }
-    unsigned long long dc[RB], df[RB];
-#pragma unroll
-    for (int r = 0; r < RB; r++) {
-        dc[r] = lc[r] + ((unsigned long long)hc[r] << 32) - (unsigned long long)M * wsum;
-        df[r] = lf[r] + ((unsigned long long)hf[r] << 32);
     }
     const int lane = threadIdx.x & 31;
 #pragma unroll
