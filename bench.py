@@ -560,6 +560,8 @@ def main():
         d2h = sum(2 * n + 8 * _lib.N_COUNTS for op in OPS)
         line["e2e"] = {"value": len(OPS) * n * world * e2e_steps / dt / 1e9, "unit": "Gelem/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "copy_GBps_per_rank": {"h2d": h2d * e2e_steps / dt / 1e9, "d2h": d2h * e2e_steps / dt / 1e9},
+                       "copy_GBps_all_ranks": (h2d + d2h) * e2e_steps * world / dt / 1e9,
                        "path": "int16 codes in pinned host memory -> chunked H2D / sfb_elementwise / D2H on two "
                                "streams, status counts read back every op"}
         # the reference's Device.run contract: int64 NumPy codes in, int64 codes + boolean masks out,
