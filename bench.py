@@ -737,63 +737,60 @@ def bench_matmuls(dev, fmt, torch, n=8192, rank=0, world=1, dist=None):
     return res
 
 
-def bench_wide_prepared(torch, tB, n, rank, world, dist, want_sha):
-    """The wide n^3 matmul with B prepared once (a replicated, static
-    operand: the reference's prepared weight), its output rows gathered on
-    every rank while the next rows compute.  Rows go to ranks block-cyclically
-    in ``parts`` pieces of P rows (piece j of rank r = global rows
-    [(j world + r) P, (j world + r + 1) P)), so the all-gather of piece j lands
-    contiguously, in global order, in rows [j world P, (j + 1) world P) of the
-    full output, with no copy; it runs on NCCL's stream beside piece j + 1's
-    kernels.  ``ms`` = compute + gather, CUDA events, max over ranks."""
+def bench_wide_prepared(torch, tB, n, rank, world, dist, want_sha, reps=4):
+    """The wide n^3 matmul as a serving loop would run it: B prepared once
+    (a replicated, static operand: the reference's prepared weight), calls
+    back to back, each call's output rows all-gathered on NCCL's stream while
+    the next call computes (two output buffers).  Rows are split evenly over
+    the ranks.  ``ms`` = time per call over ``reps`` calls, the last call's
+    gather included: CUDA events, max over ranks."""
     import hashlib
     from superfloat.python_b200 import _lib, _shard, workloads
-    parts = 2 if world > 1 else 1
-    if n % (world * parts):
+    if n % world:
         return None
-    P = n // (world * parts)
+    P = n // world
     dev = tB.device
     A, _ = workloads.wide_square(n, n, n, 0)
-    rows = np.concatenate([A[lo:hi] for lo, hi in _shard.cyclic_pieces(n, world, parts, rank)])
+    tA = torch.from_numpy(A[rank * P:(rank + 1) * P]).to(torch.int16).to(dev)
     del A
-    tA = torch.from_numpy(rows).to(torch.int16).to(dev)
     prep = torch.empty(_lib.wide_prepared_b_bytes(16, "v4.9.2", n, n), dtype=torch.uint8, device=dev)
     _lib.wide_prepare_b(16, "v4.9.2", tB, n, n, n, prep)
     ws = torch.empty(_lib.wide_workspace(16, "v4.9.2", 1, P, n, n), dtype=torch.uint8, device=dev)
-    loc = torch.empty(parts, P, n, dtype=torch.int16, device=dev)
-    full = torch.empty(n, n, dtype=torch.int16, device=dev)
+    loc = torch.empty(2, P, n, dtype=torch.int16, device=dev)
+    full = torch.empty(2, n, n, dtype=torch.int16, device=dev)
     cnt = torch.zeros(8, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream()
 
-    def step():
+    def calls(k):
         works = []
-        for j in range(parts):
-            _lib.matmul_wide_prepared(16, "v4.9.2", tA[j * P:(j + 1) * P], tB, prep, None, 0, loc[j], None, cnt, 1,
-                                      P, n, n, n, n, 0, P * n, 0, 0, 0, ws)
-            works.append(_shard.gather_piece(full, loc[j], j, dist, world, async_op=True))
-        for w in works:
+        for i in range(k):
+            b = i & 1
+            if len(works) >= 2 and works[-2] is not None:
+                works[-2].wait()                  # this buffer's previous gather has finished
+            _lib.matmul_wide_prepared(16, "v4.9.2", tA, tB, prep, None, 0, loc[b], None, cnt, 1, P, n, n, n, n,
+                                      0, P * n, 0, 0, 0, ws)
+            works.append(_shard.gather_piece(full[b], loc[b], 0, dist, world, async_op=True))
+        for w in works[-2:]:
             if w is not None:
                 w.wait()
 
-    for _ in range(2):
-        step()
+    calls(2)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 3
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0.record(stream)
-    for _ in range(reps):
-        step()
+    calls(reps)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = _shard.max_over_ranks(e0.elapsed_time(e1) / reps, "cuda", dist, world)
     _lib.check_counts(cnt.cpu().numpy())
     out = {"ms": ms, "TOPS": 2 * n ** 3 / (ms / 1e3) / 1e12, "unit": "sf16 TOPS (2*M*N*K/s)",
-           "includes": "compute and the all-gather of the output rows (overlapped); B prepared once, outside",
-           "sharding": f"rows of A block-cyclic over {world} GPU(s) in {parts} piece(s) of {P} rows, B replicated"}
+           "includes": f"{reps} calls back to back, each with its output rows all-gathered on every rank "
+                       "beside the next call's compute (the last gather included); B prepared once, outside",
+           "sharding": f"rows of A over {world} GPU(s), {P} rows each, B replicated"}
     if rank == 0:
-        sha = hashlib.sha256(full.cpu().numpy().astype("<i2").tobytes()).hexdigest()[:16]
+        sha = hashlib.sha256(full[(reps - 1) & 1].cpu().numpy().astype("<i2").tobytes()).hexdigest()[:16]
         out["codes_sha256"] = sha
         out["codes_equal_unprepared"] = sha == want_sha if want_sha else None
     del tA, prep, ws, loc, full

@@ -159,7 +159,7 @@ def test_wide_accumulator_clips(gpu, rng):
 
 
 def test_wide_8192_workload_first_rows(gpu):
-    """The 8192^3 wide workload on the GPU; rows 0..15 against the reference's run."""
+    """The 8192^3 wide workload on the GPU; rows 0..511 against the reference's run."""
     import torch
     A, B = workloads.wide_square(8192, 8192, 8192, 0)
     o, cnt, fl = gpu.run_device("matmul_wide", FORMATS[16], gpu.upload(A), gpu.upload(B), flags=True, shift=0)
@@ -168,6 +168,14 @@ def test_wide_8192_workload_first_rows(gpu):
     f16 = fl[:16].cpu().numpy()
     assert sha_codes(o16) == r["codes"]
     assert sha_mask((f16 & 1) != 0) == r["overflow"] and sha_mask((f16 & 2) != 0) == r["underflow"]
+    # rows 0..511 in blocks of 16 against the reference's own compiled MX loop
+    wr = golden("wide_8192_rows512.json")
+    o512, f512 = o[:wr["rows"]].cpu().numpy(), fl[:wr["rows"]].cpu().numpy()
+    for b in wr["blocks"]:
+        r0, r1 = b["r0"], b["r0"] + wr["block"]
+        assert sha_codes(o512[r0:r1]) == b["codes"], r0
+        assert sha_mask((f512[r0:r1] & 1) != 0) == b["overflow"], r0
+        assert sha_mask((f512[r0:r1] & 2) != 0) == b["underflow"], r0
     cnt = cnt.cpu().numpy()
     frac = cnt[0] / (8192 * 8192)
     assert 0.005 < frac < 0.02 and cnt[4] == 0       # ~1% saturate, no accumulator clip

@@ -199,3 +199,10 @@ def test_oracle_wide_acc_equals_the_references_own_c_loop():
                 assert got[2] == want[2]
                 if k == 2400 and bits == 16:
                     assert got[1][:2, :2].all()            # the accumulator's limit is reached
+
+
+def test_wide_rows512_fixture_agrees_with_the_rows16_run():
+    """The 512-row fixture's first block is the 16-row run recorded before."""
+    a = golden("wide_8192_rows512.json")["blocks"][0]
+    b = golden("ref_runs.json")["wide_8192_rows16"]
+    assert a["codes"] == b["codes"] and a["overflow"] == b["overflow"] and a["underflow"] == b["underflow"]
