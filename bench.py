@@ -533,8 +533,7 @@ def main():
 
     # end to end: codes in pinned host memory, copies inside the timed region
     if not args.no_e2e:
-        from superfloat.python_b200._hostpath import HostPipeline
-        pipe = HostPipeline(dev)
+        from superfloat.python_b200._hostpath import HostPipeline, MultiOpPipeline
         hx = {}
         for name, v in (("x", x), ("y", y), ("z", z), ("d", d)):
             t = torch.empty(n, dtype=torch.int16, pin_memory=True)
@@ -542,28 +541,39 @@ def main():
             hx[name] = t
         hargs = {"add": ("x", "y"), "sub": ("x", "y"), "mul": ("x", "y"), "fma": ("x", "y", "z"), "div": ("x", "d")}
         hout = {op: torch.empty(n, dtype=torch.int16, pin_memory=True) for op in OPS}
-        for op in OPS:                               # warm-up of the host path
-            pipe.run(op, fmt, *(hx[a] for a in hargs[op]), out=hout[op])
         e2e_steps = max(1, min(5, args.steps))
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            for op in OPS:
-                pipe.run(op, fmt, *(hx[a] for a in hargs[op]), out=hout[op])   # returns after the counts are read
-        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev.torch_device)
-        if world > 1:
-            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-        dt = float(dt.item())
-        h2d = sum(2 * n * len(hargs[op]) for op in OPS)
-        d2h = sum(2 * n + 8 * _lib.N_COUNTS for op in OPS)
+
+        def timed_host(fn):
+            fn()                                         # warm-up of the host path
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(e2e_steps):
+                fn()                                     # returns after the counts are read
+            dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev.torch_device)
+            if world > 1:
+                dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+            return float(dt.item())
+
+        # the step's four operands copied in once per chunk, the five ops, the five results copied out
+        multi = MultiOpPipeline(dev, ("x", "y", "z", "d"), [(op, hargs[op]) for op in OPS])
+        dt = timed_host(lambda: multi.run(fmt, hx, [hout[op] for op in OPS]))
+        h2d = 4 * 2 * n
+        d2h = len(OPS) * (2 * n + 8 * _lib.N_COUNTS)
         line["e2e"] = {"value": len(OPS) * n * world * e2e_steps / dt / 1e9, "unit": "Gelem/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "copy_GBps_per_rank": {"h2d": h2d * e2e_steps / dt / 1e9, "d2h": d2h * e2e_steps / dt / 1e9},
                        "copy_GBps_all_ranks": (h2d + d2h) * e2e_steps * world / dt / 1e9,
-                       "path": "int16 codes in pinned host memory -> chunked H2D / sfb_elementwise / D2H on two "
-                               "streams, status counts read back every op"}
+                       "path": "int16 codes in pinned host memory -> MultiOpPipeline: per 8M-code chunk the four "
+                               "operands copied in once, add/sub/mul/fma/div on the device, the five results "
+                               "copied out, two streams; status counts read back every step"}
+        # each op with its own copies of its operands (HostPipeline, one call per op)
+        pipe = HostPipeline(dev)
+        dt1 = timed_host(lambda: [pipe.run(op, fmt, *(hx[a] for a in hargs[op]), out=hout[op]) for op in OPS])
+        line["e2e_inputs_per_op"] = {"value": len(OPS) * n * world * e2e_steps / dt1 / 1e9, "unit": "Gelem/s",
+                                     "h2d_bytes_per_step": sum(2 * n * len(hargs[op]) for op in OPS),
+                                     "path": "HostPipeline, one call per op: each op copies its own operands in"}
         # the reference's Device.run contract: int64 NumPy codes in, int64 codes + boolean masks out,
         # timed on every rank (each rank its own 2^26 elements) with its share of the host's cores
         xs = {"add": (x, y), "sub": (x, y), "mul": (x, y), "fma": (x, y, z), "div": (x, d)}
@@ -897,26 +907,30 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     ids = torch.randint(0, 50257, (batch, seq), generator=torch.Generator().manual_seed(0)).cuda()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def timed(fn):
+    per_rep = {}
+
+    def timed(fn, key):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
         torch.cuda.synchronize()
-        e0.record()
-        for _ in range(reps):
+        evs[0].record()
+        for i in range(reps):
             out = fn(ids)
-        e1.record()
+            evs[i + 1].record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / reps, out
+        per_rep[key] = [round(evs[i].elapsed_time(evs[i + 1]), 2) for i in range(reps)]
+        return evs[0].elapsed_time(evs[-1]) / reps, out
 
     torch._dynamo.reset()
     with torch.no_grad(), warnings.catch_warnings():
         warnings.simplefilter("ignore")
         eager_logits = model(ids).logits                  # prepares the weights (cached per weight)
         model(ids)
-        eager_ms, _ = timed(model)
+        eager_ms, _ = timed(model, "eager")
         n_rep = len(sft.compile_reports())
         compiled = torch.compile(model, backend="superfloat")
         compiled(ids)                                     # traces and compiles
         compiled(ids)
-        ms, out = timed(compiled)
+        ms, out = timed(compiled, "compiled")
     reps_new = sft.compile_reports()[n_rep:]
     same = bool(torch.equal(out.logits, eager_logits))
     torch._dynamo.reset()
@@ -925,7 +939,7 @@ def bench_gpt2(torch, batch=8, seq=512, reps=3, accumulate="chain"):
     st = sft.last_status(model)
     return {"ms_per_forward": ms, "tokens_per_s": R / (ms / 1e3), "sf_layers": len(st),
             "sf16_TOPS": 2 * products / (ms / 1e3) / 1e12, "saturated": sum(v.saturated or 0 for v in st.values()),
-            "eager_ms_per_forward": eager_ms, "compiled_equals_eager": same,
+            "eager_ms_per_forward": eager_ms, "compiled_equals_eager": same, "ms_per_rep": per_rep,
             "sf_op_nodes_on_device": sum(len(r.on_device) for r in reps_new),
             "sf_op_nodes_host_emulated": sum(len(r.host_emulated) for r in reps_new), "graphs": len(reps_new),
             "workload": f"GPT-2-small sft.convert(sf16, accumulate={accumulate!r}) forward through "

@@ -100,6 +100,59 @@ class HostPipeline:
         return res
 
 
+class MultiOpPipeline:
+    """Several elementwise ops over the same host-resident operands (int16
+    codes in pinned host memory), chunked over two streams: per chunk each
+    distinct operand is copied in once, every op runs on it, and every
+    result is copied back, so an operand that several ops read crosses PCIe
+    once per chunk.  One chunk's copies overlap the other stream's kernels,
+    and the copy engines run both directions at once.  Status counts
+    accumulate per op on the device and are read once at the end."""
+
+    def __init__(self, dev, names, ops, chunk: int = 1 << 23, slots: int = 2):
+        import torch
+        self.dev = dev
+        self.chunk = chunk
+        self.names = list(names)                 # operand names
+        self.ops = list(ops)                     # (op, (operand names...)) in run order
+        d = dev.torch_device
+        self.streams = [torch.cuda.Stream(device=d) for _ in range(slots)]
+        self.ins = [{nm: torch.empty(chunk, dtype=torch.int16, device=d) for nm in self.names}
+                    for _ in range(slots)]
+        self.outs = [[torch.empty(chunk, dtype=torch.int16, device=d) for _ in self.ops] for _ in range(slots)]
+        self.counts = torch.zeros(slots, len(self.ops), _lib.N_COUNTS, dtype=torch.int64, device=d)
+
+    def run(self, fmt, inputs: dict, outputs: list):
+        """``outputs[i][j] = ops[i](inputs...)[j]`` for host int16 tensors of
+        one length (pinned for the copies to overlap).  Returns the event
+        counts per op (numpy int64[ops, 8])."""
+        import torch
+        n = inputs[self.names[0]].numel()
+        self.counts.zero_()
+        cur = torch.cuda.current_stream(self.dev.torch_device)
+        for st in self.streams:
+            st.wait_stream(cur)
+        for k, (lo, hi) in enumerate(cuts(n, self.chunk)):
+            m = hi - lo
+            slot = k % len(self.streams)
+            st = self.streams[slot]
+            with torch.cuda.stream(st):
+                dev_in = {nm: self.ins[slot][nm][:m] for nm in self.names}
+                for nm in self.names:
+                    dev_in[nm].copy_(inputs[nm][lo:hi], non_blocking=True)
+                for i, (op, args) in enumerate(self.ops):
+                    xs = [dev_in[a] for a in args] + [None] * (3 - len(args))
+                    o = self.outs[slot][i][:m]
+                    _lib.elementwise(op, fmt.bits, xs[0], xs[1], xs[2], o, None, self.counts[slot, i], stream=st)
+                    outputs[i][lo:hi].copy_(o, non_blocking=True)
+        for st in self.streams:
+            cur.wait_stream(st)
+        res = self.counts.sum(0).cpu().numpy()
+        for c in res:
+            _lib.check_counts(c)
+        return res
+
+
 class PluginStager:
     """The ``Device.run`` contract (int64 NumPy codes in, int64 codes and
     boolean event masks out) for large equal-shape elementwise calls.

@@ -202,3 +202,28 @@ def test_device_run_stages_large_calls(gpu):
         for e, m in ev.items():
             np.testing.assert_array_equal(masks[e], np.broadcast_to(m, got.shape))
     assert gpu._stager is not None
+
+
+def test_multi_op_pipeline_equals_the_oracle(gpu, rng):
+    """Several ops over shared host operands, each operand copied in once per
+    chunk (small chunks: several per call, both streams): every result and
+    every op's counts equal the oracle, twice in a row."""
+    import torch
+    from superfloat.python_b200._hostpath import MultiOpPipeline
+    n = 5 * (1 << 12) + 3
+    vals = {nm: edge_codes(16, n, rng) for nm in ("x", "y", "z")}
+    ops = [("add", ("x", "y")), ("div", ("y", "x")), ("fma", ("x", "y", "z")), ("neg", ("z",)), ("mul", ("z", "x"))]
+    pipe = MultiOpPipeline(gpu, ("x", "y", "z"), ops, chunk=1 << 12)
+    hin = {}
+    for nm, v in vals.items():
+        t = torch.empty(n, dtype=torch.int16, pin_memory=True)
+        t.copy_(torch.from_numpy(v))
+        hin[nm] = t
+    for _ in range(2):
+        outs = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in ops]
+        counts = pipe.run(FORMATS[16], hin, outs)
+        for i, (op, args) in enumerate(ops):
+            want, ev = sfref.ew(op, 16, *(vals[a] for a in args))
+            np.testing.assert_array_equal(outs[i].numpy(), want, err_msg=op)
+            for j, e in enumerate(("overflow", "underflow", "divide", "invalid")):
+                assert int(counts[i][j]) == int(np.count_nonzero(ev.get(e, False))), (op, e)
