@@ -567,7 +567,7 @@ def main():
                        "copy_GBps_all_ranks": (h2d + d2h) * e2e_steps * world / dt / 1e9,
                        "path": "int16 codes in pinned host memory -> MultiOpPipeline: per 8M-code chunk the four "
                                "operands copied in once, add/sub/mul/fma/div on the device, the five results "
-                               "copied out, two streams; status counts read back every step"}
+                               "copied out, four streams; status counts read back every step"}
         # each op with its own copies of its operands (HostPipeline, one call per op)
         pipe = HostPipeline(dev)
         dt1 = timed_host(lambda: [pipe.run(op, fmt, *(hx[a] for a in hargs[op]), out=hout[op]) for op in OPS])

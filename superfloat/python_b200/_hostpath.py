@@ -109,7 +109,7 @@ class MultiOpPipeline:
     and the copy engines run both directions at once.  Status counts
     accumulate per op on the device and are read once at the end."""
 
-    def __init__(self, dev, names, ops, chunk: int = 1 << 23, slots: int = 2):
+    def __init__(self, dev, names, ops, chunk: int = 1 << 23, slots: int = 4):
         import torch
         self.dev = dev
         self.chunk = chunk
@@ -171,7 +171,7 @@ class PluginStager:
 
     MAX_EVENTS = 2                  # events an op reports (fma: overflow, underflow)
 
-    def __init__(self, dev, chunk: int = 1 << 22, slots: int = 3):
+    def __init__(self, dev, chunk: int = 1 << 23, slots: int = 4):
         import threading
         import torch
         self.dev = dev
