@@ -980,6 +980,36 @@ Layout layout_for(int64_t M, int64_t N, int64_t K) {
 
 // The calling thread's wait settings for the GEMM launches it makes
 // (sfb_wide_wait_limit): 0 polls = kSpinLimit, and the stall test off.
+// The GEMM runs on a second stream beside the remainder kernel (they read
+// the prepared planes and write different outputs; the finish kernel waits
+// for both), so that each kernel's last, partly filled wave overlaps the
+// other's work.  One such stream and its two events per host thread and
+// device, made again when the device's context changes.  The no-allocation
+// entry point launches everything on the caller's stream (t_serial).
+struct SideStream {
+    unsigned long long ctx;
+    cudaStream_t s;
+    cudaEvent_t fork, join;
+};
+thread_local SideStream t_side[64] = {};
+thread_local bool t_serial = false;
+
+SideStream *side_stream(int dev) {
+    const unsigned long long ctx = context_id();
+    SideStream &ss = t_side[dev];
+    if (ss.s != nullptr && ctx != 0 && ss.ctx == ctx) return &ss;
+    ss = SideStream{};
+    if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+        (void)cudaGetLastError();
+        ss = SideStream{};
+        return nullptr;
+    }
+    ss.ctx = context_id();
+    return &ss;
+}
+
 thread_local unsigned t_wait_polls = 0;
 thread_local int t_wait_stall = 0;
 
@@ -1149,10 +1179,18 @@ int wide_tc_try(int bits, int mx, const int16_t *A, const int16_t *B, const int8
         in.u = mx_unit(mx, true);
         in.counts = counts;
         in.U = reinterpret_cast<uint16_t *>(base + L.off_u);
-        tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), GEMM_THREADS, GEMM_SMEM, st>>>(
+        SideStream *side = t_serial ? nullptr : side_stream(dev);
+        cudaStream_t gst = st;
+        if (side && cudaEventRecord(side->fork, st) == cudaSuccess &&
+            cudaStreamWaitEvent(side->s, side->fork, 0) == cudaSuccess)
+            gst = side->s;
+        tc_gemm_kernel<<<dim3((unsigned)((L.Np + GN - 1) / GN), (unsigned)(L.Mp / TILE)), GEMM_THREADS, GEMM_SMEM, gst>>>(
             tmA, tmB, (int)(L.Kp / TILE), SX, (int)L.Np, &counts->reserved[0], t_wait_polls ? t_wait_polls : kSpinLimit,
             t_wait_stall);
         wide_rem_kernel<<<dim3((unsigned)(L.Np / (RNW * 32)), (unsigned)(L.Mp / RM)), 256, REM_SMEM, st>>>(in);
+        if (gst != st &&
+            (cudaEventRecord(side->join, gst) != cudaSuccess || cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess))
+            return check_launch("sfb_matmul_wide (stream join)");
         const int64_t fx = (N + 255) / 256;
         const dim3 fgrid((unsigned)fx, (unsigned)std::max<int64_t>(1, std::min<int64_t>(M, (int64_t)sm_count() * 8 / fx)));
         wide_tc_finish_kernel<<<fgrid, 256, 0, st>>>(in);
@@ -1258,7 +1296,10 @@ extern "C" int sfb_matmul_wide_noalloc(int bits, int mx, const int16_t *A, const
                          "sfb_matmul_wide_noalloc: %lld x %lld x %lld needs %lld bytes of scratch, more than the "
                          "%lld this entry point holds; use sfb_matmul_wide with a workspace",
                          (long long)M, (long long)N, (long long)K, (long long)need, (long long)kNoAllocScratchBytes);
-    return sfb_matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a,
-                           stride_b, stride_out, shift_sb, shift_sm, shift_sn, ptr, kNoAllocScratchBytes, counts,
-                           stream);
+    sfb::t_serial = true;                // everything on the caller's stream: no stream or event is made
+    const int rc = sfb_matmul_wide(bits, mx, A, B, shift_arr, shift, out, flags, batch, M, N, K, lda, ldb, stride_a,
+                                   stride_b, stride_out, shift_sb, shift_sm, shift_sn, ptr, kNoAllocScratchBytes,
+                                   counts, stream);
+    sfb::t_serial = false;
+    return rc;
 }
