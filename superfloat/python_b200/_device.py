@@ -19,6 +19,7 @@ use.  A maintainer adds it to the reference's own runtime with
 from __future__ import annotations
 
 import threading
+import warnings
 
 import numpy as np
 
@@ -149,7 +150,9 @@ class B200Device(Device):
     def upload(self, codes: np.ndarray):
         """int64 host codes -> int16 device tensor (same shape)."""
         torch = self._ready()
-        host = torch.from_numpy(np.ascontiguousarray(codes)).to(torch.int16)
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")          # a read-only caller array: it is only read here
+            host = torch.from_numpy(np.ascontiguousarray(codes)).to(torch.int16)
         return host.pin_memory().to(self.torch_device, non_blocking=True)
 
     # --- device-resident execution ---------------------------------------------------------
