@@ -810,7 +810,7 @@ def bench_wide_prepared(torch, tB, n, rank, world, dist, want_sha, reps=4):
 def bench_sweep(torch, dist, rank, world, bits=16):
     """Every sf16 code pair through add, sub, mul and div (4 x 65535^2 =
     1.7e10 pairs), the a-rows split evenly over the ranks; each row folds
-    into two 64-bit digests on the device.  Device time is the max over
+    into one 32-bit digest on the device.  Device time is the max over
     ranks; rank 0 gathers the row digests and checks their sha256 against
     the reference's (tests/golden/sweep.json) when that file is present."""
     from superfloat.python_b200 import _shard, sweep
@@ -834,12 +834,11 @@ def bench_sweep(torch, dist, rank, world, bits=16):
     golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "sweep.json")
     ref = json.load(open(golden))["widths"][str(bits)] if os.path.exists(golden) else None
     match = True
-    for op, (rc, rf, cnt) in outs.items():
-        rows = _shard.gather_rows(torch.stack([rc, rf], 1), cuts, dist, world)
+    for op, (rd, cnt) in outs.items():
+        rows = _shard.gather_rows(rd, cuts, dist, world)
         _shard.sum_counts(cnt, dist, world)
         if rank == 0:
-            rows = rows.cpu().numpy()
-            sha = sweep.digest(rows[:, 0].view(np.uint64), rows[:, 1].view(np.uint64))
+            sha = sweep.digest(sweep.host_rows(rows))
             c = cnt.cpu().numpy()
             ok = ref is not None and sha == ref[op]["sha"] and all(
                 int(c[i]) == ref[op][f"n_{e}"] for i, e in enumerate(("overflow", "underflow", "divide", "invalid")))

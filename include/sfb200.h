@@ -354,13 +354,13 @@ SFB_API int sfb_elementwise_signmag(int op, int bits, const uint16_t *a, const u
  * the reference's Device API: the GPU form of its exhaustive check,
  * tools/exhaustive.py:146-181.  For op in SFB_OP_ADD / SUB / MUL / DIV and
  * the rows a = a_lo .. a_hi - 1 (codes, -M <= a_lo <= a_hi <= M + 1), entry
- * a - a_lo of row_codes and of row_flags has ADDED to it
- *     sum over j = 0 .. 2M of  code(a, j - M) * w_j     (mod 2^64)
- *     sum over j = 0 .. 2M of  flags(a, j - M) * w_j    (mod 2^64)
- * with w_j = splitmix64(j) and flags the SFB_F_* bits of that pair; zero
- * both buffers first.  Event totals add into counts.  Device buffers. */
-SFB_API int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint64_t *row_codes, uint64_t *row_flags,
-                      sfb_counts *counts, sfb_stream stream);
+ * a - a_lo of row_digest has ADDED to it
+ *     sum over j = 0 .. 2M of  ((code(a, j - M) + M) | flags(a, j - M) << 16) * w_j   (mod 2^32)
+ * with w_j = (low 32 bits of splitmix64(j)) | 1 and flags the SFB_F_* bits
+ * of that pair; zero the buffer first.  Event totals add into counts.
+ * Device buffers. */
+SFB_API int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint32_t *row_digest, sfb_counts *counts,
+                      sfb_stream stream);
 
 #ifdef __cplusplus
 }

@@ -47,7 +47,7 @@ SIGNATURES = {
     "sfb_wide_prepare_b": (_i32, [_i32, _i32, _p, _i64, _i64, _i64, _p, _i64, _p]),
     "sfb_matmul_wide_prepared": (_i32, [_i32, _i32, _p, _p, _p, _p, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64,
                                         _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
-    "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p, _p]),
+    "sfb_sweep": (_i32, [_i32, _i32, _i64, _i64, _p, _p, _p]),
     "sfb_reduce_workspace": (_i64, [_i64, _i64]),
     "sfb_to_bits": (_i32, [_i32, _p, _p, _i64, _p]),
     "sfb_linear_scale_scratch": (_i64, []),
@@ -287,11 +287,10 @@ def dot(bits, a, b, n, out, flags, workspace, counts, stream=None):
     check(rc, "sf dot")
 
 
-def sweep(op, bits, a_lo, a_hi, row_codes, row_flags, counts, stream=None):
+def sweep(op, bits, a_lo, a_hi, row_digest, counts, stream=None):
     if op not in ("add", "sub", "mul", "div"):
         raise ValueError(f"the sweep covers add, sub, mul and div, not {op!r}")
-    rc = load().sfb_sweep(OPS[op], bits, a_lo, a_hi, _ptr(row_codes), _ptr(row_flags), _ptr(counts),
-                          _stream(stream))
+    rc = load().sfb_sweep(OPS[op], bits, a_lo, a_hi, _ptr(row_digest), _ptr(counts), _stream(stream))
     check(rc, "sf sweep")
 
 

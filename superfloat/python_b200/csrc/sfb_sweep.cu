@@ -4,14 +4,19 @@
 // Rows are the a codes of [a_lo, a_hi); every row pairs a with all 2M+1
 // codes b_j = j - M and evaluates the op with the elementwise kernels' own
 // per-element arithmetic (sfb_ew_ops.cuh).  Nothing per pair is stored: each
-// row folds into two 64-bit digests, sum_j code * w_j and sum_j flags * w_j
-// (mod 2^64, w_j = splitmix64(j)), and the events are totalled.
+// row folds into one 32-bit digest
+//     sum_j ((code + M) | flags << 16) * w_j   (mod 2^32),
+// w_j = the low word of splitmix64(j), made odd, and the events are totalled.
+// A wrong code or flag at one pair changes the digest by a nonzero multiple
+// (below 2^20) of an odd weight, which is never 0 mod 2^32, so a single
+// wrong pair is always seen; several cancel with probability about 2^-32.
 //
 // A CTA owns RB consecutive rows; its threads stride over j, compute w_j
-// once and apply it to the RB rows, keeping 2 RB running digests in
-// registers; a warp shuffle reduction and one 64-bit atomic add per row and
-// warp finish the row.  The sweep is ALU-bound (about 2^32 pairs per op at
-// sf16), with 16 bytes written per row.
+// once and apply it to the RB rows (one multiply-add per pair), keeping RB
+// running digests in registers; a warp shuffle reduction and one 32-bit
+// atomic add per row and warp finish the row.  The sweep is bound by
+// instruction issue (about 2^32 pairs per op at sf16), with 4 bytes written
+// per row.
 #include "sfb_common.cuh"
 #include "sfb_ew_ops.cuh"
 
@@ -20,7 +25,7 @@ namespace {
 
 using namespace ewops;
 
-constexpr int SW_THREADS = 256, RB = 8;
+constexpr int SW_THREADS = 256, RB = 16;
 
 __device__ __forceinline__ unsigned long long splitmix64(unsigned long long x) {
     unsigned long long z = x + 0x9E3779B97F4A7C15ull;
@@ -31,19 +36,17 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long x) {
 
 template <int OP, int BITS>
 __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, int a_hi,
-                                                          unsigned long long *__restrict__ row_codes,
-                                                          unsigned long long *__restrict__ row_flags,
-                                                          sfb_counts *counts) {
+                                                          uint32_t *__restrict__ row_digest, sfb_counts *counts) {
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
     const int M = w.M, n = 2 * w.M + 1;
     const int r0 = a_lo + blockIdx.x * RB;
-    unsigned long long dc[RB], df[RB];
+    uint32_t dg[RB];
 #pragma unroll
-    for (int r = 0; r < RB; r++) dc[r] = 0, df[r] = 0;
+    for (int r = 0; r < RB; r++) dg[r] = 0;
     Counts cnt;
     for (int j = threadIdx.x; j < n; j += SW_THREADS) {
-        const unsigned long long wj = splitmix64((unsigned long long)j);
+        const uint32_t wj = (uint32_t)splitmix64((unsigned long long)j) | 1u;
         const int b = j - M;
 #pragma unroll
         for (int r = 0; r < RB; r++) {
@@ -51,8 +54,7 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
             if (a < a_hi) {
                 Ev ev;
                 const int k = ew_one<OP, BITS>(a, b, 0, w, 0, ev);
-                dc[r] += (unsigned long long)(long long)k * wj;
-                df[r] += (unsigned long long)flag_byte(ev) * wj;
+                dg[r] += ((uint32_t)(k + M) | (flag_byte(ev) << 16)) * wj;
                 tally(cnt, ev);
             }
         }
@@ -61,35 +63,28 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
 #pragma unroll
     for (int r = 0; r < RB; r++) {
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            dc[r] += __shfl_xor_sync(0xffffffffu, dc[r], o);
-            df[r] += __shfl_xor_sync(0xffffffffu, df[r], o);
-        }
+        for (int o = 16; o; o >>= 1) dg[r] += __shfl_xor_sync(0xffffffffu, dg[r], o);
         const int a = r0 + r;
-        if (lane == 0 && a < a_hi) {
-            atomicAdd(&row_codes[a - a_lo], dc[r]);
-            atomicAdd(&row_flags[a - a_lo], df[r]);
-        }
+        if (lane == 0 && a < a_hi) atomicAdd(&row_digest[a - a_lo], dg[r]);
     }
     flush_counts(cnt, counts, sc);
 }
 
 template <int OP>
-void launch_sweep(int bits, int a_lo, int a_hi, unsigned long long *rc, unsigned long long *rf, sfb_counts *counts,
-                  cudaStream_t st) {
+void launch_sweep(int bits, int a_lo, int a_hi, uint32_t *rd, sfb_counts *counts, cudaStream_t st) {
     const int grid = (a_hi - a_lo + RB - 1) / RB;
     const Width w = width(bits);
     if (bits == 16)
-        sweep_kernel<OP, 16><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rc, rf, counts);
+        sweep_kernel<OP, 16><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rd, counts);
     else
-        sweep_kernel<OP, 0><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rc, rf, counts);
+        sweep_kernel<OP, 0><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rd, counts);
 }
 
 }  // namespace
 }  // namespace sfb
 
-extern "C" int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint64_t *row_codes, uint64_t *row_flags,
-                         sfb_counts *counts, sfb_stream stream) {
+extern "C" int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint32_t *row_digest, sfb_counts *counts,
+                         sfb_stream stream) {
     using namespace sfb;
     if (bits < 4 || bits > 16) return set_error(SFB_EINVAL, "sfb_sweep: width %d is not 4..16", bits);
     const int64_t M = (1 << (bits - 1)) - 1;
@@ -97,16 +92,13 @@ extern "C" int sfb_sweep(int op, int bits, int64_t a_lo, int64_t a_hi, uint64_t 
         return set_error(SFB_EINVAL, "sfb_sweep: rows [%lld, %lld) are not within [-%lld, %lld]", (long long)a_lo,
                          (long long)a_hi, (long long)M, (long long)M);
     if (a_lo == a_hi) return SFB_OK;
-    if (row_codes == nullptr || row_flags == nullptr)
-        return set_error(SFB_EINVAL, "sfb_sweep: null row digest buffer");
+    if (row_digest == nullptr) return set_error(SFB_EINVAL, "sfb_sweep: null row digest buffer");
     cudaStream_t st = (cudaStream_t)stream;
-    auto rc = reinterpret_cast<unsigned long long *>(row_codes);
-    auto rf = reinterpret_cast<unsigned long long *>(row_flags);
     switch (op) {
-        case SFB_OP_ADD: launch_sweep<SFB_OP_ADD>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
-        case SFB_OP_SUB: launch_sweep<SFB_OP_SUB>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
-        case SFB_OP_MUL: launch_sweep<SFB_OP_MUL>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
-        case SFB_OP_DIV: launch_sweep<SFB_OP_DIV>(bits, (int)a_lo, (int)a_hi, rc, rf, counts, st); break;
+        case SFB_OP_ADD: launch_sweep<SFB_OP_ADD>(bits, (int)a_lo, (int)a_hi, row_digest, counts, st); break;
+        case SFB_OP_SUB: launch_sweep<SFB_OP_SUB>(bits, (int)a_lo, (int)a_hi, row_digest, counts, st); break;
+        case SFB_OP_MUL: launch_sweep<SFB_OP_MUL>(bits, (int)a_lo, (int)a_hi, row_digest, counts, st); break;
+        case SFB_OP_DIV: launch_sweep<SFB_OP_DIV>(bits, (int)a_lo, (int)a_hi, row_digest, counts, st); break;
         default: return set_error(SFB_EINVAL, "sfb_sweep: op %d is not add, sub, mul or div", op);
     }
     return check_launch("sfb_sweep");

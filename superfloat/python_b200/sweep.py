@@ -4,16 +4,17 @@ The device counterpart of the reference's exhaustive check
 (tools/exhaustive.py:146-181): for an op in add / sub / mul / div and a
 width N, every pair (a, b) of codes in [-M, M] is evaluated with the same
 device arithmetic as the elementwise kernels.  Writing 2^32 results out is
-pointless, so each a-row is folded on the device into two 64-bit digests,
+pointless, so each a-row is folded on the device into one 32-bit digest,
 
-    codes[a] = sum_j  uint64(code(a, b_j)) * w_j      (mod 2^64)
-    flags[a] = sum_j  uint64(flags(a, b_j)) * w_j     (mod 2^64)
+    digest[a] = sum_j  ((code(a, b_j) + M) | flags(a, b_j) << 16) * w_j      (mod 2^32)
 
-with b_j = j - M, w_j = splitmix64(j) and the flag bits overflow 1,
-underflow 2, divide 4, invalid 8; plus the event totals.  The digest of a
-sweep is the sha256 of the little-endian row digests (codes, then flags),
-computed here on the host.  Rows shard across GPUs with no exchange but the
-final gather.
+with b_j = j - M, w_j = (the low word of splitmix64(j)) | 1 and the flag
+bits overflow 1, underflow 2, divide 4, invalid 8; plus the event totals.
+The weights are odd, so one wrong code or flag (a nonzero change below 2^20
+of one term) always changes the digest; several cancel with probability
+about 2^-32.  The digest of a sweep is the sha256 of the little-endian row
+digests, computed here on the host.  Rows shard across GPUs with no exchange
+but the final gather.
 """
 from __future__ import annotations
 
@@ -36,43 +37,41 @@ def splitmix64(x: np.ndarray) -> np.ndarray:
 
 
 def weights(bits: int) -> np.ndarray:
+    """w_j, j = 0 .. 2M: the low word of splitmix64(j), made odd (uint64 holding 32 bits)."""
     M = (1 << (bits - 1)) - 1
-    return splitmix64(np.arange(2 * M + 1, dtype=np.uint64))
+    return (splitmix64(np.arange(2 * M + 1, dtype=np.uint64)) & np.uint64(0xFFFFFFFF)) | np.uint64(1)
 
 
-def fold_rows(codes: np.ndarray, flags: np.ndarray, w: np.ndarray):
-    """Row digests of (rows, 2M+1) code and flag arrays (the host restatement
-    of what the sweep kernel accumulates)."""
+def fold_rows(codes: np.ndarray, flags: np.ndarray, w: np.ndarray, bits: int) -> np.ndarray:
+    """Row digests (uint32) of (rows, 2M+1) code and flag arrays: the host
+    restatement of what the sweep kernel accumulates."""
+    M = (1 << (bits - 1)) - 1
+    word = (codes.astype(np.int64) + M).astype(np.uint64) | (flags.astype(np.uint64) << np.uint64(16))
     with np.errstate(over="ignore"):
-        dc = (codes.astype(np.int64).astype(np.uint64) * w[None, :]).sum(axis=1, dtype=np.uint64)
-        df = (flags.astype(np.uint64) * w[None, :]).sum(axis=1, dtype=np.uint64)
-    return dc, df
+        d = (word * w[None, :]).sum(axis=1, dtype=np.uint64)
+    return (d & np.uint64(0xFFFFFFFF)).astype(np.uint32)
 
 
-def digest(row_codes: np.ndarray, row_flags: np.ndarray) -> str:
-    h = hashlib.sha256()
-    h.update(np.ascontiguousarray(row_codes, dtype="<u8").tobytes())
-    h.update(np.ascontiguousarray(row_flags, dtype="<u8").tobytes())
-    return h.hexdigest()
+def digest(row_digests: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(row_digests, dtype="<u4").tobytes()).hexdigest()
 
 
 def run_device(op: str, bits: int, a_lo: int | None = None, a_hi: int | None = None, device=None, stream=None):
     """Row digests for a in [a_lo, a_hi) (default: all 2M+1 codes) on the
-    current CUDA device.  Returns (row_codes, row_flags) uint64 device
-    tensors and the event counts (int64 device tensor of 8)."""
+    current CUDA device.  Returns the row digests (int32 device tensor
+    holding the uint32 words) and the event counts (int64 device tensor of 8)."""
     import torch
     M = (1 << (bits - 1)) - 1
     a_lo = -M if a_lo is None else a_lo
     a_hi = M + 1 if a_hi is None else a_hi
     n = max(0, a_hi - a_lo)
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    rc = torch.zeros(n, dtype=torch.int64, device=dev)
-    rf = torch.zeros(n, dtype=torch.int64, device=dev)
+    rd = torch.zeros(n, dtype=torch.int32, device=dev)
     cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device=dev)
-    _lib.sweep(op, bits, a_lo, a_hi, rc, rf, cnt, stream)
-    return rc, rf, cnt
+    _lib.sweep(op, bits, a_lo, a_hi, rd, cnt, stream)
+    return rd, cnt
 
 
-def host_rows(rc, rf):
-    """Device int64 row digests as host uint64 arrays."""
-    return rc.cpu().numpy().view(np.uint64), rf.cpu().numpy().view(np.uint64)
+def host_rows(rd) -> np.ndarray:
+    """Device row digests as a host uint32 array."""
+    return rd.cpu().numpy().view(np.uint32)

@@ -7,7 +7,7 @@ Run where the reference tree is (its root as the argument or in SF_REFERENCE_ROO
 For each width in WIDTHS and op in add / sub / mul / div, every pair of
 codes (a, b) in [-M, M]^2 goes through the reference's ``vec.OPS[op]``
 (src/sf/_vectorized.py, the path tools/exhaustive.py:157-162 sweeps), and
-each a-row is folded into the row digests that
+each a-row is folded into the row digest that
 ``superfloat.python_b200.sweep.fold_rows`` defines.  sweep.json keeps the
 sha256 of all row digests, the event totals, and the row digests of a few
 sample rows.  About 5 minutes for sf16 on 8 processes.
@@ -45,8 +45,7 @@ def _work(args):
     n = 2 * M + 1
     codes = np.arange(-M, M + 1, dtype=np.int64)
     w = sweep.weights(bits)
-    dc = np.empty(r1 - r0, np.uint64)
-    df = np.empty(r1 - r0, np.uint64)
+    dg = np.empty(r1 - r0, np.uint32)
     counts = dict.fromkeys(sweep.FLAG_BITS, 0)
     step = max(1, (1 << 22) // n)
     for s in range(r0, r1, step):
@@ -61,10 +60,9 @@ def _work(args):
                 m = np.broadcast_to(m, ka.shape)
                 fl |= m.astype(np.uint64) * np.uint64(bit)
                 counts[name] += int(np.count_nonzero(m))
-        c, f = sweep.fold_rows(np.broadcast_to(rk, ka.shape).reshape(e - s, n), fl.reshape(e - s, n), w)
-        dc[s - r0:e - r0] = c
-        df[s - r0:e - r0] = f
-    return r0, dc, df, counts
+        dg[s - r0:e - r0] = sweep.fold_rows(np.broadcast_to(rk, ka.shape).reshape(e - s, n), fl.reshape(e - s, n),
+                                            w, bits)
+    return r0, dg, counts
 
 
 def main(argv):
@@ -78,8 +76,8 @@ def main(argv):
     ref = reference_root(args[0] if args else None)
     os.environ.setdefault("SF_CACHE_DIR", "/tmp/sf_cache_golden")
     out = {"source": "reference src/sf/_vectorized.py OPS over every code pair",
-           "fold": "row digests of superfloat.python_b200.sweep.fold_rows; sha256 of codes then flags, "
-                   "little-endian uint64, rows a = -M..M",
+           "fold": "row digests of superfloat.python_b200.sweep.fold_rows; sha256 of the little-endian uint32 "
+                   "row digests, rows a = -M..M",
            "widths": {}}
     ctx = mp.get_context("spawn")
     with ctx.Pool(procs) as pool:
@@ -92,20 +90,17 @@ def main(argv):
                 cuts = np.linspace(0, n, procs * 4 + 1).astype(int)
                 jobs = [(ref, bits, op, int(cuts[i]), int(cuts[i + 1])) for i in range(len(cuts) - 1)
                         if cuts[i + 1] > cuts[i]]
-                dc = np.empty(n, np.uint64)
-                df = np.empty(n, np.uint64)
+                dg = np.empty(n, np.uint32)
                 tot = dict.fromkeys(sweep.FLAG_BITS, 0)
-                for r0, c, f, cnt in pool.imap_unordered(_work, jobs):
-                    dc[r0:r0 + c.size] = c
-                    df[r0:r0 + f.size] = f
+                for r0, d, cnt in pool.imap_unordered(_work, jobs):
+                    dg[r0:r0 + d.size] = d
                     for k, v in cnt.items():
                         tot[k] += v
                 rows = np.linspace(0, n - 1, SAMPLE_ROWS).astype(int)
                 out["widths"][str(bits)][op] = {
-                    "pairs": n * n, "sha": sweep.digest(dc, df),
+                    "pairs": n * n, "sha": sweep.digest(dg),
                     **{f"n_{k}": v for k, v in tot.items()},
-                    "sample_a": [int(r) - M for r in rows], "sample_codes": [int(dc[r]) for r in rows],
-                    "sample_flags": [int(df[r]) for r in rows]}
+                    "sample_a": [int(r) - M for r in rows], "sample_digests": [int(dg[r]) for r in rows]}
                 print(f"sf{bits} {op}: {n * n:,} pairs in {time.time() - t0:.0f}s", flush=True)
     with open(os.path.join(HERE, "sweep.json"), "w") as f:
         json.dump(out, f, indent=1)

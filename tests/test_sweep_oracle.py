@@ -25,10 +25,10 @@ def oracle_rows(op, bits, a_codes):
         if name in ev:
             fl |= np.broadcast_to(ev[name], ka.shape).astype(np.uint64) * np.uint64(bit)
     rows = len(a_codes)
-    dc, df = sweep.fold_rows(np.broadcast_to(k, ka.shape).reshape(rows, -1), fl.reshape(rows, -1),
-                             sweep.weights(bits))
+    d = sweep.fold_rows(np.broadcast_to(k, ka.shape).reshape(rows, -1), fl.reshape(rows, -1),
+                        sweep.weights(bits), bits)
     counts = {n: int(np.count_nonzero(np.broadcast_to(m, ka.shape))) for n, m in ev.items()}
-    return dc, df, counts
+    return d, counts
 
 
 @pytest.mark.parametrize("bits", [8, 4])
@@ -36,8 +36,8 @@ def oracle_rows(op, bits, a_codes):
 def test_oracle_full_sweep_matches_reference(op, bits):
     g = golden("sweep.json")["widths"][str(bits)][op]
     M, _ = sfref.consts(bits)
-    dc, df, counts = oracle_rows(op, bits, np.arange(-M, M + 1))
-    assert sweep.digest(dc, df) == g["sha"]
+    d, counts = oracle_rows(op, bits, np.arange(-M, M + 1))
+    assert sweep.digest(d) == g["sha"]
     for name in sweep.FLAG_BITS:
         assert counts.get(name, 0) == g[f"n_{name}"], name
 
@@ -45,6 +45,28 @@ def test_oracle_full_sweep_matches_reference(op, bits):
 @pytest.mark.parametrize("op", sweep.OPS)
 def test_oracle_sf16_sample_rows_match_reference(op):
     g = golden("sweep.json")["widths"]["16"][op]
-    dc, df, _ = oracle_rows(op, 16, g["sample_a"])
-    assert [int(v) for v in dc] == g["sample_codes"]
-    assert [int(v) for v in df] == g["sample_flags"]
+    d, _ = oracle_rows(op, 16, g["sample_a"])
+    assert [int(v) for v in d] == g["sample_digests"]
+
+
+def test_one_wrong_pair_always_changes_a_row_digest():
+    """A single wrong code or flag changes its row's digest (odd weights),
+    at every position of a row, for the smallest and largest changes."""
+    bits = 8
+    M = 127
+    w = sweep.weights(bits)
+    assert (w & np.uint64(1)).all()
+    rng = np.random.default_rng(5)
+    codes = rng.integers(-M, M + 1, (1, 2 * M + 1))
+    flags = rng.integers(0, 16, (1, 2 * M + 1)).astype(np.uint64)
+    base = sweep.fold_rows(codes, flags, w, bits)[0]
+    for j in range(2 * M + 1):
+        for dc, dfl in ((1, 0), (-1, 0), (0, 1), (0, 8)):
+            c2, f2 = codes.copy(), flags.copy()
+            if dc and abs(c2[0, j] + dc) <= M:
+                c2[0, j] += dc
+            elif dfl:
+                f2[0, j] ^= np.uint64(dfl)
+            else:
+                continue
+            assert sweep.fold_rows(c2, f2, w, bits)[0] != base, (j, dc, dfl)
