@@ -201,38 +201,175 @@ def _linear_like(m):
     return isinstance(m, (nn.Linear, SFLinear, SFHFConv1D)) or is_hf_conv1d(m)
 
 
-def find_lm_heads(model: nn.Module) -> dict:
-    """The LM head(s), {id(module): why}: the model's get_output_embeddings();
-    else a linear tied to an embedding's weight; else the last linear whose
-    output size is an embedding's vocabulary (src/sf/torch/_modules.py:263-292)."""
+def _head_from_output_embeddings(model, linears, embeddings) -> dict:
     get = getattr(model, "get_output_embeddings", None)
-    if callable(get):
-        try:
-            head = get()
-        except Exception:  # noqa: BLE001  (a model's own hook may raise)
-            head = None
-        if isinstance(head, nn.Module) and _linear_like(head):
-            return {id(head): "LM head (the model's get_output_embeddings())"}
-    embs = [m for m in model.modules() if isinstance(m, nn.Embedding)]
-    if not embs:
+    if not callable(get):
         return {}
-    lins = [m for m in model.modules() if _linear_like(m)]
-    tied = {}
-    for m in lins:
-        w = getattr(m, "weight", None)
-        for e in embs:
-            if w is e.weight or (w is not None and w.data_ptr() == e.weight.data_ptr()
-                                 and w.numel() == e.weight.numel()):
-                tied[id(m)] = "LM head (weight tied to the embeddings)"
-    if tied:
-        return tied
-    vocab = {e.num_embeddings for e in embs}
-    last = [m for m in lins if (getattr(m, "out_features", None) or getattr(m, "nf", None)) in vocab]
-    return {id(last[-1]): "LM head (last layer with the vocabulary's output size)"} if last else {}
+    try:
+        head = get()
+    except Exception:  # noqa: BLE001  (a model's own hook may raise)
+        return {}
+    if isinstance(head, nn.Module) and _linear_like(head):
+        return {id(head): "LM head (the model's get_output_embeddings())"}
+    return {}
+
+
+def _heads_tied_to_embeddings(model, linears, embeddings) -> dict:
+    def shares(w, e):
+        return w is e.weight or (w is not None and w.data_ptr() == e.weight.data_ptr()
+                                 and w.numel() == e.weight.numel())
+    return {id(m): "LM head (weight tied to the embeddings)" for m in linears
+            if any(shares(getattr(m, "weight", None), e) for e in embeddings)}
+
+
+def _head_by_vocabulary(model, linears, embeddings) -> dict:
+    vocab = {e.num_embeddings for e in embeddings}
+    hits = [m for m in linears if (getattr(m, "out_features", None) or getattr(m, "nf", None)) in vocab]
+    return {id(hits[-1]): "LM head (last layer with the vocabulary's output size)"} if hits else {}
+
+
+def find_lm_heads(model: nn.Module) -> dict:
+    """The LM head(s), {id(module): why}, by the first rule that finds one:
+    the model's get_output_embeddings(); a linear tied to an embedding's
+    weight; the last linear whose output size is an embedding's vocabulary
+    (src/sf/torch/_modules.py:263-292).  The last two need an nn.Embedding."""
+    linears = [m for m in model.modules() if _linear_like(m)]
+    embeddings = [m for m in model.modules() if isinstance(m, nn.Embedding)]
+    for rule in (_head_from_output_embeddings, _heads_tied_to_embeddings, _head_by_vocabulary):
+        if rule is not _head_from_output_embeddings and not embeddings:
+            return {}
+        found = rule(model, linears, embeddings)
+        if found:
+            return found
+    return {}
 
 
 def _custom_forward(m, base) -> bool:
     return type(m).forward is not base.forward
+
+
+# layer types with no SF form: reported as skipped, run in float
+_NO_SF_FORM = (nn.Conv1d, nn.Conv3d, nn.ConvTranspose1d, nn.ConvTranspose2d, nn.ConvTranspose3d, nn.Bilinear,
+               nn.LSTM, nn.GRU, nn.RNN, nn.MultiheadAttention)
+
+
+def _module_names(model) -> set:
+    return {n for n, _ in model.named_modules(remove_duplicate=False)}
+
+
+def _unknown_names(model, names, what):
+    missing = sorted(set(names) - _module_names(model))
+    if missing:
+        raise ValueError(f"{what}: no module named {', '.join(map(repr, missing))}")
+
+
+class _Converter:
+    """One pass of ``convert``: the width each layer gets, the SF layer that
+    replaces it, the report.  A module reached twice (a shared submodule) is
+    replaced once and the alias recorded."""
+
+    def __init__(self, cfg, cfg16, per_layer, keep_ids, keep_names):
+        self.cfg, self.cfg16 = cfg, cfg16
+        self.per_layer = per_layer              # path -> SFConfig (widths=)
+        self.keep_ids, self.keep_names = keep_ids, keep_names
+        self.report = ConversionReport()
+        self.replaced = {}                      # id(module) -> (first path, replacement or None)
+        self.walked = set()
+
+    def config_for(self, module, path) -> SFConfig:
+        if path in self.per_layer:
+            c = self.per_layer[path]
+        elif self.cfg.bits < 16 and (id(module) in self.keep_ids or path in self.keep_names):
+            self.report.kept_sf16.append((path, self.keep_ids.get(id(module)) or "named in keep_sf16"))
+            c = self.cfg16
+        else:
+            c = self.cfg
+        self.report.widths[path] = c.bits
+        return c
+
+    def _skip(self, path, kind, why):
+        self.report.skipped.append((path, kind, why))
+
+    def _make(self, module, path):
+        """(SF replacement or None, whether the module is a leaf of the walk)."""
+        kind = type(module).__name__
+        if isinstance(module, (SFLinear, SFConv2d, SFHFConv1D)):
+            self.report.converted.append((path, kind + " (already SF)"))
+            return None, True
+        if isinstance(module, nn.Linear):
+            if _custom_forward(module, nn.Linear):
+                self._skip(path, kind, f"a subclass of nn.Linear with its own forward ({kind}); runs as it was")
+            elif not module.weight.is_floating_point():
+                self._skip(path, kind, f"weights stored as {module.weight.dtype}")
+            else:
+                self.report.converted.append((path, "Linear"))
+                return SFLinear.from_float(module, path, self.config_for(module, path)), True
+            return None, True
+        if is_hf_conv1d(module):
+            if not module.weight.is_floating_point():
+                self._skip(path, kind, f"weights stored as {module.weight.dtype}")
+                return None, True
+            self.report.converted.append((path, "Conv1D (Hugging Face)"))
+            return SFHFConv1D(module, path, self.config_for(module, path)), True
+        if isinstance(module, nn.Conv2d):
+            ok, why = convertible_conv(module)
+            if not (ok and module.weight.is_floating_point()):
+                self._skip(path, "Conv2d", why or f"weights stored as {module.weight.dtype}")
+                return None, True
+            self.report.converted.append((path, "Conv2d"))
+            return SFConv2d(module, path, self.config_for(module, path)), True
+        if isinstance(module, _NO_SF_FORM):
+            self._skip(path, kind, "no SF version here; runs in float")
+            return None, True
+        return None, False                      # a container: walk into it
+
+    def replace(self, module, path):
+        seen = self.replaced.get(id(module))
+        if seen is not None:                    # met before: the same replacement, no second walk
+            first, rep = seen
+            if rep is not None:
+                self.report.shared.append((path, first))
+            return rep, True
+        rep, leaf = self._make(module, path)
+        self.replaced[id(module)] = (path, rep)
+        return rep, leaf
+
+    def walk(self, parent, prefix):
+        if id(parent) in self.walked:
+            return
+        self.walked.add(id(parent))
+        for name, child in list(parent._modules.items()):
+            if child is None:
+                continue
+            path = f"{prefix}.{name}" if prefix else name
+            rep, leaf = self.replace(child, path)
+            if rep is not None:
+                setattr(parent, name, rep)
+            elif not leaf:
+                self.walk(child, path)
+
+    def run(self, model):
+        rep, leaf = self.replace(model, "")
+        if rep is not None:
+            model = rep
+        elif not leaf:
+            self.walk(model, "")
+        model._sf_conversion_report = self.report
+        return model
+
+
+def _keep_plan(model, keep_sf16, bits):
+    """(LM heads by id, module names) that stay at sf16 when ``bits`` < 16."""
+    if keep_sf16 == "auto":
+        return (find_lm_heads(model) if bits < 16 else {}), set()
+    if keep_sf16 in (False, None):
+        return {}, set()
+    if isinstance(keep_sf16, str) or not hasattr(keep_sf16, "__iter__"):
+        raise ValueError(f"keep_sf16 must be \"auto\", False or a list of module names, got {keep_sf16!r}")
+    names = set(keep_sf16)
+    if bits < 16:
+        _unknown_names(model, names, "keep_sf16")
+    return {}, names
 
 
 def convert(model: nn.Module, dtype="sf16", scale: str = "per_tensor", headroom: str = "bound",
@@ -258,110 +395,13 @@ def convert(model: nn.Module, dtype="sf16", scale: str = "per_tensor", headroom:
     cfg = SFConfig(_bits_of(dtype), scale, headroom, accumulate, shift)
     if not inplace:
         model = copy.deepcopy(model)
-    report = ConversionReport()
-    cfg16 = SFConfig(16, scale, headroom, accumulate, shift)
-    keep_ids, keep_names = {}, set()
-    if keep_sf16 == "auto":
-        if cfg.bits < 16:
-            keep_ids = find_lm_heads(model)
-    elif keep_sf16 in (False, None):
-        pass
-    elif isinstance(keep_sf16, str) or not hasattr(keep_sf16, "__iter__"):
-        raise ValueError(f"keep_sf16 must be \"auto\", False or a list of module names, got {keep_sf16!r}")
-    else:
-        keep_names = set(keep_sf16)
-        if cfg.bits < 16:
-            known = {n for n, _ in model.named_modules(remove_duplicate=False)}
-            missing = sorted(keep_names - known)
-            if missing:
-                raise ValueError(f"keep_sf16: no module named {', '.join(map(repr, missing))}")
+    keep_ids, keep_names = _keep_plan(model, keep_sf16, cfg.bits)
     per_layer = {}
     if widths:
-        known = {n for n, _ in model.named_modules(remove_duplicate=False)}
-        missing = sorted(set(widths) - known)
-        if missing:
-            raise ValueError(f"widths: no module named {', '.join(map(repr, missing))}")
+        _unknown_names(model, widths, "widths")
         per_layer = {n: SFConfig(_bits_of(d), scale, headroom, accumulate, shift) for n, d in widths.items()}
-
-    def cfg_for(child, full):
-        if full in per_layer:
-            c = per_layer[full]
-        elif cfg.bits >= 16:
-            c = cfg
-        else:
-            why = keep_ids.get(id(child)) or ("named in keep_sf16" if full in keep_names else None)
-            if why is None:
-                c = cfg
-            else:
-                report.kept_sf16.append((full, why))
-                c = cfg16
-        report.widths[full] = c.bits
-        return c
-
-    done, seen = {}, set()
-
-    def replacement(child, full):
-        key = id(child)
-        if key in done:
-            name, rep = done[key]
-            if rep is not None:
-                report.shared.append((full, name))
-            return rep, True
-        rep = None
-        if isinstance(child, (SFLinear, SFConv2d, SFHFConv1D)):
-            report.converted.append((full, type(child).__name__ + " (already SF)"))
-        elif isinstance(child, nn.Linear):
-            if _custom_forward(child, nn.Linear):
-                report.skipped.append((full, type(child).__name__, f"a subclass of nn.Linear with its own forward "
-                                       f"({type(child).__name__}); runs as it was"))
-            elif not child.weight.is_floating_point():
-                report.skipped.append((full, type(child).__name__, f"weights stored as {child.weight.dtype}"))
-            else:
-                rep = SFLinear.from_float(child, full, cfg_for(child, full))
-                report.converted.append((full, "Linear"))
-        elif is_hf_conv1d(child):
-            if child.weight.is_floating_point():
-                rep = SFHFConv1D(child, full, cfg_for(child, full))
-                report.converted.append((full, "Conv1D (Hugging Face)"))
-            else:
-                report.skipped.append((full, type(child).__name__, f"weights stored as {child.weight.dtype}"))
-        elif isinstance(child, nn.Conv2d):
-            ok, why = convertible_conv(child)
-            if ok and child.weight.is_floating_point():
-                rep = SFConv2d(child, full, cfg_for(child, full))
-                report.converted.append((full, "Conv2d"))
-            else:
-                report.skipped.append((full, "Conv2d", why or f"weights stored as {child.weight.dtype}"))
-        elif isinstance(child, (nn.Conv1d, nn.Conv3d, nn.ConvTranspose1d, nn.ConvTranspose2d, nn.ConvTranspose3d,
-                                nn.Bilinear, nn.LSTM, nn.GRU, nn.RNN, nn.MultiheadAttention)):
-            report.skipped.append((full, type(child).__name__, "no SF version here; runs in float"))
-        else:
-            done[key] = (full, None)
-            return None, False
-        done[key] = (full, rep)
-        return rep, True
-
-    def visit(parent, prefix):
-        if id(parent) in seen:
-            return
-        seen.add(id(parent))
-        for child_name, child in list(parent._modules.items()):
-            if child is None:
-                continue
-            full = f"{prefix}.{child_name}" if prefix else child_name
-            rep, leaf = replacement(child, full)
-            if rep is not None:
-                setattr(parent, child_name, rep)
-            elif not leaf:
-                visit(child, full)
-
-    rep, leaf = replacement(model, "")
-    if rep is not None:
-        model = rep
-    elif not leaf:
-        visit(model, "")
-    model._sf_conversion_report = report
-    return model
+    cfg16 = SFConfig(16, scale, headroom, accumulate, shift)
+    return _Converter(cfg, cfg16, per_layer, keep_ids, keep_names).run(model)
 
 
 def conversion_report(model: nn.Module) -> ConversionReport:
