@@ -556,9 +556,29 @@ def main():
                 dist.all_reduce(dt, op=dist.ReduceOp.MAX)
             return float(dt.item())
 
-        # the step's four operands copied in once per chunk, the five ops, the five results copied out
+        # the step's four operands copied in once per chunk, the five ops, the five results copied out;
+        # each step's counts are read while the next step's copies run
         multi = MultiOpPipeline(dev, ("x", "y", "z", "d"), [(op, hargs[op]) for op in OPS])
-        dt = timed_host(lambda: multi.run(fmt, hx, [hout[op] for op in OPS]))
+
+        def e2e_steps_run():
+            pending = None
+            for _ in range(e2e_steps):
+                nxt = multi.run_async(fmt, hx, [hout[op] for op in OPS])
+                if pending is not None:
+                    pending.result()
+                pending = nxt
+            pending.result()
+
+        multi.run(fmt, hx, [hout[op] for op in OPS])            # warm-up of the host path
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        e2e_steps_run()
+        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev.torch_device)
+        if world > 1:
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        dt = float(dt.item())
         h2d = 4 * 2 * n
         d2h = len(OPS) * (2 * n + 8 * _lib.N_COUNTS)
         line["e2e"] = {"value": len(OPS) * n * world * e2e_steps / dt / 1e9, "unit": "Gelem/s",
@@ -567,7 +587,8 @@ def main():
                        "copy_GBps_all_ranks": (h2d + d2h) * e2e_steps * world / dt / 1e9,
                        "path": "int16 codes in pinned host memory -> MultiOpPipeline: per 8M-code chunk the four "
                                "operands copied in once, add/sub/mul/fma/div on the device, the five results "
-                               "copied out, four streams; status counts read back every step"}
+                               "copied out, four streams; every step's status counts read back while the next "
+                               "step's copies run"}
         # each op with its own copies of its operands (HostPipeline, one call per op)
         pipe = HostPipeline(dev)
         dt1 = timed_host(lambda: [pipe.run(op, fmt, *(hx[a] for a in hargs[op]), out=hout[op]) for op in OPS])

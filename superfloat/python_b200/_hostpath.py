@@ -102,12 +102,18 @@ class HostPipeline:
 
 class MultiOpPipeline:
     """Several elementwise ops over the same host-resident operands (int16
-    codes in pinned host memory), chunked over two streams: per chunk each
-    distinct operand is copied in once, every op runs on it, and every
+    codes in pinned host memory), chunked over several streams: per chunk
+    each distinct operand is copied in once, every op runs on it, and every
     result is copied back, so an operand that several ops read crosses PCIe
-    once per chunk.  One chunk's copies overlap the other stream's kernels,
+    once per chunk.  One chunk's copies overlap the other streams' kernels,
     and the copy engines run both directions at once.  Status counts
-    accumulate per op on the device and are read once at the end."""
+    accumulate per op and stream on the device and come back with the last
+    copies of each stream.
+
+    ``run_async`` only queues a call and returns a ``Pending`` whose
+    ``result()`` waits for it and gives the counts, so a caller can queue the
+    next call's copies before reading this one's counts: consecutive calls
+    then keep the copy engines busy instead of draining between calls."""
 
     def __init__(self, dev, names, ops, chunk: int = 1 << 23, slots: int = 4):
         import torch
@@ -120,18 +126,31 @@ class MultiOpPipeline:
         self.ins = [{nm: torch.empty(chunk, dtype=torch.int16, device=d) for nm in self.names}
                     for _ in range(slots)]
         self.outs = [[torch.empty(chunk, dtype=torch.int16, device=d) for _ in self.ops] for _ in range(slots)]
-        self.counts = torch.zeros(slots, len(self.ops), _lib.N_COUNTS, dtype=torch.int64, device=d)
 
-    def run(self, fmt, inputs: dict, outputs: list):
-        """``outputs[i][j] = ops[i](inputs...)[j]`` for host int16 tensors of
-        one length (pinned for the copies to overlap).  Returns the event
-        counts per op (numpy int64[ops, 8])."""
+    class Pending:
+        def __init__(self, done, host_counts, dev_counts):
+            self.done, self.host_counts, self.dev_counts = done, host_counts, dev_counts
+
+        def result(self):
+            """Wait for the call; its event counts per op (numpy int64[ops, 8])."""
+            for ev in self.done:
+                ev.synchronize()
+            res = self.host_counts.numpy().sum(0)
+            for c in res:
+                _lib.check_counts(c)
+            return res
+
+    def run_async(self, fmt, inputs: dict, outputs: list) -> "MultiOpPipeline.Pending":
+        """Queue ``outputs[i][j] = ops[i](inputs...)[j]`` for host int16
+        tensors of one length (pinned for the copies to overlap)."""
         import torch
         n = inputs[self.names[0]].numel()
-        self.counts.zero_()
-        cur = torch.cuda.current_stream(self.dev.torch_device)
+        d = self.dev.torch_device
+        cur = torch.cuda.current_stream(d)
+        counts = torch.zeros(len(self.streams), len(self.ops), _lib.N_COUNTS, dtype=torch.int64, device=d)
+        host_counts = torch.empty(counts.shape, dtype=torch.int64, pin_memory=True)
         for st in self.streams:
-            st.wait_stream(cur)
+            st.wait_stream(cur)                  # the zeroed counts
         for k, (lo, hi) in enumerate(cuts(n, self.chunk)):
             m = hi - lo
             slot = k % len(self.streams)
@@ -143,14 +162,23 @@ class MultiOpPipeline:
                 for i, (op, args) in enumerate(self.ops):
                     xs = [dev_in[a] for a in args] + [None] * (3 - len(args))
                     o = self.outs[slot][i][:m]
-                    _lib.elementwise(op, fmt.bits, xs[0], xs[1], xs[2], o, None, self.counts[slot, i], stream=st)
+                    _lib.elementwise(op, fmt.bits, xs[0], xs[1], xs[2], o, None, counts[slot, i], stream=st)
                     outputs[i][lo:hi].copy_(o, non_blocking=True)
+        done = []
+        for slot, st in enumerate(self.streams):
+            with torch.cuda.stream(st):
+                host_counts[slot].copy_(counts[slot], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(st)
+                done.append(ev)
+        counts.record_stream(cur)
         for st in self.streams:
-            cur.wait_stream(st)
-        res = self.counts.sum(0).cpu().numpy()
-        for c in res:
-            _lib.check_counts(c)
-        return res
+            counts.record_stream(st)
+        return MultiOpPipeline.Pending(done, host_counts, counts)
+
+    def run(self, fmt, inputs: dict, outputs: list):
+        """``run_async`` and wait: the event counts per op (numpy int64[ops, 8])."""
+        return self.run_async(fmt, inputs, outputs).result()
 
 
 class PluginStager:

@@ -219,11 +219,20 @@ def test_multi_op_pipeline_equals_the_oracle(gpu, rng):
         t = torch.empty(n, dtype=torch.int16, pin_memory=True)
         t.copy_(torch.from_numpy(v))
         hin[nm] = t
-    for _ in range(2):
-        outs = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in ops]
-        counts = pipe.run(FORMATS[16], hin, outs)
+    def check(outs, counts):
         for i, (op, args) in enumerate(ops):
             want, ev = sfref.ew(op, 16, *(vals[a] for a in args))
             np.testing.assert_array_equal(outs[i].numpy(), want, err_msg=op)
             for j, e in enumerate(("overflow", "underflow", "divide", "invalid")):
                 assert int(counts[i][j]) == int(np.count_nonzero(ev.get(e, False))), (op, e)
+
+    for _ in range(2):
+        outs = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in ops]
+        check(outs, pipe.run(FORMATS[16], hin, outs))
+    # two calls queued before either is read
+    outs1 = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in ops]
+    outs2 = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in ops]
+    p1 = pipe.run_async(FORMATS[16], hin, outs1)
+    p2 = pipe.run_async(FORMATS[16], hin, outs2)
+    check(outs1, p1.result())
+    check(outs2, p2.result())
