@@ -121,54 +121,54 @@ __device__ __forceinline__ void emit(const Epi &e, const Width &w, int64_t idx, 
 //     p-1 = |a| |b| - 1 (unsigned)              (the underflow minimum)
 //     s   = t * (sa sb) + acc                   (sa, sb = +-1)
 //     acc = clip(s, -M, M),  overflow |= s ^ acc
-template <int BM>
+template <int BM, int CN = BN>
 struct GStage {
     uint32_t a_abs[BK][BM];   // |a|
     uint32_t a_hi[BK][BM];    // |a| << (32 - (N-1))
     int32_t a_sgn[BK][BM];    // +1 or -1
-    uint32_t b_abs[BK][BN];
-    int32_t b_sgn[BK][BN];    // +1 or -1
+    uint32_t b_abs[BK][CN];
+    int32_t b_sgn[BK][CN];    // +1 or -1
 };
 
-// TM rows per thread: 4, or 2 for problems so small that even 32-row tiles
-// leave SMs idle (twice the warps per output tile).  NT threads: 256 (BM =
-// 16 TM rows per CTA), or 128 (BM = 8 TM) so that small problems still
-// spread over the SMs.
-template <bool BITS16, int TM, int NT = THREADS>
+// TM rows and CT columns per thread, CN columns per CTA (NT / (CN / CT) row
+// groups, BM = that times TM rows): 4 x 4 outputs per thread on 64-column
+// tiles, or fewer for problems so small that the outputs give too few warps.
+template <bool BITS16, int TM, int NT = THREADS, int CN = BN, int CT = TN>
 __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict__ A, const int16_t *__restrict__ B,
                                                            int M, int N, int K, int64_t lda, int64_t ldb, int64_t sa,
                                                            int64_t sb, int64_t so, Width w0, Epi e, int vec,
                                                            sfb_counts *counts) {
-    constexpr int BM = (NT / 16) * TM;
+    constexpr int BM = (NT / (CN / CT)) * TM;
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    GStage<BM> *st = reinterpret_cast<GStage<BM> *>(smem_raw);
+    GStage<BM, CN> *st = reinterpret_cast<GStage<BM, CN> *>(smem_raw);
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
     const Width w = BITS16 ? Width{16, 15, 32767} : w0;
     const int hi_shift = 32 - w.sh;
     const int tid = threadIdx.x;
-    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int tx = tid % (CN / CT), ty = tid / (CN / CT);
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * CN;
     const int64_t z = blockIdx.z;
     A += z * sa;
     B += z * sb;
 
-    int acc[TM][TN];
-    uint32_t um[TM][TN], ov[TM][TN];
+    int acc[TM][CT];
+    uint32_t um[TM][CT], ov[TM][CT];
 #pragma unroll
     for (int i = 0; i < TM; i++)
 #pragma unroll
-        for (int j = 0; j < TN; j++) acc[i][j] = 0, um[i][j] = 0xFFFFFFFFu, ov[i][j] = 0;
+        for (int j = 0; j < CT; j++) acc[i][j] = 0, um[i][j] = 0xFFFFFFFFu, ov[i][j] = 0;
 
     // loader roles.  A: PER = 32 / (NT / BM) k of one row per thread; B: 8
     // columns of BPASS k rows per thread.  Vector loads when the rows are aligned.
     constexpr int TPR = NT / BM;               // threads per A row: 4 or 8
     constexpr int PER = BK / TPR;              // k per thread: 8 or 4
     constexpr int AV = PER < 8 ? PER : 8;      // codes per A vector load
-    constexpr int BROWS = NT / 8, BPASS = BK / BROWS;
+    constexpr int BROWS = NT / (CN / 8), BPASS = BK / BROWS;
     static_assert(PER % AV == 0 && (AV == 8 || AV == 4) && BPASS * BROWS == BK, "chain2 loader shape");
+    static_assert(CT == 4 || CT == 2, "four or two columns per thread");
     const int ar = tid / TPR, ah = tid % TPR;
-    const int bk = tid >> 3, bc = (tid & 7) * 8;
+    const int bk = tid / (CN / 8), bc = (tid % (CN / 8)) * 8;
     PackV<AV> ra[PER / AV];
     Pack8 rb[BPASS];
     auto load_regs = [&](int k0) {
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
             }
         }
     };
-    auto store_regs = [&](GStage<BM> &s) {
+    auto store_regs = [&](GStage<BM, CN> &s) {
 #pragma unroll
         for (int q = 0; q < PER / AV; q++)
 #pragma unroll
@@ -226,9 +226,9 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
     }
     __syncthreads();
     for (int kt = 0; kt < nk; kt++) {
-        GStage<BM> &cur = st[kt & 1];
+        GStage<BM, CN> &cur = st[kt & 1];
         if (kt + 1 < nk) load_regs((kt + 1) * BK);
-#pragma unroll 2
+#pragma unroll 8
         for (int k = 0; k < BK; k++) {
             uint32_t aa[TM], ahi[TM];
             int32_t as_[TM];
@@ -251,14 +251,23 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
                 ahi[0] = hv.x, ahi[1] = hv.y;
                 as_[0] = sv.x, as_[1] = sv.y;
             }
-            const uint4 bv = *reinterpret_cast<const uint4 *>(&cur.b_abs[k][tx * TN]);
-            const int4 bs = *reinterpret_cast<const int4 *>(&cur.b_sgn[k][tx * TN]);
-            const uint32_t ba[TN] = {bv.x, bv.y, bv.z, bv.w};
-            const int32_t bs_[TN] = {bs.x, bs.y, bs.z, bs.w};
+            uint32_t ba[CT];
+            int32_t bs_[CT];
+            if constexpr (CT == 4) {
+                const uint4 bv = *reinterpret_cast<const uint4 *>(&cur.b_abs[k][tx * CT]);
+                const int4 bs = *reinterpret_cast<const int4 *>(&cur.b_sgn[k][tx * CT]);
+                ba[0] = bv.x, ba[1] = bv.y, ba[2] = bv.z, ba[3] = bv.w;
+                bs_[0] = bs.x, bs_[1] = bs.y, bs_[2] = bs.z, bs_[3] = bs.w;
+            } else {
+                const uint2 bv = *reinterpret_cast<const uint2 *>(&cur.b_abs[k][tx * CT]);
+                const int2 bs = *reinterpret_cast<const int2 *>(&cur.b_sgn[k][tx * CT]);
+                ba[0] = bv.x, ba[1] = bv.y;
+                bs_[0] = bs.x, bs_[1] = bs.y;
+            }
 #pragma unroll
             for (int i = 0; i < TM; i++)
 #pragma unroll
-                for (int j = 0; j < TN; j++) {
+                for (int j = 0; j < CT; j++) {
                     const uint32_t t = __umulhi(ahi[i], ba[j]);
                     um[i][j] = min(um[i][j], aa[i] * ba[j] + 0xFFFFFFFFu);
                     const int32_t s = (int32_t)t * (as_[i] * bs_[j]) + acc[i][j];
@@ -278,8 +287,8 @@ __global__ void __launch_bounds__(NT, 2) chain2_kernel(const int16_t *__restrict
     for (int i = 0; i < TM; i++) {
         const int gm = m0 + ty * TM + i;
 #pragma unroll
-        for (int j = 0; j < TN; j++) {
-            const int gn = n0 + tx * TN + j;
+        for (int j = 0; j < CT; j++) {
+            const int gn = n0 + tx * CT + j;
             if (gm < M && gn < N)
                 emit(e, w, z * so + (int64_t)gm * N + gn, gn, acc[i][j], ov[i][j] != 0, um[i][j] < unit_m1, cnt);
         }
@@ -754,18 +763,28 @@ int launch_chain(int bits, const int16_t *A, const int16_t *B, const Epi &e, int
     }
     const bool b16 = bits == 16;
     if (batch * ((M + 31) / 32) * nt < (int64_t)sm_count()) {
-        // so few outputs that 32 x 64 tiles would not give every SM one: 16 x 64 tiles
-        // on 128-thread CTAs, two rows per thread
-        const dim3 g1((unsigned)nt, (unsigned)((M + 15) / 16), (unsigned)batch);
-        const int smem = 2 * (int)sizeof(GStage<16>);
-        auto kern = b16 ? chain2_kernel<true, 2, 128> : chain2_kernel<false, 2, 128>;
-        static unsigned long long attr_t[64][2] = {};
-        if (ctx == 0 || attr_t[dev][b16] != ctx) {
-            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-                return check_launch(what);
-            attr_t[dev][b16] = context_id();
+        // so few outputs that 32 x 64 tiles would not give every SM one: 32-column tiles,
+        // 32 x 32 (four rows per thread) while they still give every SM a CTA, else
+        // 16 x 32 while those give half the SMs one, else 8 x 32 on 64-thread CTAs
+        // (each under the default 48 KB of dynamic shared memory)
+        static_assert(2 * sizeof(GStage<32, 32>) <= 48 * 1024, "default dynamic shared memory");
+        const int64_t n32 = (N + 31) / 32, sms = sm_count();
+        if (batch * ((M + 31) / 32) * n32 >= sms) {
+            const dim3 g((unsigned)n32, (unsigned)((M + 31) / 32), (unsigned)batch);
+            auto kern = b16 ? chain2_kernel<true, 4, 128, 32, 2> : chain2_kernel<false, 4, 128, 32, 2>;
+            kern<<<g, 128, 2 * sizeof(GStage<32, 32>), st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w,
+                                                             e, vec, counts);
+        } else if (batch * ((M + 15) / 16) * n32 >= sms / 2) {
+            const dim3 g((unsigned)n32, (unsigned)((M + 15) / 16), (unsigned)batch);
+            auto kern = b16 ? chain2_kernel<true, 2, 128, 32, 2> : chain2_kernel<false, 2, 128, 32, 2>;
+            kern<<<g, 128, 2 * sizeof(GStage<16, 32>), st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w,
+                                                             e, vec, counts);
+        } else {
+            const dim3 g((unsigned)n32, (unsigned)((M + 7) / 8), (unsigned)batch);
+            auto kern = b16 ? chain2_kernel<true, 2, 64, 32, 2> : chain2_kernel<false, 2, 64, 32, 2>;
+            kern<<<g, 64, 2 * sizeof(GStage<8, 32>), st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e,
+                                                           vec, counts);
         }
-        kern<<<g1, 128, smem, st>>>(A, B, (int)M, (int)N, (int)K, lda, ldb, sa, sb, so, w, e, vec, counts);
         return check_launch(what);
     }
     if (batch * mt * nt < 2 * (int64_t)sm_count()) {
