@@ -42,6 +42,39 @@ def test_chain_random_shapes(gpu, bits, frac, rng):
         np.testing.assert_array_equal(masks["underflow"], ev["underflow"])
 
 
+def _chain_small_tier(M, N, sms):
+    """Which tiling the general chain picks for a 2-D problem too small for
+    32 x 64 tiles (sfb_chain.cu launch_chain): 32x32, 16x32 or 8x32; None above."""
+    c = lambda rows, cols: -(-M // rows) * -(-N // cols)
+    if c(32, 64) >= sms:
+        return None
+    if c(32, 32) >= sms:
+        return "32x32"
+    return "16x32" if c(16, 32) >= sms // 2 else "8x32"
+
+
+@pytest.mark.parametrize("bits", [16, 8])
+def test_chain_small_problem_tilings(gpu, bits, rng):
+    """Every tiling of the small-problem tier, on ragged shapes with odd K
+    (scalar loads) and even K (vector loads), against the oracle."""
+    import torch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    shapes = [(400, 390, 97), (448, 352, 64), (300, 200, 333), (280, 256, 96), (100, 90, 77), (24, 40, 128)]
+    tiers = set()
+    for (M, N, K) in shapes:
+        tiers.add(_chain_small_tier(M, N, sms))
+        A = _codes(rng, bits, (M, K))
+        B = _codes(rng, bits, (K, N))
+        A[0] = _codes(rng, bits, K, 0.01)
+        want, ev = sfref.matmul_chain(bits, A, B)
+        got, masks = gpu.run("matmul", FORMATS[bits], A, B)
+        np.testing.assert_array_equal(got, want, err_msg=f"{M}x{N}x{K}")
+        np.testing.assert_array_equal(masks["overflow"], ev["overflow"])
+        np.testing.assert_array_equal(masks["underflow"], ev["underflow"])
+    if sms == 148:
+        assert tiers == {"32x32", "16x32", "8x32"}
+
+
 def test_chain_golden_dot(gpu):
     for c in golden("chain.json")["cases"]:
         if c["op"] != "dot":
