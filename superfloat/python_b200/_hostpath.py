@@ -254,36 +254,43 @@ class PluginStager:
                 for i, e in enumerate(evs):
                     t_masks[e][lo:hi].copy_(self.h_mask[slot][i, :m])       # bool bytes, a plain copy
 
-            for k, lo in enumerate(range(0, n, self.chunk)):
-                hi = min(n, lo + self.chunk)
-                m = hi - lo
-                slot = k % nslot
-                if len(pending) == nslot:
-                    finish(pending.pop(0))                              # frees this slot
-                hin = self.h_in[slot]
-                for i, src in enumerate(flat):
-                    hin[i][:m].copy_(src[lo:hi])                        # int64 -> int16
-                st = self.streams[slot]
-                with torch.cuda.stream(st):
-                    din = self.d_in[slot]
-                    for i in range(len(flat)):
-                        din[i][:m].copy_(hin[i][:m], non_blocking=True)
-                    b = din[1][:m] if len(flat) > 1 else None
-                    c = din[2][:m] if len(flat) > 2 else None
-                    _lib.elementwise(op, bits, din[0][:m], b, c, self.d_out[slot][:m], self.d_fl[slot][:m],
-                                     self.counts[slot], pow_n=pow_n, stream=st)
-                    self.h_out[slot][:m].copy_(self.d_out[slot][:m], non_blocking=True)
-                    # each event's mask as bool bytes, split from the event byte on the device
-                    for i, e in enumerate(evs):
-                        tmp = self.d_tmp[slot][:m]
-                        torch.bitwise_and(self.d_fl[slot][:m], event_bits[e], out=tmp)
-                        torch.ne(tmp, 0, out=self.d_mask[slot][i, :m])
-                    for i in range(len(evs)):
-                        self.h_mask[slot][i, :m].copy_(self.d_mask[slot][i, :m], non_blocking=True)
-                    self.done[slot].record(st)
-                pending.append((slot, lo, hi))
-            while pending:
-                finish(pending.pop(0))
+            try:
+                for k, lo in enumerate(range(0, n, self.chunk)):
+                    hi = min(n, lo + self.chunk)
+                    m = hi - lo
+                    slot = k % nslot
+                    if len(pending) == nslot:
+                        finish(pending.pop(0))                              # frees this slot
+                    hin = self.h_in[slot]
+                    for i, src in enumerate(flat):
+                        hin[i][:m].copy_(src[lo:hi])                        # int64 -> int16
+                    st = self.streams[slot]
+                    with torch.cuda.stream(st):
+                        din = self.d_in[slot]
+                        for i in range(len(flat)):
+                            din[i][:m].copy_(hin[i][:m], non_blocking=True)
+                        b = din[1][:m] if len(flat) > 1 else None
+                        c = din[2][:m] if len(flat) > 2 else None
+                        _lib.elementwise(op, bits, din[0][:m], b, c, self.d_out[slot][:m], self.d_fl[slot][:m],
+                                         self.counts[slot], pow_n=pow_n, stream=st)
+                        self.h_out[slot][:m].copy_(self.d_out[slot][:m], non_blocking=True)
+                        # each event's mask as bool bytes, split from the event byte on the device
+                        for i, e in enumerate(evs):
+                            tmp = self.d_tmp[slot][:m]
+                            torch.bitwise_and(self.d_fl[slot][:m], event_bits[e], out=tmp)
+                            torch.ne(tmp, 0, out=self.d_mask[slot][i, :m])
+                        for i in range(len(evs)):
+                            self.h_mask[slot][i, :m].copy_(self.d_mask[slot][i, :m], non_blocking=True)
+                        self.done[slot].record(st)
+                    pending.append((slot, lo, hi))
+                while pending:
+                    finish(pending.pop(0))
+            except BaseException:
+                # copies of this call may still read the pinned slots: let them
+                # finish before the next call refills them
+                for st in self.streams:
+                    st.synchronize()
+                raise
             for st in self.streams:
                 cur.wait_stream(st)
             res = self.counts.sum(0).cpu().numpy()
