@@ -1,25 +1,28 @@
 """Benchmark: bit-exact sf16 elementwise ops on B200 (Gelem/s), with the wide
-8192^3 and chain 512^3 matmuls measured beside it.
+8192^3 and chain 512^3 matmuls, the converted GPT-2-small forward and the
+exhaustive sf16 pair sweep measured beside it.
 
 One step = the five status-reporting sf16 ops (add, sub, mul, fma, div) over
 2^26-element inputs resident in HBM, each op's exact event counts reduced on
 the device (and all-reduced over ranks when N > 1: the status exchange).
-``value`` = elements processed by all ranks / max-over-ranks device time.
-``e2e`` = the same ops on codes in pinned HOST memory (int16, the device
-word's width): the host->device copies of every step's inputs, the kernels,
-the device->host copies of the result codes and the read of the status
-counts are all inside the timed region (chunked over two streams so copies
-overlap kernels).  ``e2e_plugin_int64`` is the reference's own plug-in
-contract, ``Device.run`` on int64 NumPy arrays returning int64 codes and
-boolean masks, once per op.
+Each timed step is one CUDA graph replay (the step's counter reset and the
+five launches, captured once per step buffer), so host launch overhead does
+not gap the device.  ``value`` = elements processed by all ranks /
+max-over-ranks device time.  ``e2e`` = the same ops on codes in pinned HOST
+memory (int16, the device word's width): the host->device copies of every
+step's inputs, the kernels, the device->host copies of the result codes and
+the read of the status counts are all inside the timed region (chunked over
+four streams so copies overlap kernels).  ``e2e_plugin_int64`` is the
+reference's own plug-in contract, ``Device.run`` on int64 NumPy arrays
+returning int64 codes and boolean masks, once per op.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 N > 1 is launched with torchrun; each rank runs its own 2^26 elements (weak
 scaling, no data-path collective; only the status counts are all-reduced).
 ``--impl reference`` times the reference's host implementation of the same
-ops (the oracle's NumPy restatement of src/sf/_vectorized.py, the reference's
-own code path being NumPy) on this host's cores, on rank 0 only.
+ops (its own src/sf/_vectorized.py when the reference is installed, else the
+oracle's NumPy restatement) on this host's cores, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -455,22 +458,57 @@ def main():
                           device=dev.torch_device)
     bufs = list(allbufs.unbind(0))
 
-    def step(evs=None, buf=None):
+    def step(evs=None, buf=None, st=None, only=None):
         buf.zero_()
-        for i, op in enumerate(OPS):
-            if evs is not None:
-                evs[op][0].record(stream)
-            dev.run_device(op, fmt, *targs[op], out=outs[op], counts=buf[i])
-            if evs is not None:
-                evs[op][1].record(stream)
+        # the timed op last: its closing event then falls on the step boundary
+        order = [op for op in OPS if op != only] + ([only] if only else [])
+        for op in order:
+            i = OPS.index(op)
+            timed = evs is not None and (only is None or op == only)
+            if timed:
+                evs[op][0].record(st or stream)
+            dev.run_device(op, fmt, *targs[op], out=outs[op], counts=buf[i], stream=st)
+            if timed:
+                evs[op][1].record(st or stream)
 
     def drain():
         if world > 1:
             dist.all_reduce(allbufs)
 
-    for i in range(args.warmup):
-        step(buf=bufs[i])
+    # warm-up: eager steps with every op's launch bracketed by events (each
+    # op's kernel time, and which op's launch is longest)
+    warm_evs = []
+    for i in range(max(1, args.warmup)):
+        evs = {op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
+        step(evs, bufs[i])
+        warm_evs.append(evs)
     drain()
+    torch.cuda.synchronize()
+    warm = {op: [evs[op][0].elapsed_time(evs[op][1]) for evs in warm_evs] for op in OPS}
+    # the first step carries the first launches' set-up: left out when there are more
+    warm_ms = {op: statistics.median(v[1:] if len(v) > 1 else v) for op, v in warm.items()}
+    dom = max(OPS, key=warm_ms.get)
+
+    # one CUDA graph per timed step (the step's counter buffer zeroed and the
+    # five launches), so the host's launch overhead stays out of the device's
+    # way; the longest op's launch, last in the step, is bracketed by events
+    # inside the graph (recorded on every replay) for its kernel time over the
+    # timed region.  Events around every launch would put a drain before each
+    # one (~10% of the step); the other ops' kernel times come from the warm-up.
+    graphs, dom_evs = [], []
+    side = torch.cuda.Stream(device=dev.torch_device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):                       # a warm-up off the capturing stream
+        step(buf=bufs[0], st=side)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        g = torch.cuda.CUDAGraph()
+        evs = {dom: (torch.cuda.Event(enable_timing=True, external=True),
+                     torch.cuda.Event(enable_timing=True, external=True))}
+        with torch.cuda.graph(g):
+            step(evs, bufs[i], st=torch.cuda.current_stream(), only=dom)
+        graphs.append(g)
+        dom_evs.append(evs[dom])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -478,17 +516,13 @@ def main():
     if sampler:
         sampler.start()
         time.sleep(0.3)
-    per_op = {op: [] for op in OPS}
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t_start.record(stream)
-    evs_all = []
     for i in range(args.steps):
-        evs = {op: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for op in OPS}
-        step(evs, bufs[i])
-        evs_all.append(evs)
+        graphs[i].replay()
     drain()                                  # the status reduction is part of the timed work
     t_end.record(stream)
     counts = bufs[args.steps - 1]
@@ -497,9 +531,8 @@ def main():
         dist.barrier()
     clocks = sampler.stop() if sampler else None
     ms_total = t_start.elapsed_time(t_end)
-    for evs in evs_all:
-        for op in OPS:
-            per_op[op].append(evs[op][0].elapsed_time(evs[op][1]))
+    dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in dom_evs)
+    del graphs
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev.torch_device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -512,13 +545,14 @@ def main():
     cnt = counts.cpu().numpy()
 
     hbm, peak_kind = peaks()
-    mean_ms = {op: statistics.mean(v) for op, v in per_op.items()}
-    dom = max(mean_ms, key=mean_ms.get)
-    achieved = BYTES_PER_ELEM[dom] * n / (mean_ms[dom] / 1e3) / 1e9
+    achieved = BYTES_PER_ELEM[dom] * n / (dom_ms / 1e3) / 1e9
     traffic = traffic_from_profiles(f"ew_{dom}_{n}")
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                 "traffic": traffic, "kernel": f"ew_kernel<{dom}>", "peak_kind": peak_kind,
-                "per_op_GBps": {op: BYTES_PER_ELEM[op] * n / (mean_ms[op] / 1e3) / 1e9 for op in OPS},
+                "launch_ms": dom_ms,
+                "launch_ms_source": "CUDA events around this op's launch inside every timed step's graph",
+                "per_op_GBps_warmup": {op: BYTES_PER_ELEM[op] * n / (warm_ms[op] / 1e3) / 1e9 for op in OPS},
+                "per_op_source": "median of the warm-up steps after the first, events around every launch",
                 "algorithmic_bytes_per_launch": BYTES_PER_ELEM[dom] * n}
 
     line = {"metric": METRIC, "value": value, "unit": "Gelem/s", "n_gpus": world, "steps": args.steps,
