@@ -881,49 +881,36 @@ def bench_wide_prepared(torch, tB, n, rank, world, dist, want_sha, reps=4):
 
 def bench_sweep(torch, dist, rank, world, bits=16):
     """Every sf16 code pair through add, sub, mul and div (4 x 65535^2 =
-    1.7e10 pairs), the a-rows dealt to the ranks in interleaved pieces (eight
-    per rank when N > 1: a div row costs more the nearer a is to 0, so one
-    block per rank would leave the middle ranks the slowest); each row folds
+    1.7e10 pairs), the a-rows split evenly over the ranks; each row folds
     into one 32-bit digest on the device.  Device time is the max over
     ranks; rank 0 gathers the row digests and checks their sha256 against
     the reference's (tests/golden/sweep.json) when that file is present."""
-    from superfloat.python_b200 import _lib, _shard, sweep
+    from superfloat.python_b200 import _shard, sweep
     M = (1 << (bits - 1)) - 1
     n = 2 * M + 1
-    per_rank = 8 if world > 1 else 1
-    pieces = _shard.interleaved_pieces(n, world, per_rank, -M)
-    mine = pieces[rank::world]
-    rows = sum(hi - lo for lo, hi in mine)
+    cuts = _shard.row_cuts(n, world, -M)
+    lo, hi = cuts[rank], cuts[rank + 1]
     for op in sweep.OPS:                                   # warm-up on a few rows
-        sweep.run_device(op, bits, mine[0][0], min(mine[0][1], mine[0][0] + 64))
+        sweep.run_device(op, bits, lo, min(hi, lo + 64))
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    outs = {}
-    for op in sweep.OPS:
-        rd = torch.zeros(rows, dtype=torch.int32, device="cuda")
-        cnt = torch.zeros(_lib.N_COUNTS, dtype=torch.int64, device="cuda")
-        off = 0
-        for lo, hi in mine:
-            _lib.sweep(op, bits, lo, hi, rd[off:off + hi - lo], cnt)
-            off += hi - lo
-        outs[op] = (rd, cnt)
+    outs = {op: sweep.run_device(op, bits, lo, hi) for op in sweep.OPS}
     e1.record()
     torch.cuda.synchronize()
     ms = _shard.max_over_ranks(e0.elapsed_time(e1), "cuda", dist, world)
     res = {"ms": ms, "value": len(sweep.OPS) * n * n / (ms / 1e3) / 1e9, "unit": "Gpairs/s (add, sub, mul, div)",
-           "pairs": len(sweep.OPS) * n * n, "bits": bits,
-           "sharding": f"a-rows over {world} GPU(s) in {per_rank} interleaved piece(s) per rank"}
+           "pairs": len(sweep.OPS) * n * n, "bits": bits, "sharding": f"a-rows over {world} GPU(s)"}
     golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "sweep.json")
     ref = json.load(open(golden))["widths"][str(bits)] if os.path.exists(golden) else None
     match = True
     for op, (rd, cnt) in outs.items():
-        full = _shard.gather_interleaved(rd, pieces, rank, dist, world)
+        rows = _shard.gather_rows(rd, cuts, dist, world)
         _shard.sum_counts(cnt, dist, world)
         if rank == 0:
-            sha = sweep.digest(sweep.host_rows(full))
+            sha = sweep.digest(sweep.host_rows(rows))
             c = cnt.cpu().numpy()
             ok = ref is not None and sha == ref[op]["sha"] and all(
                 int(c[i]) == ref[op][f"n_{e}"] for i, e in enumerate(("overflow", "underflow", "divide", "invalid")))

@@ -61,44 +61,6 @@ def gather_rows(local, cuts, dist=None, world: int = 1):
     return torch.cat([parts[r][:cuts[r + 1] - cuts[r]] for r in range(world)])
 
 
-def interleaved_pieces(n: int, world: int, per_rank: int, start: int = 0) -> list[tuple[int, int]]:
-    """[start, start + n) cut into world x per_rank near-equal pieces, in
-    order; piece p belongs to rank p mod world.  Rows whose cost changes
-    along the range (the sweep's div rows grow dearer toward a = 0) then
-    spread evenly over the ranks, where one block per rank would not."""
-    k = world * per_rank
-    return [(start + (n * p) // k, start + (n * (p + 1)) // k) for p in range(k)]
-
-
-def gather_interleaved(local, pieces, rank: int, dist=None, world: int = 1):
-    """Every rank's rows of ``pieces`` (its own pieces p = rank, rank + world,
-    ... concatenated along dim 0, as ``local``) gathered into the whole
-    range in piece order, on every rank."""
-    import torch
-    if dist is None or world == 1:
-        return local
-    sizes = [sum(hi - lo for lo, hi in pieces[r::world]) for r in range(world)]
-    if local.shape[0] != sizes[rank]:
-        raise ValueError(f"rank {rank} holds {local.shape[0]} rows, its pieces have {sizes[rank]}")
-    rows_max = max(sizes)
-    pad = torch.zeros((rows_max,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
-    pad[:local.shape[0]] = local
-    wire = pad
-    if not _nccl_type(pad.dtype):                    # NCCL has no int16: send the bytes
-        wire = pad.reshape(rows_max, -1).view(torch.uint8)
-    parts = [torch.empty_like(wire) for _ in range(world)]
-    dist.all_gather(parts, wire)
-    if wire is not pad:
-        parts = [q.view(pad.dtype).reshape(pad.shape) for q in parts]
-    offs = [0] * world
-    out = []
-    for p, (lo, hi) in enumerate(pieces):
-        r = p % world
-        out.append(parts[r][offs[r]:offs[r] + hi - lo])
-        offs[r] += hi - lo
-    return torch.cat(out)
-
-
 def cyclic_pieces(n: int, world: int, parts: int, rank: int) -> list[tuple[int, int]]:
     """Rows of ``rank`` when n rows go to the ranks block-cyclically in
     ``parts`` pieces of P = n / (world parts) rows: piece j is global rows

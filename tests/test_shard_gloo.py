@@ -50,15 +50,9 @@ def _worker(rank, world, port, out):
                                      world, async_op=True) for j, (lo, hi) in enumerate(pieces)]
         for w in works:
             w.wait()
-        # interleaved pieces of a ragged range (the sweep's a-rows): int32 and int16 rows
-        ipieces = _shard.interleaved_pieces(255, world, 3, -127)
-        mine = torch.cat([torch.arange(lo, hi, dtype=torch.int32) for lo, hi in ipieces[rank::world]])
-        inter32 = _shard.gather_interleaved(mine, ipieces, rank, dist, world)
-        inter16 = _shard.gather_interleaved(mine.to(torch.int16)[:, None].repeat(1, 2), ipieces, rank, dist, world)
         if rank == 0:
             np.save(out, {"g16": g16.numpy(), "codes": codes.numpy(), "flags": flags.numpy(), "cnt": cnt.numpy(), "t": t,
-                          "rows": allrows.numpy(), "cyclic": full.numpy(), "inter32": inter32.numpy(),
-                          "inter16": inter16.numpy()}, allow_pickle=True)
+                          "rows": allrows.numpy(), "cyclic": full.numpy()}, allow_pickle=True)
     finally:
         dist.destroy_process_group()
 
@@ -81,18 +75,6 @@ def test_sharded_matmul_and_gathers_over_gloo(tmp_path):
     assert r["g16"].dtype == np.int16
     np.testing.assert_array_equal(r["g16"], (np.arange(9)[:, None] * 1000 - 4000).repeat(3, 1))
     np.testing.assert_array_equal(r["cyclic"], np.arange(24)[:, None].repeat(3, 1))
-    np.testing.assert_array_equal(r["inter32"], np.arange(-127, 128))
-    np.testing.assert_array_equal(r["inter16"], np.arange(-127, 128)[:, None].repeat(2, 1))
-
-
-def test_interleaved_pieces_cover_the_range():
-    from superfloat.python_b200 import _shard
-    for n in (1, 7, 255, 65535):
-        for world in (1, 2, 3, 8):
-            for per in (1, 4, 8):
-                p = _shard.interleaved_pieces(n, world, per, -(n // 2))
-                assert len(p) == world * per and p[0][0] == -(n // 2) and p[-1][1] == n - n // 2
-                assert all(a[1] == b[0] for a, b in zip(p, p[1:])) and all(hi >= lo for lo, hi in p)
 
 
 def test_row_cuts_cover_every_row():
