@@ -11,12 +11,17 @@
 // (below 2^20) of an odd weight, which is never 0 mod 2^32, so a single
 // wrong pair is always seen; several cancel with probability about 2^-32.
 //
-// A CTA owns RB consecutive rows; its threads stride over j, compute w_j
-// once and apply it to the RB rows (one multiply-add per pair), keeping RB
-// running digests in registers; a warp shuffle reduction and one 32-bit
-// atomic add per row and warp finish the row.  The sweep is bound by
+// A CTA owns RB consecutive rows and one span of j; its threads stride
+// over the span, compute w_j once and apply it to the RB rows (one
+// multiply-add per pair), keeping RB running digests in registers; a warp
+// shuffle reduction and one 32-bit atomic add per row and warp add the
+// span's share to the row (the digest is a sum, so spans add).  A launch of
+// few rows (a rank's share of a multi-GPU sweep) splits j into as many spans
+// as it takes to give every SM several CTAs.  The sweep is bound by
 // instruction issue (about 2^32 pairs per op at sf16), with 4 bytes written
 // per row.
+#include <algorithm>
+
 #include "sfb_common.cuh"
 #include "sfb_ew_ops.cuh"
 
@@ -35,7 +40,7 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long x) {
 }
 
 template <int OP, int BITS>
-__global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, int a_hi,
+__global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, int a_hi, int jspan,
                                                           uint32_t *__restrict__ row_digest, sfb_counts *counts) {
     __shared__ unsigned sc[5];
     zero_counts_smem(sc);
@@ -45,7 +50,8 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
 #pragma unroll
     for (int r = 0; r < RB; r++) dg[r] = 0;
     Counts cnt;
-    for (int j = threadIdx.x; j < n; j += SW_THREADS) {
+    const int j0 = blockIdx.y * jspan, j1 = min(n, j0 + jspan);
+    for (int j = j0 + threadIdx.x; j < j1; j += SW_THREADS) {
         const uint32_t wj = (uint32_t)splitmix64((unsigned long long)j) | 1u;
         const int b = j - M;
 #pragma unroll
@@ -72,12 +78,22 @@ __global__ void __launch_bounds__(SW_THREADS) sweep_kernel(Width w, int a_lo, in
 
 template <int OP>
 void launch_sweep(int bits, int a_lo, int a_hi, uint32_t *rd, sfb_counts *counts, cudaStream_t st) {
-    const int grid = (a_hi - a_lo + RB - 1) / RB;
+    const int rows = (a_hi - a_lo + RB - 1) / RB;
     const Width w = width(bits);
-    if (bits == 16)
-        sweep_kernel<OP, 16><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rd, counts);
-    else
-        sweep_kernel<OP, 0><<<grid, SW_THREADS, 0, st>>>(w, a_lo, a_hi, rd, counts);
+    const int n = 2 * w.M + 1;
+    auto kern = bits == 16 ? sweep_kernel<OP, 16> : sweep_kernel<OP, 0>;
+    auto resident = [](decltype(kern) k) {
+        int b = 0;
+        return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k, SW_THREADS, 0) == cudaSuccess && b > 0 ? b : 1;
+    };
+    static const int per_sm16 = resident(sweep_kernel<OP, 16>), per_sm0 = resident(sweep_kernel<OP, 0>);
+    const int per_sm = bits == 16 ? per_sm16 : per_sm0;
+    // j spans: enough CTAs for four waves, each span at least 8 strides of the block
+    const int want = 4 * sm_count() * per_sm;
+    const int most = std::max(1, n / (8 * SW_THREADS));
+    const int spans = std::min(most, std::max(1, (want + rows - 1) / rows));
+    const int jspan = (n + spans - 1) / spans;
+    kern<<<dim3((unsigned)rows, (unsigned)spans), SW_THREADS, 0, st>>>(w, a_lo, a_hi, jspan, rd, counts);
 }
 
 }  // namespace
