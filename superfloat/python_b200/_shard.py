@@ -48,7 +48,16 @@ def gather_rows(local, cuts, dist=None, world: int = 1):
     import torch
     if dist is None or world == 1:
         return local
-    rows_max = max(cuts[r + 1] - cuts[r] for r in range(world))
+    sizes = [cuts[r + 1] - cuts[r] for r in range(world)]
+    if len(set(sizes)) == 1 and local.is_cuda and dist.get_backend() == "nccl":
+        # equal blocks: NCCL writes every rank's block straight into place
+        full = torch.empty((sizes[0] * world,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        src, dst = local.contiguous().reshape(-1), full.reshape(-1)
+        if not _nccl_type(local.dtype):              # NCCL has no int16: send the bytes
+            src, dst = src.view(torch.uint8), dst.view(torch.uint8)
+        dist.all_gather_into_tensor(dst, src)
+        return full
+    rows_max = max(sizes)
     pad = torch.zeros((rows_max,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
     pad[:local.shape[0]] = local
     wire = pad
