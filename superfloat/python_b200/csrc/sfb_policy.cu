@@ -53,9 +53,14 @@ __device__ void scan_pass(const T *__restrict__ x, int64_t R, int64_t K, int64_t
     unsigned long long nn = 0, ni = 0;
     double mx = 0.0;
     const int64_t total = R * K;
+    const bool dense = ld == K;              // rows back to back: no index split per element
     for (int64_t i = (int64_t)blockIdx.x * PT + threadIdx.x; i < total; i += (int64_t)gridDim.x * PT) {
-        const int64_t r = i / K, c = i - r * K;
-        const double v = (double)x[r * ld + c];
+        int64_t at = i;
+        if (!dense) {
+            const int64_t r = i / K;
+            at = r * ld + (i - r * K);
+        }
+        const double v = (double)x[at];
         if (isnan(v)) nn++;
         else if (isinf(v)) ni++;
         else mx = fmax(mx, fabs(v));
